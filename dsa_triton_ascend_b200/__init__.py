@@ -1,0 +1,17 @@
+"""B200 (sm_100a) implementation of the DeepSeek Sparse Attention hot path.
+
+Drop-in for the operators of 18851871668/dsa_triton_ascend, on CUDA torch tensors:
+
+* :func:`sparse_flash_attention_triton` / :class:`SparseFlashAttentionTriton`
+"""
+from ._lib import check_device_errors, lib as _load_library  # noqa: F401
+from .sparse_flash_attention import (  # noqa: F401
+    SparseFlashAttentionTriton,
+    sparse_flash_attention_triton,
+)
+
+__all__ = [
+    "sparse_flash_attention_triton",
+    "SparseFlashAttentionTriton",
+    "check_device_errors",
+]

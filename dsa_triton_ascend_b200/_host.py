@@ -1,0 +1,68 @@
+"""Host-side argument handling shared by the operators (no GPU compute here).
+
+Mirrors the reference helpers ``_default_actual_seq_lens`` / ``_tnd_cumsum_to_per_batch``
+(sparse_flash_attention_triton.py:338-347) but keeps everything on the device: TND
+inputs are addressed through per-batch row offsets instead of being copied into a
+padded BSND buffer.
+"""
+from __future__ import annotations
+
+import torch
+
+INT64_MAX = 9223372036854775807
+
+
+def lens_tensor(lens, batch: int, default: int, device) -> torch.Tensor:
+    """None -> [default]*batch; list/tuple/int -> int32 tensor; tensor -> int32 on device."""
+    if lens is None:
+        return torch.full((batch,), int(default), dtype=torch.int32, device=device)
+    if isinstance(lens, int):
+        return torch.full((batch,), lens, dtype=torch.int32, device=device)
+    if isinstance(lens, (list, tuple)):
+        if len(lens) != batch:
+            raise ValueError(f"expected {batch} sequence lengths, got {len(lens)}")
+        return torch.tensor([int(x) for x in lens], dtype=torch.int32, device=device)
+    t = torch.as_tensor(lens)
+    if t.numel() != batch:
+        raise ValueError(f"expected {batch} sequence lengths, got {t.numel()}")
+    return t.reshape(batch).to(device=device, dtype=torch.int32)
+
+
+def cumulative(lens, device) -> torch.Tensor:
+    """TND cumulative lengths (list/tuple/tensor) -> int32 tensor on device."""
+    if lens is None:
+        raise ValueError("TND layout requires cumulative actual sequence lengths")
+    if isinstance(lens, (list, tuple)):
+        return torch.tensor([int(x) for x in lens], dtype=torch.int32, device=device)
+    return torch.as_tensor(lens).reshape(-1).to(device=device, dtype=torch.int32)
+
+
+def tnd_offsets(cum: torch.Tensor):
+    """cumulative ends [B] -> (row_base [B], lens [B]); ``_tnd_cumsum_to_per_batch``."""
+    base = torch.zeros_like(cum)
+    if cum.numel() > 1:
+        base[1:] = cum[:-1]
+    return base, cum - base
+
+
+def row_bases(batch: int, stride: int, device) -> torch.Tensor:
+    return torch.arange(batch, dtype=torch.int32, device=device) * int(stride)
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    from ._lib import DSA_DTYPE_BF16, DSA_DTYPE_FP16
+    if t.dtype == torch.bfloat16:
+        return DSA_DTYPE_BF16
+    if t.dtype == torch.float16:
+        return DSA_DTYPE_FP16
+    raise ValueError(f"unsupported dtype {t.dtype}: expected bfloat16 or float16")
+
+
+def require_cuda(*ts) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("all tensors must be CUDA tensors (no CPU fallback)")
+
+
+def is_pow2_block(bs: int) -> bool:
+    return 1 <= bs <= 128 and (bs & (bs - 1)) == 0

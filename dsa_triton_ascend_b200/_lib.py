@@ -1,0 +1,102 @@
+"""ctypes binding of libdsa_b200.so (the sm_100a kernels).
+
+The library is loaded from this package directory.  There is no fallback: if the
+library is missing or cannot be loaded, every operator raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libdsa_b200.so")
+
+DSA_OK = 0
+DSA_ERR_INVALID_ARG = 1
+DSA_ERR_CUDA = 2
+DSA_ERR_TMA_DESCRIPTOR = 3
+DSA_DTYPE_BF16 = 0
+DSA_DTYPE_FP16 = 1
+
+_ERR_TEXT = {
+    DSA_ERR_INVALID_ARG: "invalid argument",
+    DSA_ERR_CUDA: "CUDA launch error",
+    DSA_ERR_TMA_DESCRIPTOR: "TMA descriptor rejected (misaligned or oversized tensor)",
+}
+
+_p = ctypes.c_void_p
+_i64 = ctypes.c_int64
+
+
+class SfaFwdParams(ctypes.Structure):
+    _fields_ = [
+        ("q", _p), ("q_rope", _p), ("key", _p), ("key_rope", _p),
+        ("sparse_indices", _p), ("act_q", _p), ("act_k", _p), ("q_row_base", _p),
+        ("k_row_base", _p), ("block_table", _p), ("out", _p), ("softmax_max", _p),
+        ("softmax_sum", _p), ("error_flag", _p),
+        ("num_rows", _i64), ("batch", _i64), ("n1", _i64), ("d", _i64), ("topk", _i64),
+        ("sparse_block_size", _i64), ("kv_rows", _i64), ("page_size", _i64),
+        ("max_blocks", _i64), ("s2_cap", _i64),
+        ("scale", ctypes.c_float), ("sparse_mode", ctypes.c_int32), ("dtype", ctypes.c_int32),
+    ]
+
+
+_lock = threading.Lock()
+_lib = None
+_err_bufs: dict = {}
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) and return the CUDA library; raises if it is missing."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise RuntimeError(
+                        f"{LIB_PATH} is missing: build it with `python -m dsa_triton_ascend_b200.build`"
+                        " (there is no CPU fallback)")
+                l = ctypes.CDLL(LIB_PATH)
+                l.dsa_version.restype = ctypes.c_int
+                l.dsa_sfa_fwd.argtypes = [ctypes.POINTER(SfaFwdParams), _p]
+                l.dsa_sfa_fwd.restype = ctypes.c_int
+                _lib = l
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != DSA_OK:
+        raise RuntimeError(f"{what}: {_ERR_TEXT.get(rc, 'error')} (code {rc})")
+
+
+def error_flag(device: torch.device) -> torch.Tensor:
+    """Per-device int32 the kernels OR their error bits into."""
+    key = torch.device(device).index
+    buf = _err_bufs.get(key)
+    if buf is None:
+        buf = torch.zeros(1, dtype=torch.int32, device=device)
+        _err_bufs[key] = buf
+    return buf
+
+
+def check_device_errors(device=None) -> None:
+    """Synchronise and raise if any kernel reported a device-side error."""
+    dev = torch.device("cuda" if device is None else device)
+    buf = error_flag(dev)
+    torch.cuda.synchronize(dev)
+    v = int(buf.item())
+    if v:
+        buf.zero_()
+        raise RuntimeError(f"dsa kernel reported device error bits 0x{v:x} "
+                           "(bit1: bounded wait timed out, bit3: misaligned shared memory)")
+
+
+def ptr(t) -> int:
+    return 0 if t is None else t.data_ptr()
+
+
+def stream_ptr(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream

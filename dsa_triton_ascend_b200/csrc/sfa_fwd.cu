@@ -1,0 +1,557 @@
+// Sparse flash attention forward for sm_100a (tcgen05 + TMA gather4, CTA pairs).
+//
+// Replaces the reference launch core `_sfa_core` / `_sfa_kernel`
+// (sparse_flash_attention_triton.py:189-332, :445-477).
+//
+// Work decomposition: one CTA pair (cluster of 2) per query token.  The 2-SM UMMA
+// with M=128 gives each CTA 64 of the 128 query heads (rows) while both CTAs feed
+// half of the B operand:
+//   * QK^T : B = gathered keys, split by token (CTA r owns tokens [32r, 32r+32) of
+//            each 64-token tile, all 576 latent+rope dims)      -> "X" ring
+//   * P V  : B = V (= key[:, :D]) split by head dim (CTA r provides D/2 dims for
+//            all 64 tokens of the tile)                          -> "H" ring
+// S (64 heads x 64 tokens) and O (64 heads x D) live in TMEM in the 2x2 layout of
+// the M=128 pair MMA: lanes 0-63 hold the first half of the columns, lanes 64-127
+// the second half.  Valid indices are compacted on the fly, so causal rows with
+// fewer than topK visible keys only pay for their valid keys.
+//
+// Warp roles (192 threads): warp 0 gathers (TMA gather4), warp 1 issues UMMA
+// (pair leader only) and owns TMEM, warps 2-5 run the online softmax, the lazy
+// O rescale and the epilogue.
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "dsa_b200.h"
+#include "sm100.cuh"
+#include "tma_host.h"
+
+namespace dsa {
+namespace sfa_fwd {
+
+constexpr int kTile = 64;          // keys per pair tile
+constexpr int kOwn = 32;           // keys per CTA in the QK B operand
+constexpr int kHeads = 64;         // heads per CTA
+constexpr int kChunkBytesX = kOwn * 128;     // one 64-dim chunk of 32 own keys
+constexpr int kChunkBytesH = kOwn * 128;     // one 64-dim chunk of 32 keys (a token half)
+constexpr int kThreads = 192;
+constexpr float kRescaleLog2 = 8.0f;         // lazy rescale threshold (log2 units)
+
+template <int D>
+struct Cfg {
+  static constexpr int kNopeChunks = D / 64;
+  static constexpr int kChunks = kNopeChunks + 1;          // + rope
+  static constexpr int kNPV = D < 256 ? D : 256;           // N of one PV MMA (both CTAs)
+  static constexpr int kNumPV = D / kNPV;                  // PV MMAs per k-step
+  static constexpr int kCpj = kNPV / 128;                  // chunks per CTA per PV MMA
+  static constexpr int kSlots = kNopeChunks / 2;           // V chunks per CTA
+  static constexpr int kQBytes = kChunks * kHeads * 128;
+  static constexpr int kXBytes = kChunks * kChunkBytesX;
+  static constexpr int kHHalf = kSlots * kChunkBytesH;
+  static constexpr int kHBytes = 2 * kHHalf;
+  static constexpr int kPBytes = kHeads * 128;
+  // smem carve-up (from a 1 KiB aligned base)
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffX = kOffQ + kQBytes;
+  static constexpr int kOffH = kOffX + 2 * kXBytes;
+  static constexpr int kOffP = kOffH + 2 * kHBytes;
+  static constexpr int kOffBars = kOffP + 2 * kPBytes;
+  // the Bars struct follows at kOffBars; total = kOffBars + sizeof(Bars)
+  static constexpr int kTmemO = 256;                        // O columns start
+  static constexpr int kTmemCols = 512;
+};
+
+struct __align__(64) Maps {
+  CUtensorMap q;    // [rows*N1, D], box 64 x 64
+  CUtensorMap qr;   // [rows*N1, 64], box 64 x 64
+  CUtensorMap k;    // [kv_rows, D], box 64 x 1 (gather4)
+  CUtensorMap kr;   // [kv_rows, 64], box 64 x 1
+};
+
+struct Args {
+  const int32_t* idx;
+  const int32_t* act_q;
+  const int32_t* act_k;
+  const int32_t* q_row_base;
+  const int32_t* k_row_base;
+  const int32_t* block_table;
+  void* out;
+  float* smax;
+  float* ssum;
+  int* err;
+  int num_rows, B, N1, topk, block, kv_rows, page, max_blocks, s2_cap, sparse_mode;
+  float scale;
+};
+
+struct __align__(16) Bars {
+  uint64_t q_full;
+  uint64_t x_full[2], x_empty[2];
+  uint64_t h_full[2], h_empty[2];
+  uint64_t s_full[2], p_full[2], pv_done[2];
+  uint32_t tmem_slot;
+  int tok[2][kTile];            // compacted key ids of the tiles being loaded
+  int rows_own[32];             // key-matrix rows of this CTA's 32 keys
+  int rows_all[64];             // key-matrix rows of all 64 keys of the tile
+  float red_max[2][4][32];
+  float red_sum[4][32];
+};
+
+// Query row -> (batch, position) and the row's visible window.
+struct RowInfo {
+  int b, s1, aq, ak, threshold;
+  bool active;
+};
+
+__device__ __forceinline__ RowInfo row_info(const Args& a, int row) {
+  RowInfo ri;
+  int lo = 0, hi = a.B - 1;
+  while (lo < hi) {  // last batch whose first row <= row
+    int mid = (lo + hi + 1) >> 1;
+    if (__ldg(a.q_row_base + mid) <= row) lo = mid; else hi = mid - 1;
+  }
+  ri.b = lo;
+  ri.s1 = row - __ldg(a.q_row_base + lo);
+  ri.aq = __ldg(a.act_q + lo);
+  ri.ak = __ldg(a.act_k + lo);
+  ri.threshold = a.sparse_mode == 0 ? ri.ak : ri.ak - ri.aq + ri.s1 + 1;
+  ri.active = ri.s1 < ri.aq && ri.threshold > 0;
+  return ri;
+}
+
+// Entry j of the (block-expanded) index row -> key position, or -1 if masked.
+// Mask rule: sparse_flash_attention_triton.py:264-266.
+__device__ __forceinline__ int key_at(const Args& a, const RowInfo& ri, const int32_t* row_idx,
+                                      int j) {
+  int blk = __ldg(row_idx + j / a.block);
+  if (blk < 0) return -1;
+  int t = blk * a.block + (j % a.block);
+  if (t >= ri.threshold || t >= ri.ak || t >= a.s2_cap) return -1;
+  if (a.block_table) {  // keys in unmapped pages are dropped (see key_row)
+    int pb = __ldg(a.block_table + (size_t)ri.b * a.max_blocks + t / a.page);
+    if (pb < 0 || (long long)pb * a.page >= a.kv_rows) return -1;
+  }
+  return t;
+}
+
+// Key position -> row of the key/key_rope matrices.
+__device__ __forceinline__ int key_row(const Args& a, int b, int t) {
+  if (a.block_table) {
+    int blk = __ldg(a.block_table + (size_t)b * a.max_blocks + t / a.page);
+    return blk * a.page + t % a.page;
+  }
+  return __ldg(a.k_row_base + b) + t;
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+template <int D, typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    sfa_fwd_kernel(const __grid_constant__ Maps maps, const Args a) {
+  using C = Cfg<D>;
+  // All shared state is dynamic (no static smem), so the window starts 1 KiB aligned
+  // as the 128-byte swizzle atoms require; checked below.
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  Bars& bars = *reinterpret_cast<Bars*>(smem_raw + C::kOffBars);
+  const uint32_t sbase = smem_u32(smem_raw);
+  const uint32_t sQ = sbase + C::kOffQ, sX = sbase + C::kOffX, sH = sbase + C::kOffH,
+                 sP = sbase + C::kOffP;
+  uint8_t* gP = smem_raw + C::kOffP;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (sbase & 1023u) {  // identical in both CTAs of the pair, so both leave together
+    if (threadIdx.x == 0) report_error(a.err, kErrMisaligned);
+    return;
+  }
+  const uint32_t cta = cluster_ctarank();
+  const int row = blockIdx.x >> 1;
+  const RowInfo ri = row_info(a, row);
+  const int32_t* row_idx = a.idx + (size_t)row * a.topk;
+  const int nent = a.topk * a.block;   // entries of the expanded index row
+
+  // ---- count the valid keys of this row (identical in both CTAs) ----
+  // A CTA that finds an earlier error recorded skips its row, so one protocol failure
+  // does not turn into a slow cascade of timeouts over the whole grid.
+  const bool abort = a.err != nullptr && *reinterpret_cast<volatile int*>(a.err) != 0;
+  int nvalid = 0;
+  if (ri.active && !abort) {
+    for (int base = 0; base < nent; base += kThreads) {
+      int j = base + threadIdx.x;
+      bool v = j < nent && key_at(a, ri, row_idx, j) >= 0;
+      nvalid += __syncthreads_count(v);
+    }
+  }
+  const int ntiles = (nvalid + kTile - 1) / kTile;
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bars.q_full), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&bars.x_full[s]), 1);
+      mbar_init(smem_u32(&bars.x_empty[s]), 1);
+      mbar_init(smem_u32(&bars.h_full[s]), 1);
+      mbar_init(smem_u32(&bars.h_empty[s]), 1);
+      mbar_init(smem_u32(&bars.s_full[s]), 1);
+      mbar_init(smem_u32(&bars.p_full[s]), 2);
+      mbar_init(smem_u32(&bars.pv_done[s]), 1);
+    }
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc<2>(smem_u32(&bars.tmem_slot), C::kTmemCols);
+    tmem_relinquish<2>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = bars.tmem_slot;
+  bool failed = false;
+
+  if (warp == 0) {
+    // ======================= loader (both CTAs) =======================
+    const uint32_t lead_q = mapa_shared(smem_u32(&bars.q_full), 0);
+    if (ntiles > 0) {
+      if (cta == 0 && lane == 0) mbar_arrive_expect_tx(smem_u32(&bars.q_full), 2 * C::kQBytes);
+      __syncwarp();
+      const int qrow0 = row * a.N1 + kHeads * (int)cta;
+      if (lane < C::kChunks) {
+        const CUtensorMap* m = lane < C::kNopeChunks ? &maps.q : &maps.qr;
+        int x = lane < C::kNopeChunks ? 64 * lane : 0;
+        tma_load_2d_pair(sQ + lane * kHeads * 128, m, lead_q, x, qrow0);
+      }
+    }
+    int cursor = 0;
+    for (int t = 0; t < ntiles && !failed; ++t) {
+      const int s = t & 1;
+      const uint32_t par = (t >> 1) & 1;
+      // -- stream-compact the next kTile valid keys of the row --
+      int have = 0;
+      while (have < kTile && cursor < nent) {
+        int j = cursor + lane;
+        int kp = j < nent ? key_at(a, ri, row_idx, j) : -1;
+        unsigned m = __ballot_sync(0xffffffffu, kp >= 0);
+        int pos = have + __popc(m & ((1u << lane) - 1u));
+        if (kp >= 0 && pos < kTile) bars.tok[s][pos] = kp;
+        int cnt = __popc(m);
+        if (have + cnt > kTile) {
+          // keep the first (kTile - have) valid lanes; resume after the last one taken
+          int need = kTile - have, last = 0;
+          unsigned mm = m;
+          for (int i = 0; i < need; ++i) { last = __ffs(mm) - 1; mm &= mm - 1; }
+          cursor += last + 1;
+          have = kTile;
+        } else {
+          have += cnt;
+          cursor += 32;
+        }
+      }
+      __syncwarp();
+      // rows of the 64 keys (invalid tail -> first key row of the batch; P is 0 there)
+      int k0 = lane < have ? bars.tok[s][lane] : 0;
+      int k1 = lane + 32 < have ? bars.tok[s][lane + 32] : 0;
+      int r0 = key_row(a, ri.b, k0), r1 = key_row(a, ri.b, k1);
+      __syncwarp();
+
+      // -- X: own 32 keys, all chunks (QK B operand) --
+      mbar_wait(smem_u32(&bars.x_empty[s]), par ^ 1, a.err, &failed);
+      failed = __any_sync(0xffffffffu, failed);
+      if (!failed) {
+        const uint32_t lead = mapa_shared(smem_u32(&bars.x_full[s]), 0);
+        if (cta == 0 && lane == 0) mbar_arrive_expect_tx(smem_u32(&bars.x_full[s]), 2 * C::kXBytes);
+        __syncwarp();
+        // own keys are tile keys [32*cta, 32*cta+32): held by r0 (cta 0) or r1 (cta 1)
+        bars.rows_own[lane] = cta == 0 ? r0 : r1;
+        __syncwarp();
+        for (int item = lane; item < 8 * C::kChunks; item += 32) {
+          int g = item & 7, c = item >> 3;
+          const CUtensorMap* m = c < C::kNopeChunks ? &maps.k : &maps.kr;
+          int x = c < C::kNopeChunks ? 64 * c : 0;
+          tma_gather4_pair(sX + s * C::kXBytes + c * kChunkBytesX + g * 512, m, lead, x,
+                           bars.rows_own[4 * g], bars.rows_own[4 * g + 1],
+                           bars.rows_own[4 * g + 2], bars.rows_own[4 * g + 3]);
+        }
+        __syncwarp();
+      }
+      // -- H: V slots of this CTA for all 64 keys (PV B operand) --
+      mbar_wait(smem_u32(&bars.h_empty[s]), par ^ 1, a.err, &failed);
+      failed = __any_sync(0xffffffffu, failed);
+      if (!failed) {
+        const uint32_t lead = mapa_shared(smem_u32(&bars.h_full[s]), 0);
+        if (cta == 0 && lane == 0) mbar_arrive_expect_tx(smem_u32(&bars.h_full[s]), 2 * C::kHBytes);
+        bars.rows_all[lane] = r0;
+        bars.rows_all[lane + 32] = r1;
+        __syncwarp();
+        for (int item = lane; item < 16 * C::kSlots; item += 32) {
+          int g = item & 15, sl = item >> 4;
+          int j = sl / C::kCpj;
+          int chunk = j * 2 * C::kCpj + (int)cta * C::kCpj + sl % C::kCpj;
+          uint32_t dst = sH + s * C::kHBytes + (g >> 3) * C::kHHalf + sl * kChunkBytesH +
+                         (g & 7) * 512;
+          tma_gather4_pair(dst, &maps.k, lead, 64 * chunk, bars.rows_all[4 * g],
+                           bars.rows_all[4 * g + 1], bars.rows_all[4 * g + 2],
+                           bars.rows_all[4 * g + 3]);
+        }
+        __syncwarp();
+      }
+    }
+  } else if (warp == 1) {
+    // ======================= MMA issuer (pair leader) =======================
+    if (cta == 0 && ntiles > 0 && lane == 0) {
+      const bool bf16 = ElemTraits<T>::kIsBf16;
+      const uint32_t id_qk = idesc_f16(128, kTile, bf16, false, false);
+      const uint32_t id_pv = idesc_f16(128, C::kNPV, bf16, false, true);
+      mbar_wait(smem_u32(&bars.q_full), 0, a.err, &failed);
+      auto issue_qk = [&](int t) {
+        const int s = t & 1;
+        if (!mbar_wait(smem_u32(&bars.x_full[s]), (t >> 1) & 1, a.err, &failed)) return;
+        tc_fence_after();
+        const uint32_t d = tmem + 32 * s;
+        for (int c = 0; c < C::kChunks; ++c)
+          for (int u = 0; u < 4; ++u) {
+            uint64_t da = smem_desc_sw128(sQ + c * kHeads * 128 + u * 32, 16, 1024);
+            uint64_t db = smem_desc_sw128(sX + s * C::kXBytes + c * kChunkBytesX + u * 32, 16, 1024);
+            umma_f16<2>(d, da, db, id_qk, (c | u) != 0);
+          }
+        umma_commit_pair(smem_u32(&bars.x_empty[s]), 3);
+        umma_commit_pair(smem_u32(&bars.s_full[s]), 3);
+      };
+      if (!failed) issue_qk(0);
+      for (int t = 0; t < ntiles && !failed; ++t) {
+        if (t + 1 < ntiles) issue_qk(t + 1);
+        const int s = t & 1;
+        const uint32_t par = (t >> 1) & 1;
+        mbar_wait(smem_u32(&bars.p_full[s]), par, a.err, &failed, true);
+        mbar_wait(smem_u32(&bars.h_full[s]), par, a.err, &failed);
+        if (failed) break;
+        tc_fence_after();
+        for (int j = 0; j < C::kNumPV; ++j)
+          for (int k = 0; k < kTile / 16; ++k) {
+            uint64_t da = smem_desc_sw128(sP + s * C::kPBytes + k * 32, 16, 1024);
+            uint64_t db = smem_desc_sw128(
+                sH + s * C::kHBytes + (k >> 1) * C::kHHalf + j * C::kCpj * kChunkBytesH +
+                    (k & 1) * 2048,
+                kChunkBytesH, 1024);
+            umma_f16<2>(tmem + C::kTmemO + j * (C::kNPV / 2), da, db, id_pv, (t | k) != 0);
+          }
+        umma_commit_pair(smem_u32(&bars.h_empty[s]), 3);
+        umma_commit_pair(smem_u32(&bars.pv_done[s]), 3);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ================= softmax / correction / epilogue (both CTAs) =================
+    const int q = warp & 3;                  // TMEM lane quadrant of this warp
+    const int hrow = 32 * (q & 1) + lane;    // head within the CTA (P row)
+    const int half = q >> 1;                 // key half of the tile / O column half
+    const uint32_t lane_addr = (uint32_t)(32 * q) << 16;
+    const float c2 = a.scale * 1.4426950408889634f;
+    const uint32_t lead_p0 = mapa_shared(smem_u32(&bars.p_full[0]), 0);
+    const uint32_t lead_p1 = mapa_shared(smem_u32(&bars.p_full[1]), 0);
+    float m_run = -INFINITY, m_ref = -INFINITY, l_part = 0.f;
+
+    for (int t = 0; t < ntiles; ++t) {
+      const int s = t & 1;
+      const uint32_t par = (t >> 1) & 1;
+      const int nv = min(kTile, nvalid - kTile * t) - kOwn * half;   // valid keys in my half
+      mbar_wait(smem_u32(&bars.s_full[s]), par, a.err, &failed);
+      bool wfail = __any_sync(0xffffffffu, failed);                  // warp-uniform
+      tc_fence_after();
+      uint32_t r[32];
+      float mloc = -INFINITY;
+      if (!wfail) {
+        tmem_ld32(tmem + lane_addr + 32 * s, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (i < nv) mloc = fmaxf(mloc, __uint_as_float(r[i]));
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = 0u;
+      }
+      bars.red_max[s][q][lane] = mloc;
+      named_bar_sync(1, 128);
+      const float mpart = bars.red_max[s][q ^ 2][lane];
+      const float mnew = fmaxf(m_run, fmaxf(mloc, mpart));
+      m_run = mnew;
+      // Lazy rescale: the exponent reference m_ref only moves when the running max
+      // exceeds it by more than 2^8; partner threads (same head) decide identically.
+      bool rescale = false;
+      float factor = 1.f;
+      if (t == 0) {
+        m_ref = mnew;
+      } else if ((mnew - m_ref) * c2 > kRescaleLog2) {
+        rescale = true;
+        factor = ex2((m_ref - mnew) * c2);
+        m_ref = mnew;
+      }
+      const float off = m_ref * c2;
+      uint32_t pk[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float p0 = (2 * i < nv) ? ex2(fmaf(__uint_as_float(r[2 * i]), c2, -off)) : 0.f;
+        float p1 = (2 * i + 1 < nv) ? ex2(fmaf(__uint_as_float(r[2 * i + 1]), c2, -off)) : 0.f;
+        l_part += p0 + p1;
+        pk[i] = ElemTraits<T>::pack2(p0, p1);
+      }
+      // P buffer s was last read by PV(t-2); O may be touched only once PV(t-1) is done.
+      if (t >= 2) mbar_wait(smem_u32(&bars.pv_done[s]), ((t >> 1) - 1) & 1, a.err, &failed);
+      if (__any_sync(0xffffffffu, rescale)) {
+        mbar_wait(smem_u32(&bars.pv_done[s ^ 1]), ((t - 1) >> 1) & 1, a.err, &failed);
+        l_part *= factor;
+        if (!__any_sync(0xffffffffu, failed)) {
+          tc_fence_after();
+          for (int cc = 0; cc < D / 2; cc += 16) {
+            uint32_t o[16];
+            tmem_ld16(tmem + lane_addr + C::kTmemO + cc, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+            tmem_st16(tmem + lane_addr + C::kTmemO + cc, o);
+          }
+          tmem_st_wait();
+        }
+      }
+      uint8_t* prow = gP + s * C::kPBytes + hrow * 128;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        int chunk = 4 * half + i;
+        uint4 v = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        *reinterpret_cast<uint4*>(prow + ((chunk ^ (hrow & 7)) << 4)) = v;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      named_bar_sync(1, 128);
+      if (warp == 2 && lane == 0) mbar_arrive_cluster(s ? lead_p1 : lead_p0);
+    }
+
+    // ------------------------------ epilogue ------------------------------
+    bars.red_sum[q][lane] = l_part;
+    if (ntiles > 0) {
+      const int tl = ntiles - 1;
+      mbar_wait(smem_u32(&bars.pv_done[tl & 1]), (tl >> 1) & 1, a.err, &failed);
+    }
+    const bool read_o = ntiles > 0 && !__any_sync(0xffffffffu, failed);
+    named_bar_sync(1, 128);
+    const float l_tot = l_part + bars.red_sum[q ^ 2][lane];
+    const int head = kHeads * (int)cta + hrow;
+    const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+    tc_fence_after();
+    T* orow = reinterpret_cast<T*>(a.out) + ((size_t)row * a.N1 + min(head, a.N1 - 1)) * D;
+    for (int j = 0; j < C::kNumPV; ++j) {
+      const int dbase = j * C::kNPV + half * (C::kNPV / 2);
+      for (int cc = 0; cc < C::kNPV / 2; cc += 32) {
+        uint32_t o[32];
+        if (read_o) {
+          tmem_ld32(tmem + lane_addr + C::kTmemO + j * (C::kNPV / 2) + cc, o);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0u;
+        }
+        if (head < a.N1) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + dbase + cc);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = ElemTraits<T>::pack2(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
+            w.y = ElemTraits<T>::pack2(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
+            w.z = ElemTraits<T>::pack2(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
+            w.w = ElemTraits<T>::pack2(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
+            dst[v] = w;
+          }
+        }
+      }
+    }
+    if (head < a.N1 && half == 0 && a.smax != nullptr) {
+      const bool any = ntiles > 0;
+      a.smax[(size_t)row * a.N1 + head] = any ? m_run * a.scale : 0.f;
+      a.ssum[(size_t)row * a.N1 + head] = any ? l_tot * ex2((m_ref - m_run) * c2) : 0.f;
+    }
+  }
+
+  // ------------------------------ teardown ------------------------------
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) tmem_dealloc<2>(tmem, C::kTmemCols);
+}
+
+template <int D>
+constexpr int smem_bytes() { return Cfg<D>::kOffBars + (int)sizeof(Bars); }
+static_assert(smem_bytes<512>() <= 232448, "D=512 smem budget (227 KiB per block)");
+
+template <int D, typename T>
+int launch(const DsaSfaFwdParams* p, cudaStream_t stream) {
+  using C = Cfg<D>;
+  const bool bf16 = ElemTraits<T>::kIsBf16;
+  Maps maps;
+  const uint64_t qrows = (uint64_t)p->num_rows * p->n1;
+  if (!make_tmap_2d_16b(&maps.q, p->q, bf16, qrows, D, (uint64_t)D * 2, 64, 64) ||
+      !make_tmap_2d_16b(&maps.qr, p->q_rope, bf16, qrows, 64, 128, 64, 64) ||
+      !make_tmap_2d_16b(&maps.k, p->key, bf16, p->kv_rows, D, (uint64_t)D * 2, 64, 1) ||
+      !make_tmap_2d_16b(&maps.kr, p->key_rope, bf16, p->kv_rows, 64, 128, 64, 1))
+    return DSA_ERR_TMA_DESCRIPTOR;
+  Args a;
+  a.idx = p->sparse_indices;
+  a.act_q = p->act_q;
+  a.act_k = p->act_k;
+  a.q_row_base = p->q_row_base;
+  a.k_row_base = p->k_row_base;
+  a.block_table = p->block_table;
+  a.out = p->out;
+  a.smax = p->softmax_max;
+  a.ssum = p->softmax_sum;
+  a.err = p->error_flag;
+  a.num_rows = (int)p->num_rows;
+  a.B = (int)p->batch;
+  a.N1 = (int)p->n1;
+  a.topk = (int)p->topk;
+  a.block = (int)p->sparse_block_size;
+  a.kv_rows = (int)p->kv_rows;
+  a.page = (int)p->page_size;
+  a.max_blocks = (int)p->max_blocks;
+  a.s2_cap = (int)p->s2_cap;
+  a.sparse_mode = p->sparse_mode;
+  a.scale = p->scale;
+  auto kern = sfa_fwd_kernel<D, T>;
+  constexpr int kSmem = smem_bytes<D>();
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
+    return DSA_ERR_CUDA;
+  kern<<<dim3(2 * (unsigned)p->num_rows), dim3(kThreads), kSmem, stream>>>(maps, a);
+  return cudaGetLastError() == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
+}
+
+}  // namespace sfa_fwd
+}  // namespace dsa
+
+extern "C" int dsa_sfa_fwd(const DsaSfaFwdParams* p, void* stream_) {
+  using namespace dsa::sfa_fwd;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (!p) return DSA_ERR_INVALID_ARG;
+  if (p->num_rows <= 0) return DSA_OK;
+  if (p->n1 < 1 || p->n1 > 128 || p->batch < 1 || p->topk < 1 || p->sparse_block_size < 1 ||
+      p->kv_rows < 1 || !p->q || !p->q_rope || !p->key || !p->key_rope || !p->sparse_indices ||
+      !p->act_q || !p->act_k || !p->q_row_base || !p->out)
+    return DSA_ERR_INVALID_ARG;
+  if (!p->block_table && !p->k_row_base) return DSA_ERR_INVALID_ARG;
+  if (p->block_table && (p->page_size < 1 || p->max_blocks < 1)) return DSA_ERR_INVALID_ARG;
+  if ((p->softmax_max == nullptr) != (p->softmax_sum == nullptr)) return DSA_ERR_INVALID_ARG;
+  const int D = (int)p->d;
+  if (p->dtype == DSA_DTYPE_BF16) {
+    if (D == 512) return launch<512, __nv_bfloat16>(p, stream);
+    if (D == 256) return launch<256, __nv_bfloat16>(p, stream);
+    if (D == 128) return launch<128, __nv_bfloat16>(p, stream);
+  } else if (p->dtype == DSA_DTYPE_FP16) {
+    if (D == 512) return launch<512, __half>(p, stream);
+    if (D == 256) return launch<256, __half>(p, stream);
+    if (D == 128) return launch<128, __half>(p, stream);
+  }
+  return DSA_ERR_INVALID_ARG;
+}

@@ -1,0 +1,97 @@
+/*
+ * dsa_b200.h -- C ABI of libdsa_b200.so, the sm_100a kernels of the DeepSeek Sparse
+ * Attention hot path.
+ *
+ * Plain pointers and sizes only.  Every tensor argument is a device pointer to a
+ * contiguous buffer; every entry point is asynchronous on `stream` (a cudaStream_t
+ * passed as void*; NULL = legacy default stream) and returns DSA_OK or an error code
+ * without synchronising.  Kernels that detect a problem on the device (a bounded
+ * wait that gave up) set bits in `*error_flag` (may be NULL); callers read it after
+ * synchronising.
+ *
+ * Each entry point replaces the launch layer of one reference operator of
+ * 18851871668/dsa_triton_ascend (file:line of the reference project given below).
+ * Layout normalisation (BSND / TND / PA_BSND), argument guards and output allocation
+ * stay in the host wrapper (dsa_triton_ascend_b200/*.py), as in the reference.
+ */
+#ifndef DSA_B200_H_
+#define DSA_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DSA_OK 0
+#define DSA_ERR_INVALID_ARG 1     /* bad size / null pointer / unsupported config */
+#define DSA_ERR_CUDA 2            /* launch or attribute error from the CUDA runtime */
+#define DSA_ERR_TMA_DESCRIPTOR 3  /* driver rejected a TMA tensor map (alignment) */
+
+#define DSA_DTYPE_BF16 0
+#define DSA_DTYPE_FP16 1
+
+/* Library version, (major << 16) | minor. */
+int dsa_version(void);
+
+/*
+ * Sparse flash attention forward (MLA-absorb: value = key[..., :d]).
+ * Replaces `_sfa_core` / `_sfa_kernel` (sparse_flash_attention_triton.py:445-477, :189-332).
+ *
+ * Query side is addressed by "query rows" r in [0, num_rows): one query token each.
+ *   q           [num_rows][n1][d]      bf16/fp16, d in {128, 256, 512}
+ *   q_rope      [num_rows][n1][64]
+ *   sparse_indices [num_rows][topk]    int32 block ids (token ids when
+ *                                      sparse_block_size == 1), -1 = padding
+ *   q_row_base  [batch]                first query row of each batch (BSND: b*S1,
+ *                                      TND: cumulative offsets); row r belongs to the
+ *                                      last batch whose base <= r, position s1 = r - base
+ *   act_q, act_k [batch]               valid query / key lengths
+ * Key side: `kv_rows` rows of key [kv_rows][d] and key_rope [kv_rows][64].
+ *   Dense (block_table == NULL): key position t of batch b is row k_row_base[b] + t.
+ *   Paged (block_table != NULL, [batch][max_blocks]): row block_table[b][t / page_size]
+ *     * page_size + t % page_size; keys in pages whose id is < 0 are skipped.
+ * A key position t is attended iff t < threshold, t < act_k[b] and t < s2_cap, with
+ * threshold = act_k[b] (sparse_mode 0) or act_k[b] - act_q[b] + s1 + 1 (sparse_mode 3);
+ * rows with s1 >= act_q[b] or threshold <= 0 produce zeros.
+ * Outputs: out [num_rows][n1][d] (query dtype); softmax_max / softmax_sum
+ *   [num_rows][n1] fp32 (both NULL to skip): max of scaled scores and sum of
+ *   exp(score - max); rows without keys get 0.
+ */
+typedef struct DsaSfaFwdParams {
+  const void* q;
+  const void* q_rope;
+  const void* key;
+  const void* key_rope;
+  const int32_t* sparse_indices;
+  const int32_t* act_q;
+  const int32_t* act_k;
+  const int32_t* q_row_base;
+  const int32_t* k_row_base;     /* dense layout only */
+  const int32_t* block_table;    /* paged layout only, else NULL */
+  void* out;
+  float* softmax_max;
+  float* softmax_sum;
+  int* error_flag;
+  int64_t num_rows;
+  int64_t batch;
+  int64_t n1;
+  int64_t d;
+  int64_t topk;
+  int64_t sparse_block_size;
+  int64_t kv_rows;
+  int64_t page_size;
+  int64_t max_blocks;
+  int64_t s2_cap;                /* exclusive upper bound on key positions */
+  float scale;
+  int32_t sparse_mode;           /* 0 or 3 */
+  int32_t dtype;                 /* DSA_DTYPE_* of q/q_rope/key/key_rope/out */
+} DsaSfaFwdParams;
+
+int dsa_sfa_fwd(const DsaSfaFwdParams* params, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSA_B200_H_ */

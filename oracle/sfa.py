@@ -110,15 +110,18 @@ def valid_positions(tok_row: np.ndarray, s1: int, aq: int, ak: int, sparse_mode:
 
 
 def sfa_fwd(q, k, qr, kr, tok_idx, scale, act_q=None, act_k=None, sparse_mode=3,
-            dtype="bf16"):
+            dtype="bf16", rounding="golden"):
     """SFA forward on BSND numpy inputs (fp32 accumulate).
 
     q [B,S1,N1,D], k [B,S2,1,D] (value = k[..., :D]), qr [B,S1,N1,64], kr [B,S2,1,64],
     tok_idx [B,S1,1,K] token ids (block ids already expanded).  Returns
     (out [B,S1,N1,D] rounded to ``dtype``, softmax_max [B,1,S1,N1], softmax_sum
     [B,1,S1,N1]); inactive/empty rows stay zero (``sparse_flash_attention_triton.py:326-332``).
-    Probabilities are rounded to ``dtype`` before P@V as the golden does
-    (``sparse_flash_attention_numpy.py:108-114, 149``).
+    ``rounding`` picks where probabilities are rounded to ``dtype`` before P@V:
+    "golden" rounds the normalised probabilities (``sparse_flash_attention_numpy.py:108-114,
+    149``); "kernel" rounds the unnormalised exp(s - max) and divides the fp32 product by
+    the row sum afterwards, as the reference kernel does (``sparse_flash_attention_triton.py:
+    309-324``).  Both are within rounding noise of each other.
     """
     q = np.asarray(q, np.float32); k = np.asarray(k, np.float32)
     qr = np.asarray(qr, np.float32); kr = np.asarray(kr, np.float32)
@@ -141,8 +144,10 @@ def sfa_fwd(q, k, qr, kr, tok_idx, scale, act_q=None, act_k=None, sparse_mode=3,
             m = sc.max(axis=1)
             e = np.exp(sc - m[:, None])
             l = e.sum(axis=1)
-            p = round_to(e / l[:, None], dtype)
-            out[b, s1] = p @ kk[:, :D]
+            if rounding == "kernel":
+                out[b, s1] = (round_to(e, dtype) @ kk[:, :D]) / l[:, None]
+            else:
+                out[b, s1] = round_to(e / l[:, None], dtype) @ kk[:, :D]
             smax[b, 0, s1] = m
             ssum[b, 0, s1] = l
     return round_to(out, dtype), smax, ssum
