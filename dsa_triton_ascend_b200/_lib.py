@@ -36,7 +36,7 @@ class SfaFwdParams(ctypes.Structure):
         ("q", _p), ("q_rope", _p), ("key", _p), ("key_rope", _p),
         ("sparse_indices", _p), ("act_q", _p), ("act_k", _p), ("q_row_base", _p),
         ("k_row_base", _p), ("block_table", _p), ("out", _p), ("softmax_max", _p),
-        ("softmax_sum", _p), ("error_flag", _p),
+        ("softmax_sum", _p), ("error_flag", _p), ("workspace", _p), ("workspace_bytes", _i64),
         ("num_rows", _i64), ("batch", _i64), ("n1", _i64), ("d", _i64), ("topk", _i64),
         ("sparse_block_size", _i64), ("kv_rows", _i64), ("page_size", _i64),
         ("max_blocks", _i64), ("s2_cap", _i64),
@@ -63,6 +63,8 @@ def lib() -> ctypes.CDLL:
                 l.dsa_version.restype = ctypes.c_int
                 l.dsa_sfa_fwd.argtypes = [ctypes.POINTER(SfaFwdParams), _p]
                 l.dsa_sfa_fwd.restype = ctypes.c_int
+                l.dsa_sfa_fwd_workspace_size.argtypes = [_i64, _i64, _i64]
+                l.dsa_sfa_fwd_workspace_size.restype = _i64
                 _lib = l
     return _lib
 

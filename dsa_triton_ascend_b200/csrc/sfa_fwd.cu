@@ -15,9 +15,11 @@
 // the second half.  Valid indices are compacted on the fly, so causal rows with
 // fewer than topK visible keys only pay for their valid keys.
 //
-// Warp roles (192 threads): warp 0 gathers (TMA gather4), warp 1 issues UMMA
-// (pair leader only) and owns TMEM, warps 2-5 run the online softmax, the lazy
-// O rescale and the epilogue.
+// Warp roles (352 threads): warps 0 and 6 gather the V slices with TMA gather4,
+// warp 1 issues UMMA (pair leader only) and owns TMEM, warps 2-5 run the online
+// softmax, the lazy O rescale and the epilogue, warps 7-10 gather the QK^T keys with
+// cp.async.  Gathering on both the TMA and the load/store path doubles the rate at
+// which one CTA can pull scattered 128-byte rows out of L2.
 
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -34,7 +36,8 @@ constexpr int kOwn = 32;           // keys per CTA in the QK B operand
 constexpr int kHeads = 64;         // heads per CTA
 constexpr int kChunkBytesX = kOwn * 128;     // one 64-dim chunk of 32 own keys
 constexpr int kChunkBytesH = kOwn * 128;     // one 64-dim chunk of 32 keys (a token half)
-constexpr int kThreads = 192;
+constexpr int kThreads = 352;       // 11 warps, see the role map in the kernel
+constexpr int kXLoaders = 128;      // cp.async threads gathering the QK^T keys
 constexpr float kRescaleLog2 = 8.0f;         // lazy rescale threshold (log2 units)
 
 template <int D>
@@ -79,6 +82,10 @@ struct Args {
   float* smax;
   float* ssum;
   int* err;
+  const void* key;          // [kv_rows][D]
+  const void* key_rope;     // [kv_rows][64]
+  const int32_t* ws_rows;   // [num_rows][nent] compacted key-matrix rows (prep kernel)
+  const int32_t* ws_count;  // [num_rows] number of valid keys per query row
   int num_rows, B, N1, topk, block, kv_rows, page, max_blocks, s2_cap, sparse_mode;
   float scale;
 };
@@ -89,9 +96,7 @@ struct __align__(16) Bars {
   uint64_t h_full[2], h_empty[2];
   uint64_t s_full[2], p_full[2], pv_done[2];
   uint32_t tmem_slot;
-  int tok[2][kTile];            // compacted key ids of the tiles being loaded
-  int rows_own[32];             // key-matrix rows of this CTA's 32 keys
-  int rows_all[64];             // key-matrix rows of all 64 keys of the tile
+  int rows_h[2][64];            // key-matrix rows of the tile's 64 keys (per H loader)
   float red_max[2][4][32];
   float red_sum[4][32];
 };
@@ -152,6 +157,32 @@ __device__ __forceinline__ void named_bar_sync(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
+// One warp per query row: compact the row's valid key positions (block-expanded,
+// masked as in sparse_flash_attention_triton.py:264-266) into key-matrix rows, in
+// index order, plus their count.  The attention kernel then streams 64 rows per tile
+// with one coalesced load and no per-tile scanning.
+__global__ void __launch_bounds__(128) sfa_prep_kernel(const Args a, int32_t* ws_rows,
+                                                       int32_t* ws_count) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 4 + warp;
+  if (row >= a.num_rows) return;
+  const RowInfo ri = row_info(a, row);
+  const int nent = a.topk * a.block;
+  int have = 0;
+  if (ri.active) {
+    const int32_t* row_idx = a.idx + (size_t)row * a.topk;
+    int32_t* out = ws_rows + (size_t)row * nent;
+    for (int base = 0; base < nent; base += 32) {
+      const int j = base + lane;
+      const int kp = j < nent ? key_at(a, ri, row_idx, j) : -1;
+      const unsigned m = __ballot_sync(0xffffffffu, kp >= 0);
+      if (kp >= 0) out[have + __popc(m & ((1u << lane) - 1u))] = key_row(a, ri.b, kp);
+      have += __popc(m);
+    }
+  }
+  if (lane == 0) ws_count[row] = have;
+}
+
 template <int D, typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     sfa_fwd_kernel(const __grid_constant__ Maps maps, const Args a) {
@@ -173,27 +204,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t cta = cluster_ctarank();
   const int row = blockIdx.x >> 1;
   const RowInfo ri = row_info(a, row);
-  const int32_t* row_idx = a.idx + (size_t)row * a.topk;
-  const int nent = a.topk * a.block;   // entries of the expanded index row
-
-  // ---- count the valid keys of this row (identical in both CTAs) ----
+  // Valid keys of this row, compacted by sfa_prep_kernel (identical in both CTAs).
   // A CTA that finds an earlier error recorded skips its row, so one protocol failure
   // does not turn into a slow cascade of timeouts over the whole grid.
   const bool abort = a.err != nullptr && *reinterpret_cast<volatile int*>(a.err) != 0;
-  int nvalid = 0;
-  if (ri.active && !abort) {
-    for (int base = 0; base < nent; base += kThreads) {
-      int j = base + threadIdx.x;
-      bool v = j < nent && key_at(a, ri, row_idx, j) >= 0;
-      nvalid += __syncthreads_count(v);
-    }
-  }
+  const int nvalid = (ri.active && !abort) ? __ldg(a.ws_count + row) : 0;
   const int ntiles = (nvalid + kTile - 1) / kTile;
+  const int32_t* rows = a.ws_rows + (size_t)row * a.topk * a.block;
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(&bars.q_full), 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(smem_u32(&bars.x_full[s]), 1);
+      mbar_init(smem_u32(&bars.x_full[s]), 2 * kXLoaders);   // every X loader of both CTAs
       mbar_init(smem_u32(&bars.x_empty[s]), 1);
       mbar_init(smem_u32(&bars.h_full[s]), 1);
       mbar_init(smem_u32(&bars.h_empty[s]), 1);
@@ -214,10 +236,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t tmem = bars.tmem_slot;
   bool failed = false;
 
-  if (warp == 0) {
-    // ======================= loader (both CTAs) =======================
-    const uint32_t lead_q = mapa_shared(smem_u32(&bars.q_full), 0);
-    if (ntiles > 0) {
+  if (warp == 0 || warp == 6) {
+    // ====== H loaders: this CTA's V dims of all 64 keys, for P V (TMA gather4) ======
+    if (warp == 0 && ntiles > 0) {   // Q of this CTA's 64 heads, once
+      const uint32_t lead_q = mapa_shared(smem_u32(&bars.q_full), 0);
       if (cta == 0 && lane == 0) mbar_arrive_expect_tx(smem_u32(&bars.q_full), 2 * C::kQBytes);
       __syncwarp();
       const int qrow0 = row * a.N1 + kHeads * (int)cta;
@@ -227,80 +249,82 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tma_load_2d_pair(sQ + lane * kHeads * 128, m, lead_q, x, qrow0);
       }
     }
-    int cursor = 0;
+    const int part = warp == 0 ? 0 : 1;                 // which half of the items
+    const int nitems = 16 * C::kSlots;
+    int* rows_h = bars.rows_h[part];
+    const int filler = nvalid > 0 ? __ldg(rows) : 0;
+    auto fetch = [&](int j) { return j < nvalid ? __ldg(rows + j) : filler; };
+    int n0 = ntiles > 0 ? fetch(lane) : 0, n1 = ntiles > 0 ? fetch(32 + lane) : 0;
     for (int t = 0; t < ntiles && !failed; ++t) {
       const int s = t & 1;
-      const uint32_t par = (t >> 1) & 1;
-      // -- stream-compact the next kTile valid keys of the row --
-      int have = 0;
-      while (have < kTile && cursor < nent) {
-        int j = cursor + lane;
-        int kp = j < nent ? key_at(a, ri, row_idx, j) : -1;
-        unsigned m = __ballot_sync(0xffffffffu, kp >= 0);
-        int pos = have + __popc(m & ((1u << lane) - 1u));
-        if (kp >= 0 && pos < kTile) bars.tok[s][pos] = kp;
-        int cnt = __popc(m);
-        if (have + cnt > kTile) {
-          // keep the first (kTile - have) valid lanes; resume after the last one taken
-          int need = kTile - have, last = 0;
-          unsigned mm = m;
-          for (int i = 0; i < need; ++i) { last = __ffs(mm) - 1; mm &= mm - 1; }
-          cursor += last + 1;
-          have = kTile;
-        } else {
-          have += cnt;
-          cursor += 32;
-        }
+      const int c0 = n0, c1 = n1;
+      if (t + 1 < ntiles) {
+        n0 = fetch(kTile * (t + 1) + lane);
+        n1 = fetch(kTile * (t + 1) + 32 + lane);
+      }
+      mbar_wait(smem_u32(&bars.h_empty[s]), ((t >> 1) & 1) ^ 1, a.err, &failed);
+      failed = __any_sync(0xffffffffu, failed);
+      if (failed) break;
+      const uint32_t lead = mapa_shared(smem_u32(&bars.h_full[s]), 0);
+      if (part == 0 && cta == 0 && lane == 0)
+        mbar_arrive_expect_tx(smem_u32(&bars.h_full[s]), 2 * C::kHBytes);
+      rows_h[lane] = c0;
+      rows_h[lane + 32] = c1;
+      __syncwarp();
+      for (int item = part * (nitems / 2) + lane; item < (part + 1) * (nitems / 2); item += 32) {
+        int g = item & 15, sl = item >> 4;
+        int j = sl / C::kCpj;
+        int chunk = j * 2 * C::kCpj + (int)cta * C::kCpj + sl % C::kCpj;
+        uint32_t dst = sH + s * C::kHBytes + (g >> 3) * C::kHHalf + sl * kChunkBytesH +
+                       (g & 7) * 512;
+        tma_gather4_pair(dst, &maps.k, lead, 64 * chunk, rows_h[4 * g], rows_h[4 * g + 1],
+                         rows_h[4 * g + 2], rows_h[4 * g + 3]);
       }
       __syncwarp();
-      // rows of the 64 keys (invalid tail -> first key row of the batch; P is 0 there)
-      int k0 = lane < have ? bars.tok[s][lane] : 0;
-      int k1 = lane + 32 < have ? bars.tok[s][lane + 32] : 0;
-      int r0 = key_row(a, ri.b, k0), r1 = key_row(a, ri.b, k1);
-      __syncwarp();
-
-      // -- X: own 32 keys, all chunks (QK B operand) --
-      mbar_wait(smem_u32(&bars.x_empty[s]), par ^ 1, a.err, &failed);
-      failed = __any_sync(0xffffffffu, failed);
-      if (!failed) {
-        const uint32_t lead = mapa_shared(smem_u32(&bars.x_full[s]), 0);
-        if (cta == 0 && lane == 0) mbar_arrive_expect_tx(smem_u32(&bars.x_full[s]), 2 * C::kXBytes);
-        __syncwarp();
-        // own keys are tile keys [32*cta, 32*cta+32): held by r0 (cta 0) or r1 (cta 1)
-        bars.rows_own[lane] = cta == 0 ? r0 : r1;
-        __syncwarp();
-        for (int item = lane; item < 8 * C::kChunks; item += 32) {
-          int g = item & 7, c = item >> 3;
-          const CUtensorMap* m = c < C::kNopeChunks ? &maps.k : &maps.kr;
-          int x = c < C::kNopeChunks ? 64 * c : 0;
-          tma_gather4_pair(sX + s * C::kXBytes + c * kChunkBytesX + g * 512, m, lead, x,
-                           bars.rows_own[4 * g], bars.rows_own[4 * g + 1],
-                           bars.rows_own[4 * g + 2], bars.rows_own[4 * g + 3]);
-        }
-        __syncwarp();
+    }
+  } else if (warp >= 7) {
+    // ====== X loaders: own 32 keys x all dims for QK^T (cp.async, 128 threads) ======
+    // thread i owns key i/4 and the 16-byte pieces (i%4) + 4j of its 1152-byte row
+    const int i = threadIdx.x - 7 * 32;
+    const int kk = i >> 2, q4 = i & 3;
+    const char* kbase = static_cast<const char*>(a.key);
+    const char* rbase = static_cast<const char*>(a.key_rope);
+    const int filler = nvalid > 0 ? __ldg(rows) : 0;
+    auto fetch = [&](int t) {
+      int j = kTile * t + kOwn * (int)cta + kk;
+      return j < nvalid ? __ldg(rows + j) : filler;
+    };
+    const uint32_t lead0 = mapa_shared(smem_u32(&bars.x_full[0]), 0);
+    const uint32_t lead1 = mapa_shared(smem_u32(&bars.x_full[1]), 0);
+    auto publish = [&](int t) {   // this thread's copies of tile t have landed
+      fence_proxy_async_smem();
+      mbar_arrive_cluster((t & 1) ? lead1 : lead0);
+    };
+    int nxt = ntiles > 0 ? fetch(0) : 0;
+    for (int t = 0; t < ntiles && !failed; ++t) {
+      const int s = t & 1;
+      const int r = nxt;
+      if (t + 1 < ntiles) nxt = fetch(t + 1);
+      mbar_wait(smem_u32(&bars.x_empty[s]), ((t >> 1) & 1) ^ 1, a.err, &failed);
+      if (failed) break;
+      const char* krow = kbase + (size_t)r * (D * 2);
+      const char* rrow = rbase + (size_t)r * 128;
+      const uint32_t xdst = sX + s * C::kXBytes + kk * 128;
+#pragma unroll
+      for (int j = 0; j < 2 * C::kChunks; ++j) {
+        const int chunk = j >> 1, sub = q4 + 4 * (j & 1);
+        const char* src = chunk < C::kNopeChunks ? krow + chunk * 128 + sub * 16 : rrow + sub * 16;
+        const uint32_t dst = xdst + chunk * kChunkBytesX + ((sub ^ (kk & 7)) << 4);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
       }
-      // -- H: V slots of this CTA for all 64 keys (PV B operand) --
-      mbar_wait(smem_u32(&bars.h_empty[s]), par ^ 1, a.err, &failed);
-      failed = __any_sync(0xffffffffu, failed);
-      if (!failed) {
-        const uint32_t lead = mapa_shared(smem_u32(&bars.h_full[s]), 0);
-        if (cta == 0 && lane == 0) mbar_arrive_expect_tx(smem_u32(&bars.h_full[s]), 2 * C::kHBytes);
-        bars.rows_all[lane] = r0;
-        bars.rows_all[lane + 32] = r1;
-        __syncwarp();
-        for (int item = lane; item < 16 * C::kSlots; item += 32) {
-          int g = item & 15, sl = item >> 4;
-          int j = sl / C::kCpj;
-          int chunk = j * 2 * C::kCpj + (int)cta * C::kCpj + sl % C::kCpj;
-          uint32_t dst = sH + s * C::kHBytes + (g >> 3) * C::kHHalf + sl * kChunkBytesH +
-                         (g & 7) * 512;
-          tma_gather4_pair(dst, &maps.k, lead, 64 * chunk, bars.rows_all[4 * g],
-                           bars.rows_all[4 * g + 1], bars.rows_all[4 * g + 2],
-                           bars.rows_all[4 * g + 3]);
-        }
-        __syncwarp();
+      asm volatile("cp.async.commit_group;" ::: "memory");
+      if (t >= 1) {
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        publish(t - 1);
       }
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    if (ntiles > 0 && !failed) publish(ntiles - 1);
   } else if (warp == 1) {
     // ======================= MMA issuer (pair leader) =======================
     if (cta == 0 && ntiles > 0 && lane == 0) {
@@ -308,17 +332,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint32_t id_qk = idesc_f16(128, kTile, bf16, false, false);
       const uint32_t id_pv = idesc_f16(128, C::kNPV, bf16, false, true);
       mbar_wait(smem_u32(&bars.q_full), 0, a.err, &failed);
+      // Descriptors are built once; each MMA only adds a compile-time byte offset
+      // (>> 4) to the start-address field, which cannot carry: shared addresses < 2^18.
+      const uint64_t dq = smem_desc_sw128(sQ, 16, 1024);
+      const uint64_t dx[2] = {smem_desc_sw128(sX, 16, 1024),
+                              smem_desc_sw128(sX + C::kXBytes, 16, 1024)};
+      const uint64_t dp[2] = {smem_desc_sw128(sP, 16, 1024),
+                              smem_desc_sw128(sP + C::kPBytes, 16, 1024)};
+      const uint64_t dh[2] = {smem_desc_sw128(sH, kChunkBytesH, 1024),
+                              smem_desc_sw128(sH + C::kHBytes, kChunkBytesH, 1024)};
       auto issue_qk = [&](int t) {
         const int s = t & 1;
-        if (!mbar_wait(smem_u32(&bars.x_full[s]), (t >> 1) & 1, a.err, &failed)) return;
+        if (!mbar_wait(smem_u32(&bars.x_full[s]), (t >> 1) & 1, a.err, &failed, true)) return;
         tc_fence_after();
         const uint32_t d = tmem + 32 * s;
+        const uint64_t bx = dx[s];
+#pragma unroll
         for (int c = 0; c < C::kChunks; ++c)
-          for (int u = 0; u < 4; ++u) {
-            uint64_t da = smem_desc_sw128(sQ + c * kHeads * 128 + u * 32, 16, 1024);
-            uint64_t db = smem_desc_sw128(sX + s * C::kXBytes + c * kChunkBytesX + u * 32, 16, 1024);
-            umma_f16<2>(d, da, db, id_qk, (c | u) != 0);
-          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            umma_f16<2>(d, dq + (uint64_t)((c * kHeads * 128 + u * 32) >> 4),
+                        bx + (uint64_t)((c * kChunkBytesX + u * 32) >> 4), id_qk, (c | u) != 0);
         umma_commit_pair(smem_u32(&bars.x_empty[s]), 3);
         umma_commit_pair(smem_u32(&bars.s_full[s]), 3);
       };
@@ -331,15 +365,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         mbar_wait(smem_u32(&bars.h_full[s]), par, a.err, &failed);
         if (failed) break;
         tc_fence_after();
+        const uint64_t bp = dp[s], bh = dh[s];
+#pragma unroll
         for (int j = 0; j < C::kNumPV; ++j)
-          for (int k = 0; k < kTile / 16; ++k) {
-            uint64_t da = smem_desc_sw128(sP + s * C::kPBytes + k * 32, 16, 1024);
-            uint64_t db = smem_desc_sw128(
-                sH + s * C::kHBytes + (k >> 1) * C::kHHalf + j * C::kCpj * kChunkBytesH +
-                    (k & 1) * 2048,
-                kChunkBytesH, 1024);
-            umma_f16<2>(tmem + C::kTmemO + j * (C::kNPV / 2), da, db, id_pv, (t | k) != 0);
-          }
+#pragma unroll
+          for (int k = 0; k < kTile / 16; ++k)
+            umma_f16<2>(tmem + C::kTmemO + j * (C::kNPV / 2), bp + (uint64_t)((k * 32) >> 4),
+                        bh + (uint64_t)(((k >> 1) * C::kHHalf + j * C::kCpj * kChunkBytesH +
+                                         (k & 1) * 2048) >> 4),
+                        id_pv, (t | k) != 0);
         umma_commit_pair(smem_u32(&bars.h_empty[s]), 3);
         umma_commit_pair(smem_u32(&bars.pv_done[s]), 3);
       }
@@ -500,6 +534,8 @@ int launch(const DsaSfaFwdParams* p, cudaStream_t stream) {
     return DSA_ERR_TMA_DESCRIPTOR;
   Args a;
   a.idx = p->sparse_indices;
+  a.key = p->key;
+  a.key_rope = p->key_rope;
   a.act_q = p->act_q;
   a.act_k = p->act_k;
   a.q_row_base = p->q_row_base;
@@ -520,6 +556,10 @@ int launch(const DsaSfaFwdParams* p, cudaStream_t stream) {
   a.s2_cap = (int)p->s2_cap;
   a.sparse_mode = p->sparse_mode;
   a.scale = p->scale;
+  a.ws_rows = static_cast<const int32_t*>(p->workspace);
+  a.ws_count = static_cast<const int32_t*>(p->workspace) + (size_t)p->num_rows * p->topk * p->sparse_block_size;
+  sfa_prep_kernel<<<dim3((unsigned)((p->num_rows + 3) / 4)), dim3(128), 0, stream>>>(
+      a, const_cast<int32_t*>(a.ws_rows), const_cast<int32_t*>(a.ws_count));
   auto kern = sfa_fwd_kernel<D, T>;
   constexpr int kSmem = smem_bytes<D>();
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
@@ -541,6 +581,8 @@ extern "C" int dsa_sfa_fwd(const DsaSfaFwdParams* p, void* stream_) {
       !p->act_q || !p->act_k || !p->q_row_base || !p->out)
     return DSA_ERR_INVALID_ARG;
   if (!p->block_table && !p->k_row_base) return DSA_ERR_INVALID_ARG;
+  if (!p->workspace || p->workspace_bytes < (int64_t)dsa_sfa_fwd_workspace_size(p->num_rows, p->topk, p->sparse_block_size))
+    return DSA_ERR_INVALID_ARG;
   if (p->block_table && (p->page_size < 1 || p->max_blocks < 1)) return DSA_ERR_INVALID_ARG;
   if ((p->softmax_max == nullptr) != (p->softmax_sum == nullptr)) return DSA_ERR_INVALID_ARG;
   const int D = (int)p->d;
@@ -554,4 +596,9 @@ extern "C" int dsa_sfa_fwd(const DsaSfaFwdParams* p, void* stream_) {
     if (D == 128) return launch<128, __half>(p, stream);
   }
   return DSA_ERR_INVALID_ARG;
+}
+
+extern "C" int64_t dsa_sfa_fwd_workspace_size(int64_t num_rows, int64_t topk, int64_t sparse_block_size) {
+  if (num_rows < 0 || topk < 0 || sparse_block_size < 1) return -1;
+  return 4 * (num_rows * topk * sparse_block_size + num_rows);
 }

@@ -156,6 +156,9 @@ def sparse_flash_attention_triton(
         smax = torch.zeros((B, 1, S1, N1), dtype=torch.float32, device=dev)
     ssum = torch.zeros_like(smax)
 
+    ws_bytes = lib().dsa_sfa_fwd_workspace_size(num_rows, topk, int(sparse_block_size))
+    ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=dev)
+
     p = SfaFwdParams()
     p.q, p.q_rope, p.key, p.key_rope = ptr(q), ptr(qr), ptr(k), ptr(kr)
     p.sparse_indices, p.act_q, p.act_k = ptr(si), ptr(act_q), ptr(act_k)
@@ -164,6 +167,7 @@ def sparse_flash_attention_triton(
     p.softmax_max = ptr(smax) if return_softmax_lse else 0
     p.softmax_sum = ptr(ssum) if return_softmax_lse else 0
     p.error_flag = ptr(error_flag(dev))
+    p.workspace, p.workspace_bytes = ptr(ws), ws_bytes
     p.num_rows, p.batch, p.n1, p.d, p.topk = num_rows, B, N1, D, topk
     p.sparse_block_size = int(sparse_block_size)
     p.kv_rows, p.page_size, p.max_blocks, p.s2_cap = kv_rows, page, max_blocks, s2_cap

@@ -73,6 +73,8 @@ typedef struct DsaSfaFwdParams {
   float* softmax_max;
   float* softmax_sum;
   int* error_flag;
+  void* workspace;               /* dsa_sfa_fwd_workspace_size() bytes, caller-owned */
+  int64_t workspace_bytes;
   int64_t num_rows;
   int64_t batch;
   int64_t n1;
@@ -89,6 +91,11 @@ typedef struct DsaSfaFwdParams {
 } DsaSfaFwdParams;
 
 int dsa_sfa_fwd(const DsaSfaFwdParams* params, void* stream);
+
+/* Workspace of dsa_sfa_fwd: the compacted key rows of every query row (int32
+ * [num_rows][topk * sparse_block_size]) and their counts (int32 [num_rows]).
+ * Returns -1 for invalid sizes. */
+int64_t dsa_sfa_fwd_workspace_size(int64_t num_rows, int64_t topk, int64_t sparse_block_size);
 
 #ifdef __cplusplus
 }
