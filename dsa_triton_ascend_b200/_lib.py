@@ -44,6 +44,22 @@ class SfaFwdParams(ctypes.Structure):
     ]
 
 
+class SfaBwdParams(ctypes.Structure):
+    _fields_ = [
+        ("q", _p), ("q_rope", _p), ("key", _p), ("key_rope", _p), ("d_out", _p), ("out", _p),
+        ("softmax_max", _p), ("softmax_sum", _p), ("sparse_indices", _p), ("act_q", _p),
+        ("act_k", _p), ("q_row_base", _p), ("k_row_base", _p), ("block_table", _p),
+        ("dq", _p), ("dqr", _p), ("dk", _p), ("dkr", _p), ("dv", _p),
+        ("dk_acc", _p), ("dkr_acc", _p), ("dv_acc", _p), ("error_flag", _p),
+        ("workspace", _p), ("workspace_bytes", _i64),
+        ("num_rows", _i64), ("batch", _i64), ("n1", _i64), ("d", _i64), ("topk", _i64),
+        ("sparse_block_size", _i64), ("kv_rows", _i64), ("page_size", _i64),
+        ("max_blocks", _i64), ("s2_cap", _i64),
+        ("scale", ctypes.c_float), ("sparse_mode", ctypes.c_int32), ("dtype", ctypes.c_int32),
+        ("defer_cast", ctypes.c_int32),
+    ]
+
+
 _lock = threading.Lock()
 _lib = None
 _err_bufs: dict = {}
@@ -65,6 +81,12 @@ def lib() -> ctypes.CDLL:
                 l.dsa_sfa_fwd.restype = ctypes.c_int
                 l.dsa_sfa_fwd_workspace_size.argtypes = [_i64, _i64, _i64]
                 l.dsa_sfa_fwd_workspace_size.restype = _i64
+                l.dsa_sfa_bwd.argtypes = [ctypes.POINTER(SfaBwdParams), _p]
+                l.dsa_sfa_bwd.restype = ctypes.c_int
+                l.dsa_sfa_bwd_cast.argtypes = [ctypes.POINTER(SfaBwdParams), _p]
+                l.dsa_sfa_bwd_cast.restype = ctypes.c_int
+                l.dsa_sfa_bwd_workspace_size.argtypes = [_i64, _i64, _i64]
+                l.dsa_sfa_bwd_workspace_size.restype = _i64
                 _lib = l
     return _lib
 

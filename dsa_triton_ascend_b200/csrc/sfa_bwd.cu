@@ -1,0 +1,861 @@
+// Sparse flash attention backward for sm_100a (tcgen05).
+//
+// Replaces the reference launch core `_sfa_grad_core` / `_sfa_grad_kernel`
+// (sparse_flash_attention_grad_triton.py:158-308, :334-376).  Same math per query row
+// (b, s1) and valid key u:
+//   P[h,u]  = exp(scale*(q.k_u + qr.kr_u) - softmax_max[h]) / softmax_sum[h]  (sum<=0 -> 1)
+//   dS[h,u] = P[h,u] * (dO[h].v_u - delta[h]) * scale,  delta[h] = dO[h].O[h],  v = k[:D]
+//   dQ = dS K,  dQr = dS Kr,  dK += dS^T Q,  dKr += dS^T Qr,  dV += P^T dO
+// P and dS are rounded to the input dtype before the three products, exactly where the
+// reference kernel rounds them (`.to(k_full.dtype)`, :271-298).
+//
+// Four kernels (the per-query working set -- Q, dO, dQ, 128 heads x 576 dims -- does not
+// fit one SM, and the dK/dV products need the heads as their reduction dimension):
+//   K1 probs : CTA pair per query row (as the forward): S = Q K^T, dP = dO V^T on
+//              tcgen05 (2-SM, heads split 64/64), then P and dS -> bf16 scratch.
+//   K2 dq    : CTA pair per query row: dQ = dS K (nope dims split across the pair like
+//              the forward's P V; rope dims on a padded N=128 MMA).
+//   K3 dkv   : one CTA per (query row, 128-key tile, part): dK = dS^T Q, dV = P^T dO,
+//              dKr = dS^T Qr on tcgen05 (M = 128 keys, K = 128 heads), drained into
+//              fp32 accumulators with coalesced vector reductions (red.global.add.v4.f32),
+//              the scatter-add of the reference (:289-300).
+//   K4 cast  : fp32 accumulators -> key dtype (separate entry point so a multi-GPU
+//              caller can all-reduce the fp32 accumulators first).
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "dsa_b200.h"
+#include "sfa_common.cuh"
+#include "sm100.cuh"
+#include "tma_host.h"
+
+namespace dsa {
+namespace sfa_bwd {
+
+using namespace dsa::sfa;
+
+constexpr int kTile = 64;       // keys per pair tile (K1, K2)
+constexpr int kOwn = 32;        // keys per CTA in a QK^T B operand
+constexpr int kHeads = 64;      // heads per CTA of a pair
+constexpr int kChunk = kOwn * 128;   // one 64-dim chunk of 32 keys
+constexpr int kHeadsPad = 128;  // heads per query row in the dS/P scratch
+constexpr int kKeyTile3 = 128;  // keys per K3 CTA
+
+struct Args {
+  // index fields (see sfa_common.cuh)
+  const int32_t* idx;
+  const int32_t* act_q;
+  const int32_t* act_k;
+  const int32_t* q_row_base;
+  const int32_t* k_row_base;
+  const int32_t* block_table;
+  int num_rows, B, N1, topk, block, kv_rows, page, max_blocks, s2_cap, sparse_mode;
+  float scale;
+  const void* key;
+  const void* key_rope;
+  const void* dout;
+  const void* out;
+  const float* smax;
+  const float* ssum;
+  void* dq;
+  void* dqr;
+  float* dk_acc;
+  float* dkr_acc;
+  float* dv_acc;
+  const int32_t* ws_rows;
+  const int32_t* ws_count;
+  void* ds;        // [num_rows][128][kp] scratch, dtype of the inputs
+  void* pp;        // [num_rows][128][kp]
+  int kp;          // keys per row in the scratch (multiple of 128)
+  int* err;
+};
+
+__device__ __forceinline__ void named_bar(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+// =====================================================================================
+// K1: probabilities and dS
+// =====================================================================================
+template <int D>
+struct Cfg1 {
+  static constexpr int kNope = D / 64;
+  static constexpr int kChunks = kNope + 1;
+  static constexpr int kQBytes = kChunks * kHeads * 128;
+  static constexpr int kOBytes = kNope * kHeads * 128;       // dO
+  static constexpr int kXBytes = kChunks * kChunk;
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffO = kOffQ + kQBytes;
+  static constexpr int kOffX = kOffO + kOBytes;
+  static constexpr int kOffBars = kOffX + 2 * kXBytes;
+};
+
+struct Maps1 {
+  CUtensorMap q, qr, dout;
+};
+
+struct __align__(16) Bars1 {
+  uint64_t q_full;
+  uint64_t x_full[2], x_empty[2], s_full[2], s_free[2];
+  uint32_t tmem_slot;
+  float red[4][32];
+};
+
+constexpr int kThreads1 = 320;   // 0: Q/dO TMA, 1: MMA, 2-5: elementwise, 6-9: key loaders
+
+template <int D, typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads1, 1)
+    sfa_bwd_probs_kernel(const __grid_constant__ Maps1 maps, const Args a) {
+  using C = Cfg1<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  Bars1& bars = *reinterpret_cast<Bars1*>(smem_raw + C::kOffBars);
+  const uint32_t sbase = smem_u32(smem_raw);
+  const uint32_t sQ = sbase + C::kOffQ, sO = sbase + C::kOffO, sX = sbase + C::kOffX;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (sbase & 1023u) {
+    if (threadIdx.x == 0) report_error(a.err, kErrMisaligned);
+    return;
+  }
+  const uint32_t cta = cluster_ctarank();
+  const int row = blockIdx.x >> 1;
+  const RowInfo ri = row_info(a, row);
+  const bool abort = a.err != nullptr && *reinterpret_cast<volatile int*>(a.err) != 0;
+  const int nvalid = (ri.active && !abort) ? __ldg(a.ws_count + row) : 0;
+  // an even number of tiles, so K3's 128-key tiles only ever read written (zeroed) slots
+  const int ntiles = nvalid > 0 ? 2 * ((nvalid + 2 * kTile - 1) / (2 * kTile)) : 0;
+  const int32_t* rows = a.ws_rows + (size_t)row * a.topk * a.block;
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bars.q_full), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&bars.x_full[s]), 2 * 128);
+      mbar_init(smem_u32(&bars.x_empty[s]), 1);
+      mbar_init(smem_u32(&bars.s_full[s]), 1);
+      mbar_init(smem_u32(&bars.s_free[s]), 2);
+    }
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc<2>(smem_u32(&bars.tmem_slot), 128);
+    tmem_relinquish<2>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = bars.tmem_slot;
+  bool failed = false;
+
+  if (warp == 0) {
+    // ---- Q and dO of this CTA's 64 heads (once) ----
+    if (ntiles > 0) {
+      const uint32_t lead = mapa_shared(smem_u32(&bars.q_full), 0);
+      if (cta == 0 && lane == 0)
+        mbar_arrive_expect_tx(smem_u32(&bars.q_full), 2 * (C::kQBytes + C::kOBytes));
+      __syncwarp();
+      const int qrow0 = row * a.N1 + kHeads * (int)cta;
+      if (lane < C::kChunks) {
+        const CUtensorMap* m = lane < C::kNope ? &maps.q : &maps.qr;
+        tma_load_2d_pair(sQ + lane * kHeads * 128, m, lead, lane < C::kNope ? 64 * lane : 0, qrow0);
+      } else if (lane < C::kChunks + C::kNope) {
+        const int c = lane - C::kChunks;
+        tma_load_2d_pair(sO + c * kHeads * 128, &maps.dout, lead, 64 * c, qrow0);
+      }
+    }
+  } else if (warp >= 6) {
+    // ---- own 32 keys of each tile, all dims (cp.async), as in the forward ----
+    const int i = threadIdx.x - 6 * 32;
+    const int kk = i >> 2, q4 = i & 3;
+    const char* kbase = static_cast<const char*>(a.key);
+    const char* rbase = static_cast<const char*>(a.key_rope);
+    const int filler = nvalid > 0 ? __ldg(rows) : 0;
+    auto fetch = [&](int t) {
+      int j = kTile * t + kOwn * (int)cta + kk;
+      return j < nvalid ? __ldg(rows + j) : filler;
+    };
+    const uint32_t lead0 = mapa_shared(smem_u32(&bars.x_full[0]), 0);
+    const uint32_t lead1 = mapa_shared(smem_u32(&bars.x_full[1]), 0);
+    auto publish = [&](int t) {
+      fence_proxy_async_smem();
+      mbar_arrive_cluster((t & 1) ? lead1 : lead0);
+    };
+    int nxt = ntiles > 0 ? fetch(0) : 0;
+    for (int t = 0; t < ntiles && !failed; ++t) {
+      const int s = t & 1;
+      const int r = nxt;
+      if (t + 1 < ntiles) nxt = fetch(t + 1);
+      mbar_wait(smem_u32(&bars.x_empty[s]), ((t >> 1) & 1) ^ 1, a.err, &failed);
+      if (failed) break;
+      const char* krow = kbase + (size_t)r * (D * 2);
+      const char* rrow = rbase + (size_t)r * 128;
+      const uint32_t xdst = sX + s * C::kXBytes + kk * 128;
+#pragma unroll
+      for (int j = 0; j < 2 * C::kChunks; ++j) {
+        const int chunk = j >> 1, sub = q4 + 4 * (j & 1);
+        const char* src = chunk < C::kNope ? krow + chunk * 128 + sub * 16 : rrow + sub * 16;
+        const uint32_t dst = xdst + chunk * kChunk + ((sub ^ (kk & 7)) << 4);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+      if (t >= 1) {
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        publish(t - 1);
+      }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    if (ntiles > 0 && !failed) publish(ntiles - 1);
+  } else if (warp == 1) {
+    // ---- UMMA issue (pair leader) ----
+    if (cta == 0 && ntiles > 0 && lane == 0) {
+      const bool bf16 = ElemTraits<T>::kIsBf16;
+      const uint32_t id = idesc_f16(128, kTile, bf16, false, false);
+      const uint64_t dq = smem_desc_sw128(sQ, 16, 1024);
+      const uint64_t dd = smem_desc_sw128(sO, 16, 1024);
+      const uint64_t dx0 = smem_desc_sw128(sX, 16, 1024);
+      const uint64_t dx1 = smem_desc_sw128(sX + C::kXBytes, 16, 1024);
+      mbar_wait(smem_u32(&bars.q_full), 0, a.err, &failed);
+      for (int t = 0; t < ntiles && !failed; ++t) {
+        const int s = t & 1;
+        if (t >= 2) mbar_wait(smem_u32(&bars.s_free[s]), ((t >> 1) - 1) & 1, a.err, &failed, true);
+        mbar_wait(smem_u32(&bars.x_full[s]), (t >> 1) & 1, a.err, &failed, true);
+        if (failed) break;
+        tc_fence_after();
+        const uint64_t bx = s ? dx1 : dx0;
+        const uint32_t d_s = tmem + 32 * s, d_p = tmem + 64 + 32 * s;
+#pragma unroll
+        for (int c = 0; c < C::kChunks; ++c)
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            umma_f16<2>(d_s, dq + (uint64_t)((c * kHeads * 128 + u * 32) >> 4),
+                        bx + (uint64_t)((c * kChunk + u * 32) >> 4), id, (c | u) != 0);
+#pragma unroll
+        for (int c = 0; c < C::kNope; ++c)
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            umma_f16<2>(d_p, dd + (uint64_t)((c * kHeads * 128 + u * 32) >> 4),
+                        bx + (uint64_t)((c * kChunk + u * 32) >> 4), id, (c | u) != 0);
+        umma_commit_pair(smem_u32(&bars.x_empty[s]), 3);
+        umma_commit_pair(smem_u32(&bars.s_full[s]), 3);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---- elementwise: P, dS -> scratch (both CTAs) ----
+    const int q = warp & 3;
+    const int hrow = 32 * (q & 1) + lane;
+    const int half = q >> 1;
+    const int head = kHeads * (int)cta + hrow;
+    const bool hvalid = head < a.N1;
+    const uint32_t lane_addr = (uint32_t)(32 * q) << 16;
+    const float c2 = a.scale * 1.4426950408889634f;
+    float off = 0.f, inv_sum = 1.f, delta = 0.f;
+    if (hvalid && ntiles > 0) {
+      const size_t hidx = (size_t)row * a.N1 + head;
+      off = __ldg(a.smax + hidx) * 1.4426950408889634f;
+      const float sm = __ldg(a.ssum + hidx);
+      inv_sum = 1.f / (sm > 0.f ? sm : 1.f);
+      const T* dor = reinterpret_cast<const T*>(a.dout) + hidx * D + half * (D / 2);
+      const T* orr = reinterpret_cast<const T*>(a.out) + hidx * D + half * (D / 2);
+      for (int d = 0; d < D / 2; d += 8) {
+        const uint4 u0 = *reinterpret_cast<const uint4*>(dor + d);
+        const uint4 u1 = *reinterpret_cast<const uint4*>(orr + d);
+        const T* x0 = reinterpret_cast<const T*>(&u0);
+        const T* x1 = reinterpret_cast<const T*>(&u1);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) delta += ElemTraits<T>::to_f(x0[e]) * ElemTraits<T>::to_f(x1[e]);
+      }
+    }
+    bars.red[q][lane] = delta;
+    named_bar(1, 128);
+    delta += bars.red[q ^ 2][lane];
+    const uint32_t lead_f0 = mapa_shared(smem_u32(&bars.s_free[0]), 0);
+    const uint32_t lead_f1 = mapa_shared(smem_u32(&bars.s_free[1]), 0);
+    T* ds_row = reinterpret_cast<T*>(a.ds) + ((size_t)row * kHeadsPad + head) * a.kp;
+    T* p_row = reinterpret_cast<T*>(a.pp) + ((size_t)row * kHeadsPad + head) * a.kp;
+    for (int t = 0; t < ntiles; ++t) {
+      const int s = t & 1;
+      mbar_wait(smem_u32(&bars.s_full[s]), (t >> 1) & 1, a.err, &failed);
+      const bool wfail = __any_sync(0xffffffffu, failed);
+      tc_fence_after();
+      uint32_t sr[32], pr[32];
+      if (!wfail) {
+        tmem_ld32(tmem + lane_addr + 32 * s, sr);
+        tmem_ld32(tmem + lane_addr + 64 + 32 * s, pr);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sr[i] = pr[i] = 0u;
+      }
+      tc_fence_before();
+      named_bar(1, 128);
+      if (warp == 2 && lane == 0) mbar_arrive_cluster(s ? lead_f1 : lead_f0);
+      const int nv = min(kTile, nvalid - kTile * t) - kOwn * half;
+      uint32_t pk_p[16], pk_s[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float p[2], g[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int k = 2 * i + e;
+          const bool v = hvalid && k < nv;
+          const float pe = v ? ex2(fmaf(__uint_as_float(sr[k]), c2, -off)) * inv_sum : 0.f;
+          p[e] = pe;
+          g[e] = v ? pe * (__uint_as_float(pr[k]) - delta) * a.scale : 0.f;
+        }
+        pk_p[i] = ElemTraits<T>::pack2(p[0], p[1]);
+        pk_s[i] = ElemTraits<T>::pack2(g[0], g[1]);
+      }
+      const int kcol = kTile * t + kOwn * half;
+      uint4* dst_s = reinterpret_cast<uint4*>(ds_row + kcol);
+      uint4* dst_p = reinterpret_cast<uint4*>(p_row + kcol);
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        dst_s[v] = make_uint4(pk_s[4 * v], pk_s[4 * v + 1], pk_s[4 * v + 2], pk_s[4 * v + 3]);
+        dst_p[v] = make_uint4(pk_p[4 * v], pk_p[4 * v + 1], pk_p[4 * v + 2], pk_p[4 * v + 3]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) tmem_dealloc<2>(tmem, 128);
+}
+
+// =====================================================================================
+// K2: dQ = dS K, dQr = dS Kr
+// =====================================================================================
+template <int D>
+struct Cfg2 {
+  static constexpr int kNope = D / 64;
+  static constexpr int kNPV = D < 256 ? D : 256;
+  static constexpr int kNumPV = D / kNPV;
+  static constexpr int kCpj = kNPV / 128;
+  static constexpr int kSlots = kNope / 2;
+  static constexpr int kABytes = kHeads * 128;               // dS tile: 64 heads x 64 keys
+  static constexpr int kHHalf = kSlots * kChunk;
+  static constexpr int kHNope = 2 * kHHalf;
+  static constexpr int kRope = kTile * 128;                   // rope of all 64 keys
+  static constexpr int kHBytes = kHNope + kRope;
+  static constexpr int kOffA = 0;
+  static constexpr int kOffH = kOffA + 2 * kABytes;
+  static constexpr int kOffBars = kOffH + 2 * kHBytes;
+  static constexpr int kTmemRope = D / 2;
+};
+
+struct Maps2 {
+  CUtensorMap ds, k, kr;
+};
+
+struct __align__(16) Bars2 {
+  uint64_t a_full[2], a_empty[2], h_full[2], h_empty[2], done;
+  uint32_t tmem_slot;
+  int rows_h[2][64];
+};
+
+constexpr int kThreads2 = 256;   // 0,6: V gathers, 1: MMA, 2-5: epilogue, 7: dS tiles
+
+template <int D, typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
+    sfa_bwd_dq_kernel(const __grid_constant__ Maps2 maps, const Args a) {
+  using C = Cfg2<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  Bars2& bars = *reinterpret_cast<Bars2*>(smem_raw + C::kOffBars);
+  const uint32_t sbase = smem_u32(smem_raw);
+  const uint32_t sA = sbase + C::kOffA, sH = sbase + C::kOffH;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (sbase & 1023u) {
+    if (threadIdx.x == 0) report_error(a.err, kErrMisaligned);
+    return;
+  }
+  const uint32_t cta = cluster_ctarank();
+  const int row = blockIdx.x >> 1;
+  const RowInfo ri = row_info(a, row);
+  const bool abort = a.err != nullptr && *reinterpret_cast<volatile int*>(a.err) != 0;
+  const int nvalid = (ri.active && !abort) ? __ldg(a.ws_count + row) : 0;
+  const int ntiles = (nvalid + kTile - 1) / kTile;
+  const int32_t* rows = a.ws_rows + (size_t)row * a.topk * a.block;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&bars.a_full[s]), 1);
+      mbar_init(smem_u32(&bars.a_empty[s]), 1);
+      mbar_init(smem_u32(&bars.h_full[s]), 1);
+      mbar_init(smem_u32(&bars.h_empty[s]), 1);
+    }
+    mbar_init(smem_u32(&bars.done), 1);
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc<2>(smem_u32(&bars.tmem_slot), 512);
+    tmem_relinquish<2>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = bars.tmem_slot;
+  bool failed = false;
+
+  if (warp == 7) {
+    // ---- dS tiles of this CTA's 64 heads ----
+    if (lane == 0) {
+      for (int t = 0; t < ntiles && !failed; ++t) {
+        const int s = t & 1;
+        if (!mbar_wait(smem_u32(&bars.a_empty[s]), ((t >> 1) & 1) ^ 1, a.err, &failed)) break;
+        const uint32_t lead = mapa_shared(smem_u32(&bars.a_full[s]), 0);
+        if (cta == 0) mbar_arrive_expect_tx(smem_u32(&bars.a_full[s]), 2 * C::kABytes);
+        tma_load_2d_pair(sA + s * C::kABytes, &maps.ds, lead, kTile * t,
+                         row * kHeadsPad + kHeads * (int)cta);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 0 || warp == 6) {
+    // ---- V slices of all 64 keys (+ rope of all keys in the leader), TMA gather4 ----
+    const int part = warp == 0 ? 0 : 1;
+    const int nitems = 16 * C::kSlots;
+    int* rows_h = bars.rows_h[part];
+    const int filler = nvalid > 0 ? __ldg(rows) : 0;
+    auto fetch = [&](int j) { return j < nvalid ? __ldg(rows + j) : filler; };
+    for (int t = 0; t < ntiles && !failed; ++t) {
+      const int s = t & 1;
+      mbar_wait(smem_u32(&bars.h_empty[s]), ((t >> 1) & 1) ^ 1, a.err, &failed);
+      failed = __any_sync(0xffffffffu, failed);
+      if (failed) break;
+      const uint32_t lead = mapa_shared(smem_u32(&bars.h_full[s]), 0);
+      if (part == 0 && cta == 0 && lane == 0)
+        mbar_arrive_expect_tx(smem_u32(&bars.h_full[s]), 2 * C::kHNope + C::kRope);
+      rows_h[lane] = fetch(kTile * t + lane);
+      rows_h[lane + 32] = fetch(kTile * t + 32 + lane);
+      __syncwarp();
+      for (int item = part * (nitems / 2) + lane; item < (part + 1) * (nitems / 2); item += 32) {
+        const int g = item & 15, sl = item >> 4;
+        const int j = sl / C::kCpj;
+        const int chunk = j * 2 * C::kCpj + (int)cta * C::kCpj + sl % C::kCpj;
+        const uint32_t dst = sH + s * C::kHBytes + (g >> 3) * C::kHHalf + sl * kChunk + (g & 7) * 512;
+        tma_gather4_pair(dst, &maps.k, lead, 64 * chunk, rows_h[4 * g], rows_h[4 * g + 1],
+                         rows_h[4 * g + 2], rows_h[4 * g + 3]);
+      }
+      if (part == 1 && cta == 0 && lane < 16) {
+        const int g = lane;
+        tma_gather4_pair(sH + s * C::kHBytes + C::kHNope + g * 512, &maps.kr, lead, 0,
+                         rows_h[4 * g], rows_h[4 * g + 1], rows_h[4 * g + 2], rows_h[4 * g + 3]);
+      }
+      __syncwarp();
+    }
+  } else if (warp == 1) {
+    if (cta == 0 && ntiles > 0 && lane == 0) {
+      const bool bf16 = ElemTraits<T>::kIsBf16;
+      const uint32_t id_n = idesc_f16(128, C::kNPV, bf16, false, true);
+      const uint32_t id_r = idesc_f16(128, 128, bf16, false, true);
+      const uint64_t da0 = smem_desc_sw128(sA, 16, 1024), da1 = smem_desc_sw128(sA + C::kABytes, 16, 1024);
+      const uint64_t dh0 = smem_desc_sw128(sH, kChunk, 1024);
+      const uint64_t dh1 = smem_desc_sw128(sH + C::kHBytes, kChunk, 1024);
+      for (int t = 0; t < ntiles && !failed; ++t) {
+        const int s = t & 1;
+        mbar_wait(smem_u32(&bars.a_full[s]), (t >> 1) & 1, a.err, &failed);
+        mbar_wait(smem_u32(&bars.h_full[s]), (t >> 1) & 1, a.err, &failed);
+        if (failed) break;
+        tc_fence_after();
+        const uint64_t ba = s ? da1 : da0, bh = s ? dh1 : dh0;
+#pragma unroll
+        for (int j = 0; j < C::kNumPV; ++j)
+#pragma unroll
+          for (int k = 0; k < kTile / 16; ++k)
+            umma_f16<2>(tmem + j * (C::kNPV / 2), ba + (uint64_t)((k * 32) >> 4),
+                        bh + (uint64_t)(((k >> 1) * C::kHHalf + j * C::kCpj * kChunk + (k & 1) * 2048) >> 4),
+                        id_n, (t | k) != 0);
+        // rope: N=128 with the leader's B half holding the 64 rope dims; the other half
+        // is never read back (it lands in TMEM lanes 64-127)
+#pragma unroll
+        for (int k = 0; k < kTile / 16; ++k)
+          umma_f16<2>(tmem + C::kTmemRope, ba + (uint64_t)((k * 32) >> 4),
+                      bh + (uint64_t)((C::kHNope + k * 2048) >> 4), id_r, (t | k) != 0);
+        umma_commit_pair(smem_u32(&bars.a_empty[s]), 3);
+        umma_commit_pair(smem_u32(&bars.h_empty[s]), 3);
+      }
+      if (!failed) umma_commit_pair(smem_u32(&bars.done), 3);
+    }
+    __syncwarp();
+  } else {
+    // ---- epilogue: dQ, dQr (both CTAs) ----
+    const int q = warp & 3;
+    const int hrow = 32 * (q & 1) + lane;
+    const int half = q >> 1;
+    const int head = kHeads * (int)cta + hrow;
+    const uint32_t lane_addr = (uint32_t)(32 * q) << 16;
+    if (ntiles > 0) mbar_wait(smem_u32(&bars.done), 0, a.err, &failed);
+    const bool read = ntiles > 0 && !__any_sync(0xffffffffu, failed);
+    tc_fence_after();
+    T* qrow = reinterpret_cast<T*>(a.dq) + ((size_t)row * a.N1 + min(head, a.N1 - 1)) * D;
+    for (int j = 0; j < C::kNumPV; ++j) {
+      const int dbase = j * C::kNPV + half * (C::kNPV / 2);
+      for (int cc = 0; cc < C::kNPV / 2; cc += 32) {
+        uint32_t o[32];
+        if (read) {
+          tmem_ld32(tmem + lane_addr + j * (C::kNPV / 2) + cc, o);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0u;
+        }
+        if (head < a.N1) {
+          uint4* dst = reinterpret_cast<uint4*>(qrow + dbase + cc);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = ElemTraits<T>::pack2(__uint_as_float(o[8 * v + 0]), __uint_as_float(o[8 * v + 1]));
+            w.y = ElemTraits<T>::pack2(__uint_as_float(o[8 * v + 2]), __uint_as_float(o[8 * v + 3]));
+            w.z = ElemTraits<T>::pack2(__uint_as_float(o[8 * v + 4]), __uint_as_float(o[8 * v + 5]));
+            w.w = ElemTraits<T>::pack2(__uint_as_float(o[8 * v + 6]), __uint_as_float(o[8 * v + 7]));
+            dst[v] = w;
+          }
+        }
+      }
+    }
+    if (half == 0) {   // lanes 0-63 of the rope accumulator hold dQr of the CTA's heads
+      T* rrow = reinterpret_cast<T*>(a.dqr) + ((size_t)row * a.N1 + min(head, a.N1 - 1)) * 64;
+      for (int cc = 0; cc < 64; cc += 32) {
+        uint32_t o[32];
+        if (read) {
+          tmem_ld32(tmem + lane_addr + C::kTmemRope + cc, o);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0u;
+        }
+        if (head < a.N1) {
+          uint4* dst = reinterpret_cast<uint4*>(rrow + cc);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = ElemTraits<T>::pack2(__uint_as_float(o[8 * v + 0]), __uint_as_float(o[8 * v + 1]));
+            w.y = ElemTraits<T>::pack2(__uint_as_float(o[8 * v + 2]), __uint_as_float(o[8 * v + 3]));
+            w.z = ElemTraits<T>::pack2(__uint_as_float(o[8 * v + 4]), __uint_as_float(o[8 * v + 5]));
+            w.w = ElemTraits<T>::pack2(__uint_as_float(o[8 * v + 6]), __uint_as_float(o[8 * v + 7]));
+            dst[v] = w;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) tmem_dealloc<2>(tmem, 512);
+}
+
+// =====================================================================================
+// K3: dK = dS^T Q, dV = P^T dO, dKr = dS^T Qr  (scatter-add into fp32)
+// =====================================================================================
+// part 0: dK nope (B = Q nope, N = D), 1: dV (B = dO, N = D), 2: dK rope (B = Qr, N = 64)
+template <int D>
+struct Cfg3 {
+  static constexpr int kABytes = 2 * kHeadsPad * 128;        // 128 keys x 128 heads, MN-major
+  static constexpr int kBChunk = kHeadsPad * 128;            // 64 dims x 128 heads
+  static constexpr int kNope = D / 64;
+  static constexpr int kOffA = 0;
+  static constexpr int kOffB = kABytes;
+  static constexpr int kOffStage = kOffB + kNope * kBChunk;
+  static constexpr int kStageBytes = 4 * 32 * 33 * 4;
+  static constexpr int kOffBars = kOffStage + kStageBytes;
+};
+
+struct Maps3 {
+  CUtensorMap ds, pp, q, qr, dout;
+};
+
+struct __align__(16) Bars3 {
+  uint64_t full, done;
+  uint32_t tmem_slot;
+};
+
+constexpr int kThreads3 = 160;   // 0-3: drain (TMEM quadrants 0-3), 4: loads + MMA
+
+template <int D, typename T>
+__global__ void __launch_bounds__(kThreads3, 1)
+    sfa_bwd_dkv_kernel(const __grid_constant__ Maps3 maps, const Args a, int tiles_per_row) {
+  using C = Cfg3<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  Bars3& bars = *reinterpret_cast<Bars3*>(smem_raw + C::kOffBars);
+  const uint32_t sbase = smem_u32(smem_raw);
+  const uint32_t sA = sbase + C::kOffA, sB = sbase + C::kOffB;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int part = blockIdx.y;
+  const int row = blockIdx.x / tiles_per_row;
+  const int kt = blockIdx.x % tiles_per_row;
+  if (sbase & 1023u) {
+    if (threadIdx.x == 0) report_error(a.err, kErrMisaligned);
+    return;
+  }
+  const RowInfo ri = row_info(a, row);
+  const bool abort = a.err != nullptr && *reinterpret_cast<volatile int*>(a.err) != 0;
+  const int nvalid = (ri.active && !abort) ? __ldg(a.ws_count + row) : 0;
+  if (kt * kKeyTile3 >= nvalid) return;   // uniform across the CTA
+  const int ncols = part == 2 ? 64 : D;
+  const int nb_chunks = ncols / 64;
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bars.full), 1);
+    mbar_init(smem_u32(&bars.done), 1);
+    fence_mbarrier_init();
+  }
+  if (warp == 4) {
+    tmem_alloc<1>(smem_u32(&bars.tmem_slot), 512);
+    tmem_relinquish<1>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars.tmem_slot;
+  bool failed = false;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      const uint32_t fb = smem_u32(&bars.full);
+      mbar_arrive_expect_tx(fb, C::kABytes + nb_chunks * C::kBChunk);
+      const CUtensorMap* am = part == 1 ? &maps.pp : &maps.ds;
+      const int hrow0 = row * kHeadsPad;
+      for (int c = 0; c < 2; ++c)   // keys [64c, 64c+64) of the tile, all 128 heads
+        tma_load_2d(sA + c * kHeadsPad * 128, am, fb, kt * kKeyTile3 + 64 * c, hrow0);
+      const CUtensorMap* bm = part == 0 ? &maps.q : part == 1 ? &maps.dout : &maps.qr;
+      for (int c = 0; c < nb_chunks; ++c)
+        tma_load_2d(sB + c * C::kBChunk, bm, fb, 64 * c, row * a.N1);
+      if (mbar_wait(fb, 0, a.err, &failed)) {
+        tc_fence_after();
+        const bool bf16 = ElemTraits<T>::kIsBf16;
+        const int n = ncols < 256 ? ncols : 256;
+        const uint32_t id = idesc_f16(128, n, bf16, true, true);
+        const uint64_t da = smem_desc_sw128(sA, kHeadsPad * 128, 1024);
+        const uint64_t db = smem_desc_sw128(sB, C::kBChunk, 1024);
+        for (int j = 0; j < ncols / n; ++j)
+          for (int k = 0; k < kHeadsPad / 16; ++k)
+            umma_f16<1>(tmem + j * n, da + (uint64_t)((k * 2048) >> 4),
+                        db + (uint64_t)((j * (n / 64) * C::kBChunk + k * 2048) >> 4), id, k != 0);
+        umma_commit(smem_u32(&bars.done));
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---- drain: TMEM row = key; coalesced vector reductions into the fp32 accumulator ----
+    float* acc = part == 0 ? a.dk_acc : part == 1 ? a.dv_acc : a.dkr_acc;
+    const int ld = ncols;
+    float* stage = reinterpret_cast<float*>(smem_raw + C::kOffStage) + warp * 32 * 33;
+    const int key0 = kt * kKeyTile3 + 32 * warp;
+    const int32_t* rows = a.ws_rows + (size_t)row * a.topk * a.block;
+    // row of the key matrix for each of this warp's 32 keys (or -1)
+    const int my_key = key0 + lane;
+    const int my_row = my_key < nvalid ? __ldg(rows + my_key) : -1;
+    mbar_wait(smem_u32(&bars.done), 0, a.err, &failed);
+    const bool wfail = __any_sync(0xffffffffu, failed);
+    tc_fence_after();
+    if (!wfail) {
+      for (int c0 = 0; c0 < ncols; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + c0, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) stage[lane * 33 + i] = __uint_as_float(r[i]);
+        __syncwarp();
+        // 4 keys x 128 bytes per instruction: lane -> (key 4*it + lane/8, cols 4*(lane%8))
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+          const int kr = 4 * it + (lane >> 3), cc = 4 * (lane & 7);
+          const int dst_row = __shfl_sync(0xffffffffu, my_row, kr);
+          if (dst_row >= 0) {
+            const float* sp = stage + kr * 33 + cc;
+            float* gp = acc + (size_t)dst_row * ld + c0 + cc;
+            asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(gp), "f"(sp[0]),
+                         "f"(sp[1]), "f"(sp[2]), "f"(sp[3])
+                         : "memory");
+          }
+        }
+        __syncwarp();
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) tmem_dealloc<1>(tmem, 512);
+}
+
+// =====================================================================================
+// K4: fp32 accumulators -> key dtype
+// =====================================================================================
+template <typename T>
+__global__ void cast_kernel(const float* __restrict__ src, T* __restrict__ dst, int64_t n) {
+  const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (i + 3 < n) {
+    const float4 v = *reinterpret_cast<const float4*>(src + i);
+    uint2 w;
+    w.x = ElemTraits<T>::pack2(v.x, v.y);
+    w.y = ElemTraits<T>::pack2(v.z, v.w);
+    *reinterpret_cast<uint2*>(dst + i) = w;
+  } else {
+    for (int64_t j = i; j < n; ++j) dst[j] = ElemTraits<T>::from_f(src[j]);
+  }
+}
+
+template <typename T>
+int cast_all(const DsaSfaBwdParams* p, cudaStream_t stream) {
+  const int64_t D = p->d;
+  const int64_t n[3] = {p->kv_rows * D, p->kv_rows * 64, p->kv_rows * D};
+  const float* src[3] = {p->dk_acc, p->dkr_acc, p->dv_acc};
+  void* dst[3] = {p->dk, p->dkr, p->dv};
+  for (int i = 0; i < 3; ++i) {
+    if (!dst[i]) continue;
+    const int64_t threads = (n[i] + 3) / 4;
+    cast_kernel<T><<<dim3((unsigned)((threads + 255) / 256)), dim3(256), 0, stream>>>(
+        src[i], static_cast<T*>(dst[i]), n[i]);
+  }
+  return cudaGetLastError() == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
+}
+
+inline int64_t padded_keys(int64_t nent) { return (nent + kKeyTile3 - 1) / kKeyTile3 * kKeyTile3; }
+inline int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
+
+template <int D, typename T>
+int launch(const DsaSfaBwdParams* p, cudaStream_t stream) {
+  const bool bf16 = ElemTraits<T>::kIsBf16;
+  const int64_t nent = p->topk * p->sparse_block_size;
+  const int64_t kp = padded_keys(nent);
+  const uint64_t qrows = (uint64_t)p->num_rows * p->n1;
+  Args a = {};
+  a.idx = p->sparse_indices;
+  a.act_q = p->act_q;
+  a.act_k = p->act_k;
+  a.q_row_base = p->q_row_base;
+  a.k_row_base = p->k_row_base;
+  a.block_table = p->block_table;
+  a.num_rows = (int)p->num_rows;
+  a.B = (int)p->batch;
+  a.N1 = (int)p->n1;
+  a.topk = (int)p->topk;
+  a.block = (int)p->sparse_block_size;
+  a.kv_rows = (int)p->kv_rows;
+  a.page = (int)p->page_size;
+  a.max_blocks = (int)p->max_blocks;
+  a.s2_cap = (int)p->s2_cap;
+  a.sparse_mode = p->sparse_mode;
+  a.scale = p->scale;
+  a.key = p->key;
+  a.key_rope = p->key_rope;
+  a.dout = p->d_out;
+  a.out = p->out;
+  a.smax = p->softmax_max;
+  a.ssum = p->softmax_sum;
+  a.dq = p->dq;
+  a.dqr = p->dqr;
+  a.dk_acc = p->dk_acc;
+  a.dkr_acc = p->dkr_acc;
+  a.dv_acc = p->dv_acc;
+  a.err = p->error_flag;
+  char* ws = static_cast<char*>(p->workspace);
+  a.ws_rows = reinterpret_cast<const int32_t*>(ws);
+  ws += align256(4 * p->num_rows * nent);
+  a.ws_count = reinterpret_cast<const int32_t*>(ws);
+  ws += align256(4 * p->num_rows);
+  a.ds = ws;
+  ws += align256(p->num_rows * kHeadsPad * kp * 2);
+  a.pp = ws;
+  a.kp = (int)kp;
+
+  Maps1 m1;
+  Maps2 m2;
+  Maps3 m3;
+  const uint64_t srows = (uint64_t)p->num_rows * kHeadsPad;
+  if (!make_tmap_2d_16b(&m1.q, p->q, bf16, qrows, D, (uint64_t)D * 2, 64, 64) ||
+      !make_tmap_2d_16b(&m1.qr, p->q_rope, bf16, qrows, 64, 128, 64, 64) ||
+      !make_tmap_2d_16b(&m1.dout, p->d_out, bf16, qrows, D, (uint64_t)D * 2, 64, 64) ||
+      !make_tmap_2d_16b(&m2.ds, a.ds, bf16, srows, kp, kp * 2, 64, 64) ||
+      !make_tmap_2d_16b(&m2.k, p->key, bf16, p->kv_rows, D, (uint64_t)D * 2, 64, 1) ||
+      !make_tmap_2d_16b(&m2.kr, p->key_rope, bf16, p->kv_rows, 64, 128, 64, 1) ||
+      !make_tmap_2d_16b(&m3.ds, a.ds, bf16, srows, kp, kp * 2, 64, 128) ||
+      !make_tmap_2d_16b(&m3.pp, a.pp, bf16, srows, kp, kp * 2, 64, 128) ||
+      !make_tmap_2d_16b(&m3.q, p->q, bf16, qrows, D, (uint64_t)D * 2, 64, 128) ||
+      !make_tmap_2d_16b(&m3.qr, p->q_rope, bf16, qrows, 64, 128, 64, 128) ||
+      !make_tmap_2d_16b(&m3.dout, p->d_out, bf16, qrows, D, (uint64_t)D * 2, 64, 128))
+    return DSA_ERR_TMA_DESCRIPTOR;
+
+  // fp32 accumulators start at zero; the prep pass compacts the valid keys of each row
+  if (cudaMemsetAsync(p->dk_acc, 0, sizeof(float) * p->kv_rows * D, stream) != cudaSuccess ||
+      cudaMemsetAsync(p->dkr_acc, 0, sizeof(float) * p->kv_rows * 64, stream) != cudaSuccess ||
+      cudaMemsetAsync(p->dv_acc, 0, sizeof(float) * p->kv_rows * D, stream) != cudaSuccess)
+    return DSA_ERR_CUDA;
+  sfa_prep_kernel<Args><<<dim3((unsigned)((p->num_rows + 3) / 4)), dim3(128), 0, stream>>>(
+      a, const_cast<int32_t*>(a.ws_rows), const_cast<int32_t*>(a.ws_count));
+
+  {
+    auto k = sfa_bwd_probs_kernel<D, T>;
+    const int smem = Cfg1<D>::kOffBars + (int)sizeof(Bars1);
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return DSA_ERR_CUDA;
+    k<<<dim3(2 * (unsigned)p->num_rows), dim3(kThreads1), smem, stream>>>(m1, a);
+  }
+  {
+    auto k = sfa_bwd_dq_kernel<D, T>;
+    const int smem = Cfg2<D>::kOffBars + (int)sizeof(Bars2);
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return DSA_ERR_CUDA;
+    k<<<dim3(2 * (unsigned)p->num_rows), dim3(kThreads2), smem, stream>>>(m2, a);
+  }
+  {
+    auto k = sfa_bwd_dkv_kernel<D, T>;
+    const int smem = Cfg3<D>::kOffBars + (int)sizeof(Bars3);
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return DSA_ERR_CUDA;
+    const int tiles = (int)(kp / kKeyTile3);
+    k<<<dim3((unsigned)(p->num_rows * tiles), 3), dim3(kThreads3), smem, stream>>>(m3, a, tiles);
+  }
+  if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
+  if (p->defer_cast) return DSA_OK;
+  return cast_all<T>(p, stream);
+}
+
+}  // namespace sfa_bwd
+}  // namespace dsa
+
+extern "C" int64_t dsa_sfa_bwd_workspace_size(int64_t num_rows, int64_t topk, int64_t sparse_block_size) {
+  using namespace dsa::sfa_bwd;
+  if (num_rows < 0 || topk < 0 || sparse_block_size < 1) return -1;
+  const int64_t nent = topk * sparse_block_size;
+  return align256(4 * num_rows * nent) + align256(4 * num_rows) +
+         2 * align256(num_rows * kHeadsPad * padded_keys(nent) * 2);
+}
+
+extern "C" int dsa_sfa_bwd(const DsaSfaBwdParams* p, void* stream_) {
+  using namespace dsa::sfa_bwd;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (!p) return DSA_ERR_INVALID_ARG;
+  if (p->num_rows < 0 || p->n1 < 1 || p->n1 > 128 || p->batch < 1 || p->topk < 1 ||
+      p->sparse_block_size < 1 || p->kv_rows < 1 || !p->q || !p->q_rope || !p->key ||
+      !p->key_rope || !p->d_out || !p->out || !p->softmax_max || !p->softmax_sum ||
+      !p->sparse_indices || !p->act_q || !p->act_k || !p->q_row_base || !p->dq || !p->dqr ||
+      !p->dk_acc || !p->dkr_acc || !p->dv_acc)
+    return DSA_ERR_INVALID_ARG;
+  if (!p->block_table && !p->k_row_base) return DSA_ERR_INVALID_ARG;
+  if (!p->workspace ||
+      p->workspace_bytes < dsa_sfa_bwd_workspace_size(p->num_rows, p->topk, p->sparse_block_size))
+    return DSA_ERR_INVALID_ARG;
+  if (p->num_rows == 0) return DSA_OK;
+  const int D = (int)p->d;
+  if (p->dtype == DSA_DTYPE_BF16) {
+    if (D == 512) return launch<512, __nv_bfloat16>(p, stream);
+    if (D == 256) return launch<256, __nv_bfloat16>(p, stream);
+    if (D == 128) return launch<128, __nv_bfloat16>(p, stream);
+  } else if (p->dtype == DSA_DTYPE_FP16) {
+    if (D == 512) return launch<512, __half>(p, stream);
+    if (D == 256) return launch<256, __half>(p, stream);
+    if (D == 128) return launch<128, __half>(p, stream);
+  }
+  return DSA_ERR_INVALID_ARG;
+}
+
+extern "C" int dsa_sfa_bwd_cast(const DsaSfaBwdParams* p, void* stream_) {
+  using namespace dsa::sfa_bwd;
+  if (!p || !p->dk_acc || !p->dkr_acc || !p->dv_acc || p->kv_rows < 1) return DSA_ERR_INVALID_ARG;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (p->dtype == DSA_DTYPE_BF16) return cast_all<__nv_bfloat16>(p, stream);
+  if (p->dtype == DSA_DTYPE_FP16) return cast_all<__half>(p, stream);
+  return DSA_ERR_INVALID_ARG;
+}

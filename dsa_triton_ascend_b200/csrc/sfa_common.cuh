@@ -1,0 +1,100 @@
+// Index handling shared by the sparse flash attention kernels (forward and backward):
+// query-row -> batch mapping, the per-entry key mask of the reference kernel, key-row
+// translation (dense or paged) and the compaction pre-pass.  The functions are
+// templates over the kernel's argument struct, which must provide the fields
+// idx, act_q, act_k, q_row_base, k_row_base, block_table, num_rows, B, topk, block,
+// kv_rows, page, max_blocks, s2_cap and sparse_mode.
+#pragma once
+
+#include <stdint.h>
+
+namespace dsa {
+namespace sfa {
+
+// Query row -> (batch, position) and the row's visible window.
+struct RowInfo {
+  int b, s1, aq, ak, threshold;
+  bool active;
+};
+
+template <class A>
+__device__ __forceinline__ RowInfo row_info(const A& a, int row) {
+  RowInfo ri;
+  int lo = 0, hi = a.B - 1;
+  while (lo < hi) {  // last batch whose first row <= row
+    int mid = (lo + hi + 1) >> 1;
+    if (__ldg(a.q_row_base + mid) <= row) lo = mid; else hi = mid - 1;
+  }
+  ri.b = lo;
+  ri.s1 = row - __ldg(a.q_row_base + lo);
+  ri.aq = __ldg(a.act_q + lo);
+  ri.ak = __ldg(a.act_k + lo);
+  ri.threshold = a.sparse_mode == 0 ? ri.ak : ri.ak - ri.aq + ri.s1 + 1;
+  ri.active = ri.s1 < ri.aq && ri.threshold > 0;
+  return ri;
+}
+
+// Entry j of the (block-expanded) index row -> key position, or -1 if masked.
+// Mask rule: sparse_flash_attention_triton.py:264-266.
+template <class A>
+__device__ __forceinline__ int key_at(const A& a, const RowInfo& ri, const int32_t* row_idx, int j) {
+  int blk = __ldg(row_idx + j / a.block);
+  if (blk < 0) return -1;
+  int t = blk * a.block + (j % a.block);
+  if (t >= ri.threshold || t >= ri.ak || t >= a.s2_cap) return -1;
+  if (a.block_table) {  // keys in unmapped pages are dropped (see key_row)
+    int pb = __ldg(a.block_table + (size_t)ri.b * a.max_blocks + t / a.page);
+    if (pb < 0 || (long long)pb * a.page >= a.kv_rows) return -1;
+  }
+  return t;
+}
+
+// Key position -> row of the key/key_rope matrices.
+template <class A>
+__device__ __forceinline__ int key_row(const A& a, int b, int t) {
+  if (a.block_table) {
+    int blk = __ldg(a.block_table + (size_t)b * a.max_blocks + t / a.page);
+    return blk * a.page + t % a.page;
+  }
+  return __ldg(a.k_row_base + b) + t;
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+// One warp per query row: compact the row's valid key positions (block-expanded,
+// masked as in sparse_flash_attention_triton.py:264-266) into key-matrix rows, in
+// index order, plus their count.  The attention kernel then streams 64 rows per tile
+// with one coalesced load and no per-tile scanning.
+template <class A>
+__global__ void __launch_bounds__(128) sfa_prep_kernel(const A a, int32_t* ws_rows, int32_t* ws_count) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 4 + warp;
+  if (row >= a.num_rows) return;
+  const RowInfo ri = row_info(a, row);
+  const int nent = a.topk * a.block;
+  int have = 0;
+  if (ri.active) {
+    const int32_t* row_idx = a.idx + (size_t)row * a.topk;
+    int32_t* out = ws_rows + (size_t)row * nent;
+    for (int base = 0; base < nent; base += 32) {
+      const int j = base + lane;
+      const int kp = j < nent ? key_at(a, ri, row_idx, j) : -1;
+      const unsigned m = __ballot_sync(0xffffffffu, kp >= 0);
+      if (kp >= 0) out[have + __popc(m & ((1u << lane) - 1u))] = key_row(a, ri.b, kp);
+      have += __popc(m);
+    }
+  }
+  if (lane == 0) ws_count[row] = have;
+}
+
+
+}  // namespace sfa
+}  // namespace dsa

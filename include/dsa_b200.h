@@ -97,6 +97,70 @@ int dsa_sfa_fwd(const DsaSfaFwdParams* params, void* stream);
  * Returns -1 for invalid sizes. */
 int64_t dsa_sfa_fwd_workspace_size(int64_t num_rows, int64_t topk, int64_t sparse_block_size);
 
+/*
+ * Sparse flash attention backward (MLA-absorb).
+ * Replaces `_sfa_grad_core` / `_sfa_grad_kernel` (sparse_flash_attention_grad_triton.py:334-376,
+ * :158-308).  Query/key addressing as in DsaSfaFwdParams.  Inputs: q, q_rope, key, key_rope,
+ * d_out and out ([num_rows][n1][d]), softmax_max / softmax_sum ([num_rows][n1], the forward's
+ * statistics).  Outputs: dq [num_rows][n1][d], dqr [num_rows][n1][64] (query dtype); the key
+ * gradients are accumulated in caller-provided fp32 buffers dk_acc [kv_rows][d],
+ * dkr_acc [kv_rows][64], dv_acc [kv_rows][d] (zeroed by the call) and, unless defer_cast is
+ * set, cast into dk / dkr / dv (key dtype, NULL to skip).  With defer_cast a caller (e.g. a
+ * multi-GPU one that all-reduces the fp32 buffers) finishes with dsa_sfa_bwd_cast().
+ * The key gradients are scatter-added with fp32 vector reductions, so their summation order
+ * is not deterministic (as in the reference, which rejects deterministic=True).
+ */
+typedef struct DsaSfaBwdParams {
+  const void* q;
+  const void* q_rope;
+  const void* key;
+  const void* key_rope;
+  const void* d_out;
+  const void* out;
+  const float* softmax_max;
+  const float* softmax_sum;
+  const int32_t* sparse_indices;
+  const int32_t* act_q;
+  const int32_t* act_k;
+  const int32_t* q_row_base;
+  const int32_t* k_row_base;
+  const int32_t* block_table;
+  void* dq;
+  void* dqr;
+  void* dk;
+  void* dkr;
+  void* dv;
+  float* dk_acc;
+  float* dkr_acc;
+  float* dv_acc;
+  int* error_flag;
+  void* workspace;               /* dsa_sfa_bwd_workspace_size() bytes, caller-owned */
+  int64_t workspace_bytes;
+  int64_t num_rows;
+  int64_t batch;
+  int64_t n1;
+  int64_t d;
+  int64_t topk;
+  int64_t sparse_block_size;
+  int64_t kv_rows;
+  int64_t page_size;
+  int64_t max_blocks;
+  int64_t s2_cap;
+  float scale;
+  int32_t sparse_mode;
+  int32_t dtype;
+  int32_t defer_cast;            /* 1: leave the key gradients in the fp32 buffers */
+} DsaSfaBwdParams;
+
+int dsa_sfa_bwd(const DsaSfaBwdParams* params, void* stream);
+
+/* Cast dk_acc / dkr_acc / dv_acc into dk / dkr / dv (the tail of dsa_sfa_bwd). */
+int dsa_sfa_bwd_cast(const DsaSfaBwdParams* params, void* stream);
+
+/* Workspace of dsa_sfa_bwd: compacted key rows and counts, plus bf16/fp16 scratch for P and
+ * dS ([num_rows][128][keys padded to 128] each).  Returns -1 for invalid sizes. */
+int64_t dsa_sfa_bwd_workspace_size(int64_t num_rows, int64_t topk, int64_t sparse_block_size);
+
 #ifdef __cplusplus
 }
 #endif

@@ -154,13 +154,15 @@ def sfa_fwd(q, k, qr, kr, tok_idx, scale, act_q=None, act_k=None, sparse_mode=3,
 
 
 def sfa_bwd(q, k, qr, kr, tok_idx, d_out, out, smax, ssum, scale, act_q=None, act_k=None,
-            sparse_mode=3, dtype="bf16"):
+            sparse_mode=3, dtype="bf16", rounding="golden"):
     """SFA backward on BSND numpy inputs; restates ``sparse_flash_attention_grad_triton.py:189-308``.
 
     P = exp(s - max) / sum (sum <= 0 -> 1, :232-234), delta = rowsum(dO*O) (:237),
     dS = P (dO.v - delta) scale (:262-268); dQ = dS K, dQr = dS Kr; dK += dS^T q,
     dKr += dS^T qr, dV += P^T dO scatter-added over rows (:270-300).  Returns
-    (dq, dk, dv, dqr, dkr) rounded to ``dtype``.
+    (dq, dk, dv, dqr, dkr) rounded to ``dtype``.  ``rounding="kernel"`` additionally rounds P
+    and dS to ``dtype`` before the three products, as the reference kernel does
+    (``dS.to(k_full.dtype)``, ``P_t.to(do_sub.dtype)``, :271-298); the golden keeps them fp32.
     """
     q = np.asarray(q, np.float32); k = np.asarray(k, np.float32)
     qr = np.asarray(qr, np.float32); kr = np.asarray(kr, np.float32)
@@ -189,6 +191,9 @@ def sfa_bwd(q, k, qr, kr, tok_idx, d_out, out, smax, ssum, scale, act_q=None, ac
             dpv = do[b, s1] @ kk.T
             delta = (do[b, s1] * o[b, s1]).sum(axis=1)
             dS = P * (dpv - delta[:, None]) * np.float32(scale)
+            if rounding == "kernel":
+                P = round_to(P, dtype)
+                dS = round_to(dS, dtype)
             dq[b, s1] = dS @ kk
             dqr[b, s1] = dS @ kkr
             np.add.at(dk[b, :, 0, :], pos, dS.T @ q[b, s1])
