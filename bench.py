@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Benchmark of the DSA hot path on B200: SFA forward (+ backward) at BASELINE config 4.
+"""Benchmark of the DSA hot path on B200: SFA forward + backward at BASELINE config 4.
 
 Workload (one step): BSND, B=1, S1=S2=8192, N1=128, D=512+64 rope, topK=2048 distinct
 causal key ids per query (-1 padded for early queries), sparse_mode=3, bf16 N(0,1)
@@ -31,7 +31,10 @@ METRIC = "SFA fwd/bwd TFLOP/s + tokens/s at N1=128,D=576,topK=2048; % roofline"
 S1 = S2 = 8192
 N1, D, DR, TOPK = 128, 512, 64, 2048
 FWD_FLOP_PER_PAIR = N1 * (2 * (D + DR) + 2 * D)              # QK^T + P V
+BWD_FLOP_PER_PAIR = N1 * (3 * 2 * (D + DR) + 2 * 2 * D)        # S, dQ, dK (576) + dP, dV (512)
 GATHER_BYTES_PER_PAIR = (D + DR) * 2                           # one bf16 key row
+# backward: the key row gathered twice (scores, dQ) + the fp32 dK/dKr/dV scatter
+BWD_BYTES_PER_PAIR = 2 * GATHER_BYTES_PER_PAIR + 4 * (2 * D + DR)
 
 
 def load_peaks():
@@ -109,28 +112,33 @@ def shard_rows(pairs_per_row: np.ndarray, world: int, rank: int):
 # ----------------------------------------------------------------------------------------
 # CPU side: the reference algorithm (numpy restatement) on a bounded sample of rows
 # ----------------------------------------------------------------------------------------
-def cpu_sample_tflops(seconds_budget: float = 10.0, rows: int = 6):
-    """Time the numpy forward on `rows` query rows spread over config 4 (all 2048 keys
-    valid), scaled by FLOPs.  Returns (TFLOP/s, description, threads)."""
+def cpu_sample_tflops(seconds_budget: float = 10.0, rows: int = 2):
+    """Time the numpy forward + backward (the reference algorithm, restated in oracle/) on
+    `rows` query rows of config 4 with all 2048 keys valid, scaled by FLOPs.
+    Returns (TFLOP/s, description, threads)."""
     from oracle import sfa as osfa
     rng = np.random.default_rng(0)
     q = rng.standard_normal((1, rows, N1, D), dtype=np.float32)
     qr = rng.standard_normal((1, rows, N1, DR), dtype=np.float32)
     k = rng.standard_normal((1, S2, 1, D), dtype=np.float32)
     kr = rng.standard_normal((1, S2, 1, DR), dtype=np.float32)
+    do = rng.standard_normal((1, rows, N1, D), dtype=np.float32)
     si = np.stack([np.sort(rng.permutation(S2)[:TOPK]) for _ in range(rows)]).astype(np.int32)
     si = si.reshape(1, rows, 1, TOPK)
+    sc = 1 / math.sqrt(576)
     t0 = time.perf_counter()
     n_done = 0
     while True:
-        osfa.sfa_fwd(q, k, qr, kr, si, 1 / math.sqrt(576), act_q=[S2], act_k=[S2], sparse_mode=0)
+        out, mx, sm = osfa.sfa_fwd(q, k, qr, kr, si, sc, act_q=[S2], act_k=[S2], sparse_mode=0)
+        osfa.sfa_bwd(q, k, qr, kr, si, do, out, mx, sm, sc, act_q=[S2], act_k=[S2], sparse_mode=0)
         n_done += 1
         if time.perf_counter() - t0 > seconds_budget or n_done >= 50:
             break
     dt = (time.perf_counter() - t0) / n_done
-    flops = rows * TOPK * FWD_FLOP_PER_PAIR
+    flops = rows * TOPK * (FWD_FLOP_PER_PAIR + BWD_FLOP_PER_PAIR)
     threads = torch.get_num_threads()
-    return flops / dt / 1e12, f"numpy SFA forward, {rows} query rows x {TOPK} keys x {N1} heads", threads
+    return (flops / dt / 1e12,
+            f"numpy SFA forward+backward, {rows} query rows x {TOPK} keys x {N1} heads", threads)
 
 
 def run_reference(args, rank, world):
@@ -150,7 +158,7 @@ def run_reference(args, rank, world):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": wall / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "config 4 SFA forward, sampled rows (CPU)", "S1": S1, "S2": S2,
+        "config": {"workload": "config 4 SFA forward + backward, sampled rows (CPU)", "S1": S1, "S2": S2,
                    "N1": N1, "D": D + DR, "topK": TOPK},
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
                          "sample": desc},
@@ -189,6 +197,7 @@ def main():
     from dsa_triton_ascend_b200.synthetic import sfa_prefill, valid_pairs_per_row
 
     w = sfa_prefill(device=dev)
+    dout_full = w["dout"]
     pairs = valid_pairs_per_row(w["si"]).cpu().numpy()
     r0, r1 = shard_rows(pairs, world, rank)
     my_pairs = int(pairs[r0:r1].sum())
@@ -197,6 +206,7 @@ def main():
     qr = w["qr"][:, r0:r1].contiguous()
     si = w["si"][:, r0:r1].contiguous()
     k, kr, scale = w["k"], w["kr"], w["scale"]
+    dout = dout_full[:, r0:r1].contiguous()
     # a row range [r0, r1) of the causal query block is a BSND query of r1-r0 rows whose
     # actual length is S1 - r0: the kernel's causal window act_k - act_q + s1 + 1 then
     # equals the window of the original row r0 + s1.
@@ -207,65 +217,95 @@ def main():
             q, k, k, si, scale, actual_seq_lengths_query=aq, query_rope=qr, key_rope=kr,
             sparse_mode=3, return_softmax_lse=True)
 
+    def bwd(out, mx, sm):
+        """Backward of this rank's rows; the fp32 key gradients are summed over ranks."""
+        accs, finish = dsa.sparse_flash_attention_grad_partial(
+            q, k, k, si, dout, out, mx, sm, scale, query_rope=qr, key_rope=kr,
+            actual_seq_lengths_query=aq, sparse_mode=3)
+        if world > 1:
+            for t in accs:
+                dist.all_reduce(t)
+        return finish()
+
+    def step(ev_f=None, ev_b=None):
+        if ev_f is not None:
+            ev_f[0].record(stream)
+        out, mx, sm = fwd()
+        if ev_f is not None:
+            ev_f[1].record(stream)
+            ev_b[0].record(stream)
+        grads = bwd(out, mx, sm)
+        if ev_b is not None:
+            ev_b[1].record(stream)
+        return out, grads
+
     def barrier():
         if world > 1:
             dist.barrier()
 
     stream = torch.cuda.current_stream(dev)
     for _ in range(args.warmup):
-        fwd()
+        step()
     torch.cuda.synchronize(dev)
     dsa.check_device_errors(dev)
 
     sampler = ClockSampler(local)
     sampler.start()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(args.steps)]
+    mk = lambda: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+    ev_f = [mk() for _ in range(args.steps)]
+    ev_b = [mk() for _ in range(args.steps)]
     barrier()
     torch.cuda.synchronize(dev)
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     start.record(stream)
     for i in range(args.steps):
-        ev[i][0].record(stream)
-        fwd()
-        ev[i][1].record(stream)
+        step(ev_f[i], ev_b[i])
     end.record(stream)
     torch.cuda.synchronize(dev)
     barrier()
     clocks = sampler.stop()
     dsa.check_device_errors(dev)
     ms_total = start.elapsed_time(end)
-    fwd_ms = float(np.mean([a.elapsed_time(b) for a, b in ev]))
+    fwd_ms = float(np.mean([a.elapsed_time(b) for a, b in ev_f]))
+    bwd_ms = float(np.mean([a.elapsed_time(b) for a, b in ev_b]))
     t = torch.tensor([ms_total], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_step = float(t.item()) / args.steps
 
-    fwd_flops_total = total_pairs * FWD_FLOP_PER_PAIR
-    value = fwd_flops_total / (ms_step * 1e-3) / 1e12
+    flops_total = total_pairs * (FWD_FLOP_PER_PAIR + BWD_FLOP_PER_PAIR)
+    value = flops_total / (ms_step * 1e-3) / 1e12
     tokens_per_s = S1 / (ms_step * 1e-3)
 
     # ---- end to end through the public API with host buffers (pinned) ----
-    hq, hqr, hk, hkr, hsi = (x.cpu().pin_memory() for x in (q, qr, k, kr, si))
-    h2d = sum(x.numel() * x.element_size() for x in (hq, hqr, hk, hkr, hsi))
-    out_h = torch.empty(q.shape, dtype=q.dtype).pin_memory()
-    st_h = torch.empty((1, 1, r1 - r0, N1), dtype=torch.float32).pin_memory()
-    d2h = out_h.numel() * 2 + 2 * st_h.numel() * 4
+    host_in = [x.cpu().pin_memory() for x in (q, qr, k, kr, si, dout)]
+    h2d = sum(x.numel() * x.element_size() for x in host_in)
+    outs_h = None
 
     def e2e_step():
-        dq_, dqr_, dk_, dkr_, dsi_ = (x.to(dev, non_blocking=True) for x in (hq, hqr, hk, hkr, hsi))
-        o, m, s = dsa.sparse_flash_attention_triton(
-            dq_, dk_, dk_, dsi_, scale, actual_seq_lengths_query=aq, query_rope=dqr_, key_rope=dkr_,
-            sparse_mode=3, return_softmax_lse=True)
-        out_h.copy_(o, non_blocking=True)
-        st_h.copy_(m, non_blocking=True)
-        st_h.copy_(s, non_blocking=True)
+        nonlocal outs_h
+        dq_, dqr_, dk_, dkr_, dsi_, ddo_ = (x.to(dev, non_blocking=True) for x in host_in)
+        o, m, s_ = dsa.sparse_flash_attention_triton(
+            dq_, dk_, dk_, dsi_, scale, actual_seq_lengths_query=aq, query_rope=dqr_,
+            key_rope=dkr_, sparse_mode=3, return_softmax_lse=True)
+        accs, finish = dsa.sparse_flash_attention_grad_partial(
+            dq_, dk_, dk_, dsi_, ddo_, o, m, s_, scale, query_rope=dqr_, key_rope=dkr_,
+            actual_seq_lengths_query=aq, sparse_mode=3)
+        if world > 1:
+            for t in accs:
+                dist.all_reduce(t)
+        res = [o] + list(finish())
+        if outs_h is None:
+            outs_h = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in res]
+        for h, t in zip(outs_h, res):
+            h.copy_(t, non_blocking=True)
 
     for _ in range(2):
         e2e_step()
     torch.cuda.synchronize(dev)
-    e_steps = max(2, min(args.steps, 5))
+    d2h = sum(x.numel() * x.element_size() for x in outs_h)
+    e_steps = max(2, min(args.steps, 4))
     barrier()
     torch.cuda.synchronize(dev)
     e0 = torch.cuda.Event(enable_timing=True)
@@ -279,27 +319,32 @@ def main():
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_ms = float(te.item()) / e_steps
-    e2e_value = fwd_flops_total / (e2e_ms * 1e-3) / 1e12
+    e2e_value = flops_total / (e2e_ms * 1e-3) / 1e12
 
     hbm_peak, tf_peak, peak_kind = load_peaks()
-    # roofline of the dominant kernel (SFA forward) on this rank's share
-    fwd_bytes = my_pairs * GATHER_BYTES_PER_PAIR
-    fwd_flops = my_pairs * FWD_FLOP_PER_PAIR
-    achieved_gbs = fwd_bytes / (fwd_ms * 1e-3) / 1e9
-    achieved_tf = fwd_flops / (fwd_ms * 1e-3) / 1e12
-    t_bytes = fwd_bytes / (hbm_peak * 1e9)
-    t_flops = fwd_flops / (tf_peak * 1e12)
+    # roofline of the dominant call on this rank's share (fwd or bwd, whichever is longer):
+    # time bound = max(algorithmic FLOPs / tensor peak, algorithmic bytes / HBM peak)
+    if bwd_ms >= fwd_ms:
+        kname, kms = "dsa_sfa_bwd", bwd_ms
+        kflops, kbytes = my_pairs * BWD_FLOP_PER_PAIR, my_pairs * BWD_BYTES_PER_PAIR
+    else:
+        kname, kms = "dsa_sfa_fwd", fwd_ms
+        kflops, kbytes = my_pairs * FWD_FLOP_PER_PAIR, my_pairs * GATHER_BYTES_PER_PAIR
+    t_bytes = kbytes / (hbm_peak * 1e9)
+    t_flops = kflops / (tf_peak * 1e12)
     bound = "hbm" if t_bytes >= t_flops else "tensor"
     roof = {"bound": bound,
-            "achieved": achieved_gbs if bound == "hbm" else achieved_tf,
+            "achieved": kbytes / (kms * 1e-3) / 1e9 if bound == "hbm" else kflops / (kms * 1e-3) / 1e12,
             "peak": hbm_peak if bound == "hbm" else tf_peak,
             "unit": "GB/s" if bound == "hbm" else "TFLOP/s",
-            "frac": (t_bytes if bound == "hbm" else t_flops) / (fwd_ms * 1e-3),
+            "frac": max(t_bytes, t_flops) / (kms * 1e-3),
             "traffic": None,
-            "kernel": "dsa_sfa_fwd",
+            "kernel": kname,
             "peak_source": peak_kind,
-            "tensor_frac": t_flops / (fwd_ms * 1e-3),
-            "achieved_tflops": achieved_tf}
+            "tensor_frac": t_flops / (kms * 1e-3),
+            "achieved_tflops": kflops / (kms * 1e-3) / 1e12}
+    fwd_roof_frac = max(my_pairs * GATHER_BYTES_PER_PAIR / (hbm_peak * 1e9),
+                        my_pairs * FWD_FLOP_PER_PAIR / (tf_peak * 1e12)) / (fwd_ms * 1e-3)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -312,14 +357,18 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded bf16 N(0,1), causal distinct top-k ids)",
-            "config": {"workload": "BASELINE config 4 SFA forward (B=1, S1=S2=8192, N1=128, D=512+64, topK=2048, mode 3)",
+            "config": {"workload": "BASELINE config 4 SFA forward + backward (B=1, S1=S2=8192, N1=128, D=512+64, topK=2048, mode 3)",
                        "global_batch": 1, "seq_len": S1, "parallelism": f"query-row shards x{world}",
                        "l2": "inputs (q 1.2 GB, out 1 GB) exceed L2; the 9.4 MB KV is L2-resident by design"},
             "tokens_per_s": tokens_per_s,
             "fwd_ms": fwd_ms,
+            "bwd_ms": bwd_ms,
+            "fwd_tflops": total_pairs * FWD_FLOP_PER_PAIR / (fwd_ms * 1e-3) / 1e12 if world == 1 else None,
+            "bwd_tflops": total_pairs * BWD_FLOP_PER_PAIR / (bwd_ms * 1e-3) / 1e12 if world == 1 else None,
+            "fwd_roofline_frac": fwd_roof_frac,
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * (2 + 6),   # per step: prep + fwd; prep, 3 bwd kernels, 3 casts
             "roofline": roof,
             "cpu_baseline": cpu,
             "clocks": clocks,
