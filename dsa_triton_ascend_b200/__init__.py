@@ -4,12 +4,14 @@ Drop-in for the operators of 18851871668/dsa_triton_ascend, on CUDA torch tensor
 
 * :func:`sparse_flash_attention_triton` / :class:`SparseFlashAttentionTriton`
 * :func:`sparse_flash_attention_grad_triton` / :class:`SparseFlashAttentionGradTriton`
+* :func:`lightning_indexer_triton` / :class:`LightningIndexerTriton`
 """
 from ._lib import check_device_errors, lib as _load_library  # noqa: F401
 from .sparse_flash_attention import (  # noqa: F401
     SparseFlashAttentionTriton,
     sparse_flash_attention_triton,
 )
+from .lightning_indexer import LightningIndexerTriton, lightning_indexer_triton  # noqa: F401
 from .sparse_flash_attention_grad import (  # noqa: F401
     SparseFlashAttentionGradTriton,
     sparse_flash_attention_grad_partial,
@@ -21,5 +23,7 @@ __all__ = [
     "SparseFlashAttentionTriton",
     "sparse_flash_attention_grad_triton",
     "SparseFlashAttentionGradTriton",
+    "lightning_indexer_triton",
+    "LightningIndexerTriton",
     "check_device_errors",
 ]

@@ -20,6 +20,7 @@ DSA_ERR_CUDA = 2
 DSA_ERR_TMA_DESCRIPTOR = 3
 DSA_DTYPE_BF16 = 0
 DSA_DTYPE_FP16 = 1
+DSA_DTYPE_FP32 = 2
 
 _ERR_TEXT = {
     DSA_ERR_INVALID_ARG: "invalid argument",
@@ -60,6 +61,18 @@ class SfaBwdParams(ctypes.Structure):
     ]
 
 
+class LiParams(ctypes.Structure):
+    _fields_ = [
+        ("query", _p), ("key", _p), ("weights", _p), ("act_q", _p), ("act_k", _p),
+        ("q_row_base", _p), ("k_row_base", _p), ("out_indices", _p), ("out_values", _p),
+        ("error_flag", _p), ("workspace", _p), ("workspace_bytes", _i64),
+        ("q_rows", _i64), ("batch", _i64), ("n1", _i64), ("n2", _i64), ("d", _i64),
+        ("kv_rows", _i64), ("sparse_count", _i64), ("s2_row", _i64), ("s2_cap", _i64),
+        ("q_len_max", _i64), ("q_len_dense", _i64),
+        ("sparse_mode", ctypes.c_int32), ("dtype", ctypes.c_int32), ("weights_dtype", ctypes.c_int32),
+    ]
+
+
 _lock = threading.Lock()
 _lib = None
 _err_bufs: dict = {}
@@ -87,6 +100,10 @@ def lib() -> ctypes.CDLL:
                 l.dsa_sfa_bwd_cast.restype = ctypes.c_int
                 l.dsa_sfa_bwd_workspace_size.argtypes = [_i64, _i64, _i64]
                 l.dsa_sfa_bwd_workspace_size.restype = _i64
+                l.dsa_li_score_topk.argtypes = [ctypes.POINTER(LiParams), _p]
+                l.dsa_li_score_topk.restype = ctypes.c_int
+                l.dsa_li_workspace_size.argtypes = [_i64, _i64, _i64]
+                l.dsa_li_workspace_size.restype = _i64
                 _lib = l
     return _lib
 

@@ -1,0 +1,520 @@
+// Lightning indexer for sm_100a: score (tcgen05) + top-k (radix select).
+//
+// Replaces the reference's `_lightning_indexer_score_core` / `_lightning_indexer_score_kernel`
+// (lightning_indexer_triton.py:147-280, :382-413) and its top-k `_stable_topk` (:339-357).
+//
+// score[row, n2, s2] = sum_{g in group n2} ReLU(q[row, g] . k[s2, n2]) * w[row, g]   (fp32)
+//
+// Score kernel: one CTA per (batch, block of Tq query tokens, key head n2).  The UMMA
+// computes S^T with the keys as M (128 per tile) and the block's (token, head) pairs as
+// N (Tq * G <= 256 columns), so the head reduction of one key is a row of TMEM owned by
+// one thread: ReLU, weight and sum happen in registers and each thread writes Tq scores.
+// Keys stream through a TMA ring (contiguous rows, no gather); TMEM is double buffered so
+// the epilogue of tile t overlaps the MMAs of tile t+1.  Invisible positions get -inf
+// (lightning_indexer_triton.py:271-276); tiles past the block's last visible key are
+// never computed (the top-k pass never reads them).
+//
+// Top-k kernel: one CTA per (row, n2): 4-pass 8-bit radix select of the k-th largest
+// score over the visible prefix, ordered compaction (ties at the threshold taken in
+// ascending index order), then a bitonic sort by (score desc, index asc).  -inf slots
+// get index -1 (:353-355).  Values are returned in the query dtype (:541-542).
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "dsa_b200.h"
+#include "sm100.cuh"
+#include "tma_host.h"
+
+namespace dsa {
+namespace li {
+
+constexpr int kKeys = 128;          // keys per tile (UMMA M)
+constexpr int kThreads = 192;       // 0: TMA, 1: MMA + TMEM, 2-5: epilogue
+
+struct Args {
+  const void* q;            // [q_rows][N1][D]
+  const void* w;            // [q_rows][N1], fp32 / fp16 / bf16
+  const int32_t* act_q;
+  const int32_t* act_k;
+  const int32_t* q_row_base;
+  const int32_t* k_row_base;
+  float* scores;            // [q_rows][N2][s2_row]
+  int* err;
+  int B, N1, N2, G, D, Tq, N, nblk, q_rows_max, s2_row, s2_cap, sparse_mode, w_dtype;
+  int q_len_dense;          // >0: BSND query, every batch has this many rows
+};
+
+__device__ __forceinline__ float load_w(const void* w, int dtype, size_t i) {
+  if (dtype == 2) return __ldg(static_cast<const float*>(w) + i);
+  if (dtype == DSA_DTYPE_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(w)[i]);
+  return __half2float(static_cast<const __half*>(w)[i]);
+}
+
+// Visible keys of query position s1 (lightning_indexer_triton.py:219-227).
+__device__ __forceinline__ int visible_limit(int s1, int aq, int ak, int s2, int mode) {
+  if (s1 >= aq) return 0;
+  if (mode == 3) {
+    int causal = min(max(ak - aq + s1 + 1, 0), s2);
+    return max(0, min(ak, causal));
+  }
+  return max(0, min(ak, s2));
+}
+
+template <int DP>
+struct Cfg {
+  static constexpr int kChunks = DP / 64;
+  static constexpr int kStageBytes = kChunks * kKeys * 128;
+  static constexpr int kStages = DP <= 128 ? 3 : 1;
+  static constexpr int kQBytes = kChunks * 256 * 128;       // up to 256 (token, head) rows
+  static constexpr int kOffQ = 0;
+  static constexpr int kOffK = kQBytes;
+  static constexpr int kOffW = kOffK + kStages * kStageBytes;
+  static constexpr int kOffBars = kOffW + 256 * 4;
+};
+
+struct __align__(16) Bars {
+  uint64_t full[3], empty[3], tfull[2], tfree[2];
+  uint32_t tmem_slot;
+  int lim[256];
+  int qrow[256];
+};
+
+template <int DP, typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    li_score_kernel(const __grid_constant__ CUtensorMap kmap, const Args a) {
+  using C = Cfg<DP>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  Bars& bars = *reinterpret_cast<Bars*>(smem_raw + C::kOffBars);
+  float* w_s = reinterpret_cast<float*>(smem_raw + C::kOffW);
+  const uint32_t sbase = smem_u32(smem_raw);
+  const uint32_t sQ = sbase + C::kOffQ, sK = sbase + C::kOffK;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (sbase & 1023u) {
+    if (threadIdx.x == 0) report_error(a.err, kErrMisaligned);
+    return;
+  }
+  const int b = blockIdx.x / a.nblk;
+  const int s1_0 = (blockIdx.x % a.nblk) * a.Tq;
+  const int n2 = blockIdx.y;
+  const int aq = __ldg(a.act_q + b), ak = __ldg(a.act_k + b);
+  const int nrows_b = a.q_len_dense > 0 ? a.q_len_dense : aq;
+  if (s1_0 >= nrows_b) return;   // uniform
+  const int qbase = __ldg(a.q_row_base + b);
+  const int kbase = __ldg(a.k_row_base + b);
+  const int N = a.N, G = a.G, Tq = a.Tq;
+
+  // ---- per token: visible limit and query row; block key range ----
+  int kmax = 0;
+  for (int tq = threadIdx.x; tq < Tq; tq += kThreads) {
+    const int s1 = s1_0 + tq;
+    const bool exists = s1 < nrows_b;
+    const int lim = exists ? visible_limit(s1, aq, ak, a.s2_cap, a.sparse_mode) : 0;
+    bars.lim[tq] = exists ? lim : -1;
+    bars.qrow[tq] = qbase + s1;
+  }
+  // ---- Q block (N rows x DP, zero padded) and weights into smem ----
+  const T* q = static_cast<const T*>(a.q);
+  uint8_t* gQ = smem_raw + C::kOffQ;
+  for (int i = threadIdx.x; i < N * (DP / 8); i += kThreads) {
+    const int r = i / (DP / 8), piece = i % (DP / 8);
+    const int tq = r / G, g = r % G;
+    const int d0 = piece * 8;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    const int s1 = s1_0 + tq;
+    if (tq < Tq && s1 < nrows_b && d0 < a.D) {
+      const T* src = q + ((size_t)(qbase + s1) * a.N1 + n2 * G + g) * a.D + d0;
+      if (d0 + 8 <= a.D) {
+        v = *reinterpret_cast<const uint4*>(src);
+      } else {
+        T tmp[8];
+        for (int e = 0; e < 8; ++e) tmp[e] = d0 + e < a.D ? src[e] : ElemTraits<T>::from_f(0.f);
+        v = *reinterpret_cast<const uint4*>(tmp);
+      }
+    }
+    const int c = d0 / 64, ch16 = (d0 % 64) / 8;
+    *reinterpret_cast<uint4*>(gQ + c * N * 128 + sw128_offset(r, ch16)) = v;
+  }
+  for (int r = threadIdx.x; r < N; r += kThreads) {
+    const int tq = r / G, g = r % G, s1 = s1_0 + tq;
+    w_s[r] = (tq < Tq && s1 < nrows_b)
+                 ? load_w(a.w, a.w_dtype, (size_t)(qbase + s1) * a.N1 + n2 * G + g)
+                 : 0.f;
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(smem_u32(&bars.full[s]), 1);
+      mbar_init(smem_u32(&bars.empty[s]), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&bars.tfull[s]), 1);
+      mbar_init(smem_u32(&bars.tfree[s]), 4);
+    }
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc<1>(smem_u32(&bars.tmem_slot), 512);
+    tmem_relinquish<1>();
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  for (int tq = 0; tq < Tq; ++tq) kmax = max(kmax, bars.lim[tq]);
+  const int ntiles = (kmax + kKeys - 1) / kKeys;
+  const uint32_t tmem = bars.tmem_slot;
+  bool failed = false;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int t = 0; t < ntiles && !failed; ++t) {
+        const int s = t % C::kStages;
+        if (!mbar_wait(smem_u32(&bars.empty[s]), ((t / C::kStages) & 1) ^ 1, a.err, &failed)) break;
+        const uint32_t fb = smem_u32(&bars.full[s]);
+        mbar_arrive_expect_tx(fb, C::kStageBytes);
+        for (int c = 0; c < C::kChunks; ++c)
+          tma_load_3d(sK + s * C::kStageBytes + c * kKeys * 128, &kmap, fb, 64 * c, n2,
+                      kbase + kKeys * t);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const bool bf16 = ElemTraits<T>::kIsBf16;
+      const uint32_t id = idesc_f16(128, N, bf16, false, false);
+      const uint64_t dq = smem_desc_sw128(sQ, 16, 1024);
+      for (int t = 0; t < ntiles && !failed; ++t) {
+        const int s = t % C::kStages, buf = t & 1;
+        if (t >= 2) mbar_wait(smem_u32(&bars.tfree[buf]), ((t >> 1) - 1) & 1, a.err, &failed);
+        mbar_wait(smem_u32(&bars.full[s]), (t / C::kStages) & 1, a.err, &failed);
+        if (failed) break;
+        tc_fence_after();
+        const uint64_t dk = smem_desc_sw128(sK + s * C::kStageBytes, 16, 1024);
+#pragma unroll
+        for (int c = 0; c < C::kChunks; ++c)
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            umma_f16<1>(tmem + 256 * buf, dk + (uint64_t)((c * kKeys * 128 + u * 32) >> 4),
+                        dq + (uint64_t)((c * N * 128 + u * 32) >> 4), id, (c | u) != 0);
+        umma_commit(smem_u32(&bars.empty[s]));
+        umma_commit(smem_u32(&bars.tfull[buf]));
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---- epilogue: one key per thread, ReLU * w summed over each token's G heads ----
+    const int qd = warp & 3;
+    const uint32_t lane_addr = (uint32_t)(32 * qd) << 16;
+    for (int t = 0; t < ntiles; ++t) {
+      const int buf = t & 1;
+      mbar_wait(smem_u32(&bars.tfull[buf]), (t >> 1) & 1, a.err, &failed);
+      const bool wfail = __any_sync(0xffffffffu, failed);
+      tc_fence_after();
+      const int key = kKeys * t + 32 * qd + lane;
+      int tok = 0, gcount = 0;
+      float acc = 0.f;
+      auto emit = [&](int tq, float v) {
+        const int lim = bars.lim[tq];
+        if (lim >= 0 && key < a.s2_row) {
+          float* dst = a.scores + ((size_t)bars.qrow[tq] * a.N2 + n2) * a.s2_row + key;
+          *dst = key < lim ? v : -INFINITY;
+        }
+      };
+      for (int c0 = 0; c0 < N; c0 += 32) {
+        uint32_t r[32];
+        if (!wfail) {
+          tmem_ld32(tmem + lane_addr + 256 * buf + c0, r);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = 0u;
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (tok < Tq) {
+            acc = fmaf(fmaxf(__uint_as_float(r[i]), 0.f), w_s[c0 + i], acc);
+            if (++gcount == G) {
+              emit(tok, acc);
+              ++tok;
+              gcount = 0;
+              acc = 0.f;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bars.tfree[buf]));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc<1>(tmem, 512);
+}
+
+// =====================================================================================
+// top-k
+// =====================================================================================
+constexpr int kTopkThreads = 512;
+
+__device__ __forceinline__ uint32_t order_key(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_float(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+struct TopkArgs {
+  const float* scores;      // [q_rows][N2][s2_row]
+  const int32_t* act_q;
+  const int32_t* act_k;
+  const int32_t* q_row_base;
+  int32_t* out_idx;         // [q_rows][N2][K]
+  void* out_val;            // [q_rows][N2][K] query dtype, or NULL
+  int* err;
+  int B, N2, K, KP, s2_row, s2_cap, sparse_mode, q_rows, q_len_dense, val_dtype;
+};
+
+// Block-wide exclusive scan of one int per thread (kTopkThreads threads); returns the
+// exclusive prefix and writes the block total into *total.
+__device__ __forceinline__ int block_scan(int v, int* warp_sums, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int s = lane < kTopkThreads / 32 ? warp_sums[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += y;
+    }
+    if (lane < kTopkThreads / 32) warp_sums[lane] = s;
+  }
+  __syncthreads();
+  const int base = warp > 0 ? warp_sums[warp - 1] : 0;
+  const int tot = warp_sums[kTopkThreads / 32 - 1];
+  __syncthreads();
+  *total = tot;
+  return base + x - v;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kTopkThreads) li_topk_kernel(const TopkArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint32_t* keys = reinterpret_cast<uint32_t*>(smem_raw);                       // s2_row
+  unsigned long long* sel = reinterpret_cast<unsigned long long*>(smem_raw + ((a.s2_row * 4 + 15) / 16) * 16);
+  __shared__ int hist[256];
+  __shared__ int warp_sums[32];
+  __shared__ int s_digit, s_above;
+  const int row = blockIdx.x, n2 = blockIdx.y;
+  // batch of this query row
+  int lo = 0, hi = a.B - 1;
+  while (lo < hi) {
+    int mid = (lo + hi + 1) >> 1;
+    if (__ldg(a.q_row_base + mid) <= row) lo = mid; else hi = mid - 1;
+  }
+  const int b = lo, s1 = row - __ldg(a.q_row_base + b);
+  const int aq = __ldg(a.act_q + b), ak = __ldg(a.act_k + b);
+  int lim = visible_limit(s1, aq, ak, a.s2_cap, a.sparse_mode);
+  if (a.q_len_dense <= 0 && s1 >= aq) lim = 0;
+  lim = min(lim, a.s2_row);
+  const float* src = a.scores + ((size_t)row * a.N2 + n2) * a.s2_row;
+  for (int i = threadIdx.x; i < lim; i += kTopkThreads) keys[i] = order_key(src[i]);
+  __syncthreads();
+  const int K = a.K;
+  int nsel;
+  if (lim <= K) {
+    for (int i = threadIdx.x; i < lim; i += kTopkThreads)
+      sel[i] = ((unsigned long long)keys[i] << 32) | (uint32_t)(~(uint32_t)i);
+    nsel = lim;
+  } else {
+    // radix select: after the 4 passes `prefix` is the key of the K-th largest element
+    uint32_t prefix = 0, mask = 0;
+    int remaining = K;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int i = threadIdx.x; i < 256; i += kTopkThreads) hist[i] = 0;
+      __syncthreads();
+      for (int i = threadIdx.x; i < lim; i += kTopkThreads) {
+        const uint32_t k = keys[i];
+        if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255], 1);
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        int above = 0, d = 255;
+        for (; d > 0; --d) {
+          if (above + hist[d] >= remaining) break;
+          above += hist[d];
+        }
+        s_digit = d;
+        s_above = above;
+      }
+      __syncthreads();
+      prefix |= (uint32_t)s_digit << shift;
+      mask |= 255u << shift;
+      remaining -= s_above;
+      __syncthreads();
+    }
+    const uint32_t thr = prefix;
+    // ordered compaction: all keys > thr, and the first `remaining` keys == thr by index
+    int gt_base = 0, eq_base = 0;
+    for (int base = 0; base < lim; base += kTopkThreads) {
+      const int i = base + threadIdx.x;
+      const uint32_t k = i < lim ? keys[i] : 0u;
+      const int is_gt = (i < lim && k > thr) ? 1 : 0;
+      const int is_eq = (i < lim && k == thr) ? 1 : 0;
+      int tot_gt, tot_eq;
+      const int pg = block_scan(is_gt, warp_sums, &tot_gt);
+      const int pe = block_scan(is_eq, warp_sums, &tot_eq);
+      const unsigned long long comp = ((unsigned long long)k << 32) | (uint32_t)(~(uint32_t)i);
+      if (is_gt) sel[gt_base + pg] = comp;
+      if (is_eq && eq_base + pe < remaining) sel[(K - remaining) + eq_base + pe] = comp;
+      gt_base += tot_gt;
+      eq_base += tot_eq;
+    }
+    nsel = K;
+  }
+  for (int i = nsel + threadIdx.x; i < a.KP; i += kTopkThreads) sel[i] = 0ull;
+  __syncthreads();
+  // bitonic sort, descending
+  for (int size = 2; size <= a.KP; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < a.KP; i += kTopkThreads) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const bool desc = (i & size) == 0;
+          const unsigned long long x = sel[i], y = sel[j];
+          if (desc ? (x < y) : (x > y)) {
+            sel[i] = y;
+            sel[j] = x;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  int32_t* oi = a.out_idx + ((size_t)row * a.N2 + n2) * K;
+  T* ov = a.out_val ? static_cast<T*>(a.out_val) + ((size_t)row * a.N2 + n2) * K : nullptr;
+  for (int j = threadIdx.x; j < K; j += kTopkThreads) {
+    if (j < nsel) {
+      const unsigned long long c = sel[j];
+      oi[j] = (int32_t)(~(uint32_t)(c & 0xffffffffull));
+      if (ov) ov[j] = ElemTraits<T>::from_f(key_float((uint32_t)(c >> 32)));
+    } else {
+      oi[j] = -1;
+      if (ov) ov[j] = ElemTraits<T>::from_f(-INFINITY);
+    }
+  }
+}
+
+template <int DP, typename T>
+int launch(const DsaLiParams* p, cudaStream_t stream) {
+  using C = Cfg<DP>;
+  const bool bf16 = ElemTraits<T>::kIsBf16;
+  const int G = (int)(p->n1 / p->n2);
+  const int Tq = 256 / G > 0 ? 256 / G : 0;
+  if (Tq < 1) return DSA_ERR_INVALID_ARG;
+  const int N = ((Tq * G + 15) / 16) * 16;
+  CUtensorMap kmap;
+  // key viewed as {D, N2, kv_rows}; box {64, 1, 128}
+  if (!make_tmap_3d_16b(&kmap, p->key, bf16, p->d, p->n2, p->kv_rows, (uint64_t)p->d * 2,
+                        (uint64_t)p->n2 * p->d * 2, 64, 1, kKeys))
+    return DSA_ERR_TMA_DESCRIPTOR;
+  Args a;
+  a.q = p->query;
+  a.w = p->weights;
+  a.act_q = p->act_q;
+  a.act_k = p->act_k;
+  a.q_row_base = p->q_row_base;
+  a.k_row_base = p->k_row_base;
+  a.scores = static_cast<float*>(p->workspace);
+  a.err = p->error_flag;
+  a.B = (int)p->batch;
+  a.N1 = (int)p->n1;
+  a.N2 = (int)p->n2;
+  a.G = G;
+  a.D = (int)p->d;
+  a.Tq = Tq;
+  a.N = N;
+  a.q_rows_max = (int)p->q_len_max;
+  a.nblk = (int)((p->q_len_max + Tq - 1) / Tq);
+  a.s2_row = (int)p->s2_row;
+  a.s2_cap = (int)p->s2_cap;
+  a.sparse_mode = p->sparse_mode;
+  a.w_dtype = p->weights_dtype;
+  a.q_len_dense = (int)p->q_len_dense;
+  auto k = li_score_kernel<DP, T>;
+  const int smem = C::kOffBars + (int)sizeof(Bars);
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return DSA_ERR_CUDA;
+  if (a.nblk > 0)
+    k<<<dim3((unsigned)(p->batch * a.nblk), (unsigned)p->n2), dim3(kThreads), smem, stream>>>(kmap, a);
+
+  TopkArgs t;
+  t.scores = a.scores;
+  t.act_q = p->act_q;
+  t.act_k = p->act_k;
+  t.q_row_base = p->q_row_base;
+  t.out_idx = p->out_indices;
+  t.out_val = p->out_values;
+  t.err = p->error_flag;
+  t.B = (int)p->batch;
+  t.N2 = (int)p->n2;
+  t.K = (int)p->sparse_count;
+  int kp = 1;
+  while (kp < t.K) kp <<= 1;
+  t.KP = kp;
+  t.s2_row = (int)p->s2_row;
+  t.s2_cap = (int)p->s2_cap;
+  t.sparse_mode = p->sparse_mode;
+  t.q_rows = (int)p->q_rows;
+  t.q_len_dense = (int)p->q_len_dense;
+  const int tsmem = ((t.s2_row * 4 + 15) / 16) * 16 + kp * 8;
+  if (tsmem > 200 * 1024) return DSA_ERR_INVALID_ARG;
+  if (cudaFuncSetAttribute(li_topk_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, tsmem) !=
+      cudaSuccess)
+    return DSA_ERR_CUDA;
+  li_topk_kernel<T><<<dim3((unsigned)p->q_rows, (unsigned)p->n2), dim3(kTopkThreads), tsmem, stream>>>(t);
+  return cudaGetLastError() == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
+}
+
+}  // namespace li
+}  // namespace dsa
+
+extern "C" int64_t dsa_li_workspace_size(int64_t q_rows, int64_t n2, int64_t s2_row) {
+  if (q_rows < 0 || n2 < 1 || s2_row < 0) return -1;
+  return 4 * q_rows * n2 * s2_row;
+}
+
+extern "C" int dsa_li_score_topk(const DsaLiParams* p, void* stream_) {
+  using namespace dsa::li;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (!p || !p->query || !p->key || !p->weights || !p->act_q || !p->act_k || !p->q_row_base ||
+      !p->k_row_base || !p->out_indices || !p->workspace)
+    return DSA_ERR_INVALID_ARG;
+  if (p->n1 < 1 || p->n2 < 1 || p->n1 % p->n2 != 0 || p->n1 / p->n2 > 256 || p->d < 16 ||
+      p->d > 256 || p->d % 8 != 0 || p->sparse_count < 1 || p->sparse_count > 4096 ||
+      p->sparse_count > p->s2_row || p->batch < 1 || p->kv_rows < 1)
+    return DSA_ERR_INVALID_ARG;
+  if (p->workspace_bytes < dsa_li_workspace_size(p->q_rows, p->n2, p->s2_row))
+    return DSA_ERR_INVALID_ARG;
+  if (p->q_rows == 0) return DSA_OK;
+  const int dp = p->d <= 64 ? 64 : p->d <= 128 ? 128 : 256;
+  if (p->dtype == DSA_DTYPE_BF16) {
+    if (dp == 64) return launch<64, __nv_bfloat16>(p, stream);
+    if (dp == 128) return launch<128, __nv_bfloat16>(p, stream);
+    return launch<256, __nv_bfloat16>(p, stream);
+  }
+  if (p->dtype == DSA_DTYPE_FP16) {
+    if (dp == 64) return launch<64, __half>(p, stream);
+    if (dp == 128) return launch<128, __half>(p, stream);
+    return launch<256, __half>(p, stream);
+  }
+  return DSA_ERR_INVALID_ARG;
+}

@@ -171,6 +171,16 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// 3-D tile load into own smem, completion on own barrier.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int32_t x, int32_t y, int32_t z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
 // 2-D tile load into own smem whose completion is signalled on the barrier of the
 // pair-leader CTA (`leader_bar` is a cluster-window address).
 __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map,

@@ -1,0 +1,135 @@
+"""lightning_indexer_triton: drop-in lightning indexer (score + top-k) on B200.
+
+Same name, argument order, defaults and guards as the reference
+``lightning_indexer_triton`` (lightning_indexer_triton.py:462-550) and its
+``LightningIndexerTriton`` cell (:416-459).  BSND / TND layouts are addressed in place.
+The score matrix is computed by a tcgen05 kernel and reduced by a radix-select top-k
+kernel (``dsa_li_score_topk``).  Ties are broken by ascending key index (the reference's
+default ``mint.topk`` leaves their order unspecified, :349-351).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _host as H
+from ._lib import LiParams, DSA_DTYPE_FP32, check, error_flag, lib, ptr, stream_ptr
+
+INT64_MAX = H.INT64_MAX
+
+
+def _weights_code(w: torch.Tensor) -> int:
+    if w.dtype == torch.float32:
+        return DSA_DTYPE_FP32
+    return H.dtype_code(w)
+
+
+def lightning_indexer_triton(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    weights: torch.Tensor,
+    actual_seq_lengths_query=None,
+    actual_seq_lengths_key=None,
+    block_table=None,
+    layout_query="BSND",
+    layout_key="BSND",
+    sparse_count=2048,
+    sparse_mode=3,
+    pre_tokens=INT64_MAX,
+    next_tokens=INT64_MAX,
+    return_value=False,
+):
+    """Lightning indexer: returns (sparse_indices int32 [.., N2, sparse_count], values in the
+    query dtype (zeros unless ``return_value``)).  ``pre_tokens``/``next_tokens`` are
+    ignored, as in the reference."""
+    if block_table is not None:   # lightning_indexer_triton.py:497-498
+        raise ValueError("PA_BSND / block_table not supported in triton lightning_indexer")
+    if sparse_mode not in (0, 3):
+        raise ValueError("Only sparse_mode 0 (full) / 3 (rightDownCausal) supported")
+    H.require_cuda(query, key, weights)
+    dev = query.device
+    is_tnd = layout_query == "TND"
+    if is_tnd:
+        cum_q = H.cumulative(actual_seq_lengths_query, dev)
+        cum_k = H.cumulative(actual_seq_lengths_key, dev)
+        B = cum_q.numel()
+        q_base, act_q = H.tnd_offsets(cum_q)
+        _, act_k = H.tnd_offsets(cum_k)
+        T1, N1, D = query.shape
+        q_rows = T1
+        q_len_max = int(act_q.max().item()) if B > 0 else 0
+        q_len_dense = 0
+        if layout_key == "TND":
+            k_base, _ = H.tnd_offsets(cum_k)
+            kv_rows, N2 = key.shape[0], key.shape[1]
+            s2 = int(act_k.max().item()) if B > 0 else 0
+        else:
+            kv_rows, N2 = key.shape[0] * key.shape[1], key.shape[2]
+            s2 = key.shape[1]
+            k_base = H.row_bases(B, s2, dev)
+    else:
+        B, S1, N1, D = query.shape
+        _, S2, N2, _ = key.shape
+        q_rows, q_len_max, q_len_dense = B * S1, S1, S1
+        q_base = H.row_bases(B, S1, dev)
+        k_base = H.row_bases(B, S2, dev)
+        act_q = H.lens_tensor(actual_seq_lengths_query, B, S1, dev)
+        act_k = H.lens_tensor(actual_seq_lengths_key, B, S2, dev)
+        kv_rows, s2 = B * S2, S2
+    if N1 % N2 != 0:              # lightning_indexer_triton.py:520-521
+        raise ValueError(f"N1({N1}) must be divisible by N2({N2})")
+    if key.shape[-1] != D or key.dtype != query.dtype:
+        raise ValueError("query and key must share dtype and head dim")
+    k_eff = min(int(sparse_count), s2)
+    if k_eff != int(sparse_count):
+        # the reference reshapes min(k, S2) results into sparse_count columns and fails
+        raise ValueError(f"sparse_count ({sparse_count}) exceeds the key length ({s2})")
+    q = query.contiguous()
+    k = key.contiguous()
+    w = weights.contiguous()
+    K = int(sparse_count)
+    out_shape = (q_rows, N2, K) if is_tnd else (B, S1, N2, K)
+    indices = torch.empty(out_shape, dtype=torch.int32, device=dev)
+    values = (torch.empty(out_shape, dtype=query.dtype, device=dev) if return_value
+              else torch.zeros(out_shape, dtype=query.dtype, device=dev))
+    ws_bytes = lib().dsa_li_workspace_size(q_rows, N2, s2)
+    ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=dev)
+    p = LiParams()
+    p.query, p.key, p.weights = ptr(q), ptr(k), ptr(w)
+    p.act_q, p.act_k, p.q_row_base, p.k_row_base = ptr(act_q), ptr(act_k), ptr(q_base), ptr(k_base)
+    p.out_indices = ptr(indices)
+    p.out_values = ptr(values) if return_value else 0
+    p.error_flag = ptr(error_flag(dev))
+    p.workspace, p.workspace_bytes = ptr(ws), ws_bytes
+    p.q_rows, p.batch, p.n1, p.n2, p.d, p.kv_rows = q_rows, B, N1, N2, D, kv_rows
+    p.sparse_count, p.s2_row, p.s2_cap = K, s2, s2
+    p.q_len_max, p.q_len_dense = q_len_max, q_len_dense
+    p.sparse_mode = int(sparse_mode)
+    p.dtype = H.dtype_code(query)
+    p.weights_dtype = _weights_code(w)
+    check(lib().dsa_li_score_topk(p, stream_ptr(dev)), "dsa_li_score_topk")
+    return indices, values
+
+
+class LightningIndexerTriton(torch.nn.Module):
+    """Module wrapper (reference cell: lightning_indexer_triton.py:416-459)."""
+
+    def __init__(self, sparse_count=2048, sparse_mode=3, layout_query="BSND", layout_key="BSND",
+                 return_value=False, pre_tokens=INT64_MAX, next_tokens=INT64_MAX):
+        super().__init__()
+        self.sparse_count = sparse_count
+        self.sparse_mode = sparse_mode
+        self.layout_query = layout_query
+        self.layout_key = layout_key
+        self.return_value = return_value
+        self.pre_tokens = pre_tokens
+        self.next_tokens = next_tokens
+
+    def forward(self, query, key, weights, actual_seq_lengths_query=None,
+                actual_seq_lengths_key=None, block_table=None):
+        return lightning_indexer_triton(
+            query, key, weights, actual_seq_lengths_query=actual_seq_lengths_query,
+            actual_seq_lengths_key=actual_seq_lengths_key, block_table=block_table,
+            layout_query=self.layout_query, layout_key=self.layout_key,
+            sparse_count=self.sparse_count, sparse_mode=self.sparse_mode,
+            pre_tokens=self.pre_tokens, next_tokens=self.next_tokens,
+            return_value=self.return_value)

@@ -30,6 +30,7 @@ extern "C" {
 
 #define DSA_DTYPE_BF16 0
 #define DSA_DTYPE_FP16 1
+#define DSA_DTYPE_FP32 2
 
 /* Library version, (major << 16) | minor. */
 int dsa_version(void);
@@ -160,6 +161,55 @@ int dsa_sfa_bwd_cast(const DsaSfaBwdParams* params, void* stream);
 /* Workspace of dsa_sfa_bwd: compacted key rows and counts, plus bf16/fp16 scratch for P and
  * dS ([num_rows][128][keys padded to 128] each).  Returns -1 for invalid sizes. */
 int64_t dsa_sfa_bwd_workspace_size(int64_t num_rows, int64_t topk, int64_t sparse_block_size);
+
+/*
+ * Lightning indexer: scores + top-k.
+ * Replaces `_lightning_indexer_score_core` / `_lightning_indexer_score_kernel` and
+ * `_stable_topk` (lightning_indexer_triton.py:382-413, :147-280, :339-357).
+ *   query [q_rows][n1][d], key [kv_rows][n2][d] (bf16/fp16, d multiple of 8, <= 256),
+ *   weights [q_rows][n1] (bf16/fp16/fp32, weights_dtype).
+ *   score[r][n2][s2] = sum over the n1/n2 query heads g of group n2 of
+ *                      ReLU(query[r][g] . key[k_row_base[b] + s2][n2]) * weights[r][g]
+ *   for s2 < visible(r) (sparse_mode 3: min(act_k, clamp(act_k - act_q + s1 + 1, 0, s2_cap));
+ *   mode 0: min(act_k, s2_cap); 0 for s1 >= act_q), -inf elsewhere.
+ * Outputs: out_indices [q_rows][n2][sparse_count] int32 ordered by (score desc, index asc),
+ * -1 where the score is -inf; out_values (query dtype, NULL to skip) the matching scores.
+ * Query rows: q_row_base[b] is batch b's first row; a BSND caller passes q_len_dense = S1
+ * (rows s1 >= act_q exist but see nothing); a TND caller passes q_len_dense = 0 (a batch has
+ * act_q rows).  q_len_max = largest row count of a batch.  s2_row = length of a score row
+ * (>= sparse_count).  Workspace: dsa_li_workspace_size() bytes (the fp32 score matrix).
+ */
+typedef struct DsaLiParams {
+  const void* query;
+  const void* key;
+  const void* weights;
+  const int32_t* act_q;
+  const int32_t* act_k;
+  const int32_t* q_row_base;
+  const int32_t* k_row_base;
+  int32_t* out_indices;
+  void* out_values;
+  int* error_flag;
+  void* workspace;
+  int64_t workspace_bytes;
+  int64_t q_rows;
+  int64_t batch;
+  int64_t n1;
+  int64_t n2;
+  int64_t d;
+  int64_t kv_rows;
+  int64_t sparse_count;
+  int64_t s2_row;
+  int64_t s2_cap;
+  int64_t q_len_max;
+  int64_t q_len_dense;
+  int32_t sparse_mode;
+  int32_t dtype;
+  int32_t weights_dtype;
+} DsaLiParams;
+
+int dsa_li_score_topk(const DsaLiParams* params, void* stream);
+int64_t dsa_li_workspace_size(int64_t q_rows, int64_t n2, int64_t s2_row);
 
 #ifdef __cplusplus
 }
