@@ -5,6 +5,8 @@ Drop-in for the operators of 18851871668/dsa_triton_ascend, on CUDA torch tensor
 * :func:`sparse_flash_attention_triton` / :class:`SparseFlashAttentionTriton`
 * :func:`sparse_flash_attention_grad_triton` / :class:`SparseFlashAttentionGradTriton`
 * :func:`lightning_indexer_triton` / :class:`LightningIndexerTriton`
+* :func:`sparse_lightning_indexer_grad_kl_loss_triton` /
+  :class:`SparseLightningIndexerGradKLLossTriton`
 """
 from ._lib import check_device_errors, lib as _load_library  # noqa: F401
 from .sparse_flash_attention import (  # noqa: F401
@@ -12,6 +14,10 @@ from .sparse_flash_attention import (  # noqa: F401
     sparse_flash_attention_triton,
 )
 from .lightning_indexer import LightningIndexerTriton, lightning_indexer_triton  # noqa: F401
+from .sparse_lightning_indexer_grad_kl_loss import (  # noqa: F401
+    SparseLightningIndexerGradKLLossTriton,
+    sparse_lightning_indexer_grad_kl_loss_triton,
+)
 from .sparse_flash_attention_grad import (  # noqa: F401
     SparseFlashAttentionGradTriton,
     sparse_flash_attention_grad_partial,
@@ -25,5 +31,7 @@ __all__ = [
     "SparseFlashAttentionGradTriton",
     "lightning_indexer_triton",
     "LightningIndexerTriton",
+    "sparse_lightning_indexer_grad_kl_loss_triton",
+    "SparseLightningIndexerGradKLLossTriton",
     "check_device_errors",
 ]

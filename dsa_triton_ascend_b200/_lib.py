@@ -73,6 +73,19 @@ class LiParams(ctypes.Structure):
     ]
 
 
+class SliParams(ctypes.Structure):
+    _fields_ = [
+        ("query", _p), ("key", _p), ("query_rope", _p), ("key_rope", _p), ("query_index", _p),
+        ("key_index", _p), ("weights", _p), ("sparse_indices", _p), ("softmax_max", _p),
+        ("softmax_sum", _p), ("act_q", _p), ("act_k", _p), ("d_query_index", _p),
+        ("d_key_index", _p), ("d_weights", _p), ("dki_acc", _p), ("loss", _p),
+        ("error_flag", _p), ("workspace", _p), ("workspace_bytes", _i64),
+        ("batch", _i64), ("s1", _i64), ("s2", _i64), ("n1", _i64), ("d", _i64),
+        ("n_index", _i64), ("d_index", _i64), ("topk", _i64),
+        ("scale", ctypes.c_float), ("dtype", ctypes.c_int32), ("weights_dtype", ctypes.c_int32),
+    ]
+
+
 _lock = threading.Lock()
 _lib = None
 _err_bufs: dict = {}
@@ -104,6 +117,10 @@ def lib() -> ctypes.CDLL:
                 l.dsa_li_score_topk.restype = ctypes.c_int
                 l.dsa_li_workspace_size.argtypes = [_i64, _i64, _i64]
                 l.dsa_li_workspace_size.restype = _i64
+                l.dsa_sli_grad.argtypes = [ctypes.POINTER(SliParams), _p]
+                l.dsa_sli_grad.restype = ctypes.c_int
+                l.dsa_sli_workspace_size.argtypes = [_i64, _i64, _i64]
+                l.dsa_sli_workspace_size.restype = _i64
                 _lib = l
     return _lib
 

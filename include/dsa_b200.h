@@ -211,6 +211,56 @@ typedef struct DsaLiParams {
 int dsa_li_score_topk(const DsaLiParams* params, void* stream);
 int64_t dsa_li_workspace_size(int64_t q_rows, int64_t n2, int64_t s2_row);
 
+/*
+ * Sparse lightning-indexer KL-loss gradient (BSND, sparse_mode 3).
+ * Replaces `_sparse_lightning_indexer_grad_kl_loss_core` and its kernels
+ * (sparse_lightning_indexer_grad_kl_loss_triton.py:355-464, :39-327).
+ *   query [batch*s1][n1][d], query_rope [batch*s1][n1][64], key [batch*s2][d],
+ *   key_rope [batch*s2][64], query_index [batch*s1][n_index][128], key_index [batch*s2][128],
+ *   weights [batch*s1][n_index] (weights_dtype), sparse_indices [batch*s1][topk] int32,
+ *   softmax_max / softmax_sum [batch*s1][n1] fp32, act_q / act_k [batch].
+ * Outputs: d_query_index (query_index dtype), d_weights (weights dtype), loss [1] fp32 (sum
+ * over rows, zeroed by the call), dki_acc [batch*s2][128] fp32 (zeroed by the call) and, if
+ * d_key_index != NULL, its cast to the key_index dtype.  n_index <= 64, n1 <= 128.
+ * Workspace: dsa_sli_workspace_size() bytes (the teacher distribution, fp32).
+ */
+typedef struct DsaSliParams {
+  const void* query;
+  const void* key;
+  const void* query_rope;
+  const void* key_rope;
+  const void* query_index;
+  const void* key_index;
+  const void* weights;
+  const int32_t* sparse_indices;
+  const float* softmax_max;
+  const float* softmax_sum;
+  const int32_t* act_q;
+  const int32_t* act_k;
+  void* d_query_index;
+  void* d_key_index;
+  void* d_weights;
+  float* dki_acc;
+  float* loss;
+  int* error_flag;
+  void* workspace;
+  int64_t workspace_bytes;
+  int64_t batch;
+  int64_t s1;
+  int64_t s2;
+  int64_t n1;
+  int64_t d;
+  int64_t n_index;
+  int64_t d_index;
+  int64_t topk;
+  float scale;
+  int32_t dtype;
+  int32_t weights_dtype;
+} DsaSliParams;
+
+int dsa_sli_grad(const DsaSliParams* params, void* stream);
+int64_t dsa_sli_workspace_size(int64_t batch, int64_t s1, int64_t topk);
+
 #ifdef __cplusplus
 }
 #endif
