@@ -100,15 +100,6 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def shard_rows(pairs_per_row: np.ndarray, world: int, rank: int):
-    """Contiguous row range of `rank` with ~equal valid-pair counts."""
-    cum = np.concatenate([[0], np.cumsum(pairs_per_row)])
-    total = cum[-1]
-    bounds = [int(np.searchsorted(cum, total * r / world, side="left")) for r in range(world + 1)]
-    bounds[0], bounds[-1] = 0, len(pairs_per_row)
-    return bounds[rank], bounds[rank + 1]
-
-
 # ----------------------------------------------------------------------------------------
 # CPU side: the reference algorithm (numpy restatement) on a bounded sample of rows
 # ----------------------------------------------------------------------------------------
@@ -194,6 +185,7 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
     import dsa_triton_ascend_b200 as dsa
+    from dsa_triton_ascend_b200.sharding import shard_act_q, shard_rows
     from dsa_triton_ascend_b200.synthetic import sfa_prefill, valid_pairs_per_row
 
     w = sfa_prefill(device=dev)
@@ -207,10 +199,7 @@ def main():
     si = w["si"][:, r0:r1].contiguous()
     k, kr, scale = w["k"], w["kr"], w["scale"]
     dout = dout_full[:, r0:r1].contiguous()
-    # a row range [r0, r1) of the causal query block is a BSND query of r1-r0 rows whose
-    # actual length is S1 - r0: the kernel's causal window act_k - act_q + s1 + 1 then
-    # equals the window of the original row r0 + s1.
-    aq = [S1 - r0]
+    aq = [shard_act_q(S1, r0)]   # see dsa_triton_ascend_b200/sharding.py
 
     def fwd():
         return dsa.sparse_flash_attention_triton(

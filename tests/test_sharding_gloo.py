@@ -1,0 +1,84 @@
+"""Multi-rank host logic on CPU ranks (gloo, world_size 2): row sharding with the causal
+length trick and the fp32 key-gradient all-reduce reproduce the single-rank result."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from dsa_triton_ascend_b200.sharding import shard_act_q, shard_rows
+
+
+def test_shard_rows_balances_pairs():
+    pairs = np.minimum(np.arange(1, 8193), 2048)
+    for world in (1, 2, 4, 8):
+        bounds = [shard_rows(pairs, world, r) for r in range(world)]
+        assert bounds[0][0] == 0 and bounds[-1][1] == len(pairs)
+        assert all(bounds[i][1] == bounds[i + 1][0] for i in range(world - 1))
+        share = [pairs[a:b].sum() for a, b in bounds]
+        assert max(share) - min(share) <= 2048
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, case, out_q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import inputs as I
+    from oracle import sfa
+    c = I.sfa_case(*case)
+    S1 = c["q"].shape[1]
+    pairs = (c["si"][0, :, 0] >= 0).sum(axis=-1)
+    r0, r1 = shard_rows(pairs, world, rank)
+    aq = [shard_act_q(S1, r0)]
+    sl = slice(r0, r1)
+    out, mx, sm = sfa.sfa_fwd(c["q"][:, sl], c["k"], c["qr"][:, sl], c["kr"], c["si"][:, sl],
+                              c["scale"], act_q=aq, sparse_mode=3)
+    dq, dk, dv, dqr, dkr = sfa.sfa_bwd(c["q"][:, sl], c["k"], c["qr"][:, sl], c["kr"],
+                                       c["si"][:, sl], c["dout"][:, sl], out, mx, sm, c["scale"],
+                                       act_q=aq, sparse_mode=3, dtype="fp32")
+    grads = [torch.from_numpy(np.ascontiguousarray(x)) for x in (dk, dv, dkr)]
+    for g in grads:
+        dist.all_reduce(g)
+    parts = [torch.from_numpy(np.ascontiguousarray(x)) for x in (out, dq)]
+    gathered = [[torch.zeros(0)] * world for _ in parts]
+    for i, p in enumerate(parts):
+        dist.all_gather_object(gathered[i], p)
+    if rank == 0:
+        out_q.put((torch.cat(gathered[0], dim=1).numpy(), torch.cat(gathered[1], dim=1).numpy(),
+                   [g.numpy() for g in grads]))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_two_rank_fwd_bwd_matches_single_rank():
+    case = (1, 12, 64, 4, 128, 16, 1, 3, "fp32", 5)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, case, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out, dq, grads = q.get(timeout=240)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    import inputs as I
+    from oracle import sfa
+    c = I.sfa_case(*case)
+    ro, rm, rs = sfa.sfa_fwd(c["q"], c["k"], c["qr"], c["kr"], c["si"], c["scale"], sparse_mode=3)
+    rdq, rdk, rdv, _, rdkr = sfa.sfa_bwd(c["q"], c["k"], c["qr"], c["kr"], c["si"], c["dout"], ro,
+                                         rm, rs, c["scale"], sparse_mode=3, dtype="fp32")
+    np.testing.assert_allclose(out, ro, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(dq, rdq, rtol=1e-5, atol=1e-6)
+    for g, r in zip(grads, (rdk, rdv, rdkr)):
+        np.testing.assert_allclose(g, r, rtol=1e-4, atol=1e-5)
