@@ -168,6 +168,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="sfa", choices=["sfa", "li", "decode", "sli"],
+                    help="sfa: config 4 forward+backward (the headline); li: config 2 indexer; "
+                         "decode: config 3 paged forward; sli: config 5 indexer KL-loss grad")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="profiling aid: time only the last ROWS query rows of config 4 "
+                         "(each sees the full 2048 keys); 0 = the whole workload")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -176,6 +182,8 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.workload != "sfa":
+        return run_other(args, rank, world, local)
 
     import torch.distributed as dist
     from datetime import timedelta
@@ -191,7 +199,11 @@ def main():
     w = sfa_prefill(device=dev)
     dout_full = w["dout"]
     pairs = valid_pairs_per_row(w["si"]).cpu().numpy()
+    if args.rows:
+        pairs[: S1 - args.rows] = 0
     r0, r1 = shard_rows(pairs, world, rank)
+    if args.rows:
+        r0 = max(r0, S1 - args.rows)
     my_pairs = int(pairs[r0:r1].sum())
     total_pairs = int(pairs.sum())
     q = w["q"][:, r0:r1].contiguous()
@@ -366,6 +378,94 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def _timed(fn, steps, warmup, stream):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    for a, b in ev:
+        a.record(stream)
+        fn()
+        b.record(stream)
+    torch.cuda.synchronize()
+    return float(np.mean([a.elapsed_time(b) for a, b in ev]))
+
+
+def run_other(args, rank, world, local):
+    """Secondary workloads (configs 2, 3, 5): one GPU, device-timed, one JSON line each.
+
+    With N GPUs every rank runs its own replica of the workload (weak scaling)."""
+    import math as _m
+    import dsa_triton_ascend_b200 as dsa
+    from dsa_triton_ascend_b200.synthetic import causal_topk_ids
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    rn = lambda *sh: torch.randn(*sh, generator=g, device=dev).to(torch.bfloat16)
+    hbm_peak, tf_peak, peak_kind = load_peaks()
+    if args.workload == "li":
+        B, S, N1_, Dh, K = 2, 4096, 64, 128, 2048
+        q, k = rn(B, S, N1_, Dh), rn(B, S, 1, Dh)
+        w = torch.randn(B, S, N1_, generator=g, device=dev) / _m.sqrt(N1_)
+        fn = lambda: dsa.lightning_indexer_triton(q, k, w, sparse_count=K, sparse_mode=3,
+                                                  return_value=True)
+        pairs = B * S * (S + 1) // 2
+        flops, nbytes = pairs * N1_ * 2 * Dh, q.numel() * 2 + k.numel() * 2 + w.numel() * 4 + 2 * B * S * K * 4
+        metric, unit, wl = "LI score+top-k TFLOP/s", "TFLOP/s", "BASELINE config 2 (B=2, S1=S2=4096, N1=64, D=128, top-2048, mode 3)"
+    elif args.workload == "decode":
+        B, N1_, page, nblk, maxb, K = 32, 128, 128, 16384, 512, 2048
+        lens = torch.randint(8192, 65537, (B,), generator=g, device=dev)
+        cache = rn(nblk, page, 1, D)
+        cache_r = rn(nblk, page, 1, DR)
+        bt = torch.randperm(nblk, generator=g, device=dev)[: B * maxb].reshape(B, maxb).int()
+        q, qr = rn(B, 1, N1_, D), rn(B, 1, N1_, DR)
+        u = torch.rand(B, 65536, generator=g, device=dev)
+        u = torch.where(torch.arange(65536, device=dev)[None] < lens[:, None], u, -1.0)
+        si = torch.sort(torch.topk(u, K, dim=1).indices, dim=1).values.int().reshape(B, 1, 1, K)
+        lens_l = lens.tolist()
+        fn = lambda: dsa.sparse_flash_attention_triton(
+            q, cache, cache, si, 1 / _m.sqrt(576), block_table=bt, actual_seq_lengths_kv=lens_l,
+            query_rope=qr, key_rope=cache_r, layout_kv="PA_BSND", sparse_mode=0,
+            return_softmax_lse=True, block_size=page)
+        pairs = B * K
+        flops, nbytes = pairs * FWD_FLOP_PER_PAIR, pairs * GATHER_BYTES_PER_PAIR
+        metric, unit, wl = "SFA decode TFLOP/s", "TFLOP/s", "BASELINE config 3 (PA_BSND, B=32, S1=1, N1=128, top-2048, 16384-block pool)"
+    else:
+        S, N1_, Ni, K = 8192, 128, 64, 2048
+        q, qr, k, kr = rn(1, S, N1_, D), rn(1, S, N1_, DR), rn(1, S, 1, D), rn(1, S, 1, DR)
+        qi, ki = rn(1, S, Ni, 128), rn(1, S, 1, 128)
+        w = torch.randn(1, S, Ni, generator=g, device=dev) / 8
+        si = causal_topk_ids(S, S, K, g, dev).reshape(1, S, 1, K)
+        sc = 1 / _m.sqrt(576)
+        _, mx, sm = dsa.sparse_flash_attention_triton(q, k, k, si, sc, query_rope=qr, key_rope=kr,
+                                                      sparse_mode=3, return_softmax_lse=True)
+        fn = lambda: dsa.sparse_lightning_indexer_grad_kl_loss_triton(
+            q, k, qi, ki, w, si, mx, sm, query_rope=qr, key_rope=kr, scale_value=sc)
+        pairs = int((si >= 0).sum().item())
+        flops = pairs * 2 * (64 * 128 * 3 + 128 * 576)
+        nbytes = pairs * (GATHER_BYTES_PER_PAIR + 256)
+        metric, unit, wl = "SLI KL-grad TFLOP/s", "TFLOP/s", "BASELINE config 5 (S1=S2=8192, N1=128, Nidx1=64, top-2048)"
+    ms = _timed(fn, args.steps, max(args.warmup, 3), stream)
+    dsa.check_device_errors(dev)
+    t_b, t_f = nbytes / (hbm_peak * 1e9), flops / (tf_peak * 1e12)
+    bound = "hbm" if t_b >= t_f else "tensor"
+    line = {"metric": metric, "value": flops / (ms * 1e-3) / 1e12 * world, "unit": unit,
+            "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "config": {"workload": wl},
+            "roofline": {"bound": bound, "achieved": (nbytes / (ms * 1e-3) / 1e9) if bound == "hbm"
+                         else flops / (ms * 1e-3) / 1e12,
+                         "peak": hbm_peak if bound == "hbm" else tf_peak,
+                         "unit": "GB/s" if bound == "hbm" else "TFLOP/s",
+                         "frac": max(t_b, t_f) / (ms * 1e-3), "traffic": None,
+                         "peak_source": peak_kind}}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":
