@@ -18,6 +18,8 @@ DSA_OK = 0
 DSA_ERR_INVALID_ARG = 1
 DSA_ERR_CUDA = 2
 DSA_ERR_TMA_DESCRIPTOR = 3
+DSA_ERR_TOO_LARGE = 4
+SFA_FWD_NOALLOC_SCRATCH_BYTES = 16 << 20   # DSA_SFA_FWD_NOALLOC_SCRATCH_BYTES
 DSA_DTYPE_BF16 = 0
 DSA_DTYPE_FP16 = 1
 DSA_DTYPE_FP32 = 2
@@ -26,6 +28,7 @@ _ERR_TEXT = {
     DSA_ERR_INVALID_ARG: "invalid argument",
     DSA_ERR_CUDA: "CUDA launch error",
     DSA_ERR_TMA_DESCRIPTOR: "TMA descriptor rejected (misaligned or oversized tensor)",
+    DSA_ERR_TOO_LARGE: "request exceeds the library's fixed scratch array",
 }
 
 _p = ctypes.c_void_p
@@ -107,6 +110,8 @@ def lib() -> ctypes.CDLL:
                 l.dsa_sfa_fwd.restype = ctypes.c_int
                 l.dsa_sfa_fwd_workspace_size.argtypes = [_i64, _i64, _i64]
                 l.dsa_sfa_fwd_workspace_size.restype = _i64
+                l.dsa_sfa_fwd_noalloc.argtypes = [ctypes.POINTER(SfaFwdParams), _p]
+                l.dsa_sfa_fwd_noalloc.restype = ctypes.c_int
                 l.dsa_sfa_bwd.argtypes = [ctypes.POINTER(SfaBwdParams), _p]
                 l.dsa_sfa_bwd.restype = ctypes.c_int
                 l.dsa_sfa_bwd_cast.argtypes = [ctypes.POINTER(SfaBwdParams), _p]

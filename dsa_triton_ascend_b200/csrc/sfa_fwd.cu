@@ -24,6 +24,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "dsa_b200.h"
 #include "sm100.cuh"
 #include "sfa_common.cuh"
@@ -522,4 +524,62 @@ extern "C" int dsa_sfa_fwd(const DsaSfaFwdParams* p, void* stream_) {
 extern "C" int64_t dsa_sfa_fwd_workspace_size(int64_t num_rows, int64_t topk, int64_t sparse_block_size) {
   if (num_rows < 0 || topk < 0 || sparse_block_size < 1) return -1;
   return 4 * (num_rows * topk * sparse_block_size + num_rows);
+}
+
+// ---------------------------------------------------------------------------------------
+// dsa_sfa_fwd_noalloc: the forward for callers that cannot allocate device memory when
+// they run attention (a serving runtime whose KV-cache pool took all free HBM at
+// start-up, or a plain C/C++ host with no allocator of its own that may not call
+// cudaMalloc on its hot path).  The only device memory dsa_sfa_fwd needs besides the
+// caller's inputs and outputs is the compaction workspace; here that workspace is the
+// file-scope array below, so the call allocates nothing.
+//
+// The array lives in every GPU that loads this module, for as long as the process runs.
+// Its name is only a host-side handle: the device address is looked up per device with
+// cudaGetSymbolAddress, once, by the first call on that device (with the device
+// current), and cached.  That first call should therefore come before any stream
+// capture.  All calls on a device share the array and it keeps the last call's
+// contents; no entry has to start at zero, because sfa_prep_kernel writes the count of
+// every query row and the key rows below each count before sfa_fwd_kernel reads them.
+// Calls that overlap on the GPU (different streams, no ordering) race on the array.
+
+static __device__ __align__(256) int32_t g_sfa_fwd_noalloc_scratch[DSA_SFA_FWD_NOALLOC_SCRATCH_BYTES / 4];
+
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kNoAllocMaxDevices] = {};
+
+// Device address of this device's scratch array (looked up on first use).
+int noalloc_scratch_address(void** addr) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return DSA_ERR_CUDA;
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return DSA_ERR_INVALID_ARG;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* a = nullptr;
+    if (cudaGetSymbolAddress(&a, g_sfa_fwd_noalloc_scratch) != cudaSuccess || !a)
+      return DSA_ERR_CUDA;
+    g_noalloc_addr[dev] = a;
+  }
+  *addr = g_noalloc_addr[dev];
+  return DSA_OK;
+}
+
+}  // namespace
+
+extern "C" int dsa_sfa_fwd_noalloc(const DsaSfaFwdParams* p, void* stream) {
+  if (!p) return DSA_ERR_INVALID_ARG;
+  if (p->num_rows <= 0) return DSA_OK;
+  const int64_t need = dsa_sfa_fwd_workspace_size(p->num_rows, p->topk, p->sparse_block_size);
+  if (need < 0) return DSA_ERR_INVALID_ARG;
+  if (need > DSA_SFA_FWD_NOALLOC_SCRATCH_BYTES) return DSA_ERR_TOO_LARGE;
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch_address(&scratch);
+  if (rc != DSA_OK) return rc;
+  DsaSfaFwdParams q = *p;
+  q.workspace = scratch;
+  q.workspace_bytes = DSA_SFA_FWD_NOALLOC_SCRATCH_BYTES;
+  return dsa_sfa_fwd(&q, stream);
 }

@@ -27,6 +27,7 @@ extern "C" {
 #define DSA_ERR_INVALID_ARG 1     /* bad size / null pointer / unsupported config */
 #define DSA_ERR_CUDA 2            /* launch or attribute error from the CUDA runtime */
 #define DSA_ERR_TMA_DESCRIPTOR 3  /* driver rejected a TMA tensor map (alignment) */
+#define DSA_ERR_TOO_LARGE 4       /* request exceeds a fixed in-library scratch array */
 
 #define DSA_DTYPE_BF16 0
 #define DSA_DTYPE_FP16 1
@@ -97,6 +98,31 @@ int dsa_sfa_fwd(const DsaSfaFwdParams* params, void* stream);
  * [num_rows][topk * sparse_block_size]) and their counts (int32 [num_rows]).
  * Returns -1 for invalid sizes. */
 int64_t dsa_sfa_fwd_workspace_size(int64_t num_rows, int64_t topk, int64_t sparse_block_size);
+
+/*
+ * Sparse flash attention forward that allocates nothing.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory when they run
+ * attention -- a serving runtime that has handed all free HBM to its KV-cache pool
+ * at start-up, or a host program that owns no allocator of its own (no torch, no
+ * pool) and may not call cudaMalloc on its hot path.
+ *
+ * Same parameters and results as dsa_sfa_fwd, except that `workspace` and
+ * `workspace_bytes` are ignored: the compaction workspace is a fixed array of
+ * DSA_SFA_FWD_NOALLOC_SCRATCH_BYTES inside the library, which every GPU that loads
+ * the library's forward module holds until the process exits.
+ *   - Calls whose dsa_sfa_fwd_workspace_size(num_rows, topk, sparse_block_size)
+ *     exceeds DSA_SFA_FWD_NOALLOC_SCRATCH_BYTES return DSA_ERR_TOO_LARGE and launch
+ *     nothing (split the query rows into several calls, or use dsa_sfa_fwd).
+ *   - The first call on a device looks up that device's copy of the array (with the
+ *     device current); make that first call before any stream capture begins.
+ *   - Every call on a device shares the one array and it keeps the last call's
+ *     contents.  Nothing in it has to start at zero (each call writes every entry it
+ *     later reads), but calls that overlap on the GPU -- on different streams without
+ *     ordering between them -- race on it and give wrong results.
+ * Calls no cudaMalloc, cudaFree or other allocating routine.
+ */
+#define DSA_SFA_FWD_NOALLOC_SCRATCH_BYTES (16LL << 20)
+int dsa_sfa_fwd_noalloc(const DsaSfaFwdParams* params, void* stream);
 
 /*
  * Sparse flash attention backward (MLA-absorb).
