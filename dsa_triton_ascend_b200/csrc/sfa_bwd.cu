@@ -15,9 +15,10 @@
 //              tcgen05 (2-SM, heads split 64/64), then P and dS -> bf16 scratch.
 //   K2 dq    : CTA pair per query row: dQ = dS K (nope dims split across the pair like
 //              the forward's P V; rope dims on a padded N=128 MMA).
-//   K3 dkv   : one CTA per (query row, 128-key tile, part): dK = dS^T Q, dV = P^T dO,
-//              dKr = dS^T Qr on tcgen05 (M = 128 keys, K = 128 heads), drained into
-//              fp32 accumulators with coalesced vector reductions (red.global.add.v4.f32),
+//   K3 dkv   : one CTA per (query row, column part), looping over the row's 128-key
+//              tiles: dK = dS^T Q, dV = P^T dO, dKr = dS^T Qr on tcgen05 (M = 128 keys,
+//              K = 128 heads), double-buffered in TMEM and drained into fp32
+//              accumulators with coalesced vector reductions (red.global.add.v4.f32),
 //              the scatter-add of the reference (:289-300).
 //   K4 cast  : fp32 accumulators -> key dtype (separate entry point so a multi-GPU
 //              caller can all-reduce the fp32 accumulators first).
@@ -548,17 +549,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
 // =====================================================================================
 // K3: dK = dS^T Q, dV = P^T dO, dKr = dS^T Qr  (scatter-add into fp32)
 // =====================================================================================
-// part 0: dK nope (B = Q nope, N = D), 1: dV (B = dO, N = D), 2: dK rope (B = Qr, N = 64)
+// One CTA per (query row, part); it walks the row's 128-key tiles. Parts split the output
+// columns so that a CTA's B operand (the row's Q / dO / Qr columns, K = 128 heads) stays
+// resident: for D = 512, parts 0-1 are dK columns [0,256) and [256,512) (A = dS, B = Q),
+// parts 2-3 the same columns of dV (A = P, B = dO) and part 4 is dKr (A = dS, B = Qr).
+// The parts of one row are adjacent in the grid, so they run together and their dS / P
+// tile reads hit L2. Per tile: warp 0 (one lane) streams the A tiles through a 2-stage TMA
+// ring and issues M=128 (keys) x N=W MMAs into one of two TMEM buffers; 16 drain warps
+// (4 per TMEM lane quadrant, each owning W/4 columns) move the finished buffer through a
+// shared-memory transpose into red.global.add.v4.f32 while the next tile's MMAs run. The
+// reductions are the bound (4352 bytes per valid pair at D=512), and one SM needs about 16
+// warps in flight to keep its share of the L2 reduction rate.
 template <int D>
 struct Cfg3 {
-  static constexpr int kABytes = 2 * kHeadsPad * 128;        // 128 keys x 128 heads, MN-major
-  static constexpr int kBChunk = kHeadsPad * 128;            // 64 dims x 128 heads
-  static constexpr int kNope = D / 64;
+  static constexpr int kW = D < 256 ? D : 256;           // output columns per part
+  static constexpr int kDParts = D / kW;
+  static constexpr int kParts = 2 * kDParts + 1;
+  static constexpr int kATile = kHeadsPad * kKeyTile3 * 2; // 128 heads x 128 keys, MN-major
+  static constexpr int kBChunk = kHeadsPad * 128;          // 64 columns x 128 heads
   static constexpr int kOffA = 0;
-  static constexpr int kOffB = kABytes;
-  static constexpr int kOffStage = kOffB + kNope * kBChunk;
-  static constexpr int kStageBytes = 4 * 32 * 33 * 4;
-  static constexpr int kOffBars = kOffStage + kStageBytes;
+  static constexpr int kOffB = 2 * kATile;
+  static constexpr int kOffStage = kOffB + (kW / 64) * kBChunk;
+  static constexpr int kStageWarp = 32 * 33 * 4;
+  static constexpr int kOffBars = kOffStage + 16 * kStageWarp;
 };
 
 struct Maps3 {
@@ -566,24 +579,67 @@ struct Maps3 {
 };
 
 struct __align__(16) Bars3 {
-  uint64_t full, done;
+  uint64_t b_full;
+  uint64_t a_full[2], a_empty[2];
+  uint64_t t_full[2], t_empty[2];
   uint32_t tmem_slot;
 };
 
-constexpr int kThreads3 = 160;   // 0-3: drain (TMEM quadrants 0-3), 4: loads + MMA
+constexpr int kThreads3 = 17 * 32;   // warp 0: TMA + MMA; warps 1-16: drain
+
+// One drain warp's share of a finished K3 tile: its 32 keys (TMEM lanes) x CW columns.
+// The columns are read into registers first and the TMEM buffer released at once, then
+// staged through shared memory (row stride 33 floats, conflict-free both ways) so that each
+// reduction instruction covers whole 128-byte (CW >= 32) or 64-byte (CW = 16) row pieces.
+template <int CW>
+__device__ __forceinline__ void dkv_drain(uint32_t taddr, uint32_t t_empty, float* stage,
+                                          float* gbase, int ld, int my_row, int lane) {
+  uint32_t r[CW];
+  if constexpr (CW >= 32) {
+    tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+    if constexpr (CW == 64) tmem_ld32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+  } else {
+    tmem_ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
+  }
+  tmem_ld_wait();
+  tc_fence_before();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(t_empty);
+  constexpr int kN = CW < 32 ? CW : 32;   // columns per staging pass
+  constexpr int kLpk = kN / 4;            // lanes per key in one instruction
+  constexpr int kKpi = 32 / kLpk;         // keys per instruction
+#pragma unroll
+  for (int c0 = 0; c0 < CW; c0 += kN) {
+#pragma unroll
+    for (int i = 0; i < kN; ++i) stage[lane * 33 + i] = __uint_as_float(r[c0 + i]);
+    __syncwarp();
+#pragma unroll
+    for (int it = 0; it < 32 / kKpi; ++it) {
+      const int kr = kKpi * it + lane / kLpk, cc = 4 * (lane % kLpk);
+      const int dst_row = __shfl_sync(0xffffffffu, my_row, kr);
+      if (dst_row >= 0) {
+        const float* sp = stage + kr * 33 + cc;
+        float* gp = gbase + (size_t)dst_row * ld + c0 + cc;
+        asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(gp), "f"(sp[0]),
+                     "f"(sp[1]), "f"(sp[2]), "f"(sp[3])
+                     : "memory");
+      }
+    }
+    __syncwarp();
+  }
+}
 
 template <int D, typename T>
 __global__ void __launch_bounds__(kThreads3, 1)
-    sfa_bwd_dkv_kernel(const __grid_constant__ Maps3 maps, const Args a, int tiles_per_row) {
+    sfa_bwd_dkv_kernel(const __grid_constant__ Maps3 maps, const Args a) {
   using C = Cfg3<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   Bars3& bars = *reinterpret_cast<Bars3*>(smem_raw + C::kOffBars);
   const uint32_t sbase = smem_u32(smem_raw);
   const uint32_t sA = sbase + C::kOffA, sB = sbase + C::kOffB;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int part = blockIdx.y;
-  const int row = blockIdx.x / tiles_per_row;
-  const int kt = blockIdx.x % tiles_per_row;
+  const int row = blockIdx.x / C::kParts;
+  const int part = blockIdx.x % C::kParts;
   if (sbase & 1023u) {
     if (threadIdx.x == 0) report_error(a.err, kErrMisaligned);
     return;
@@ -591,16 +647,27 @@ __global__ void __launch_bounds__(kThreads3, 1)
   const RowInfo ri = row_info(a, row);
   const bool abort = a.err != nullptr && *reinterpret_cast<volatile int*>(a.err) != 0;
   const int nvalid = (ri.active && !abort) ? __ldg(a.ws_count + row) : 0;
-  if (kt * kKeyTile3 >= nvalid) return;   // uniform across the CTA
-  const int ncols = part == 2 ? 64 : D;
-  const int nb_chunks = ncols / 64;
+  const int ntiles = (nvalid + kKeyTile3 - 1) / kKeyTile3;
+  if (ntiles == 0) return;   // uniform across the CTA
+
+  const bool rope = part == 2 * C::kDParts;
+  const bool is_dv = !rope && part >= C::kDParts;
+  const int W = rope ? 64 : C::kW;                         // columns of this part
+  const int col0 = rope ? 0 : (part % C::kDParts) * C::kW;  // first output column
+  float* acc = rope ? a.dkr_acc : is_dv ? a.dv_acc : a.dk_acc;
+  const int ld = rope ? 64 : D;
 
   if (threadIdx.x == 0) {
-    mbar_init(smem_u32(&bars.full), 1);
-    mbar_init(smem_u32(&bars.done), 1);
+    mbar_init(smem_u32(&bars.b_full), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&bars.a_full[s]), 1);
+      mbar_init(smem_u32(&bars.a_empty[s]), 1);
+      mbar_init(smem_u32(&bars.t_full[s]), 1);
+      mbar_init(smem_u32(&bars.t_empty[s]), 16);
+    }
     fence_mbarrier_init();
   }
-  if (warp == 4) {
+  if (warp == 0) {
     tmem_alloc<1>(smem_u32(&bars.tmem_slot), 512);
     tmem_relinquish<1>();
   }
@@ -610,73 +677,91 @@ __global__ void __launch_bounds__(kThreads3, 1)
   const uint32_t tmem = bars.tmem_slot;
   bool failed = false;
 
-  if (warp == 4) {
+  if (warp == 0) {
     if (lane == 0) {
-      const uint32_t fb = smem_u32(&bars.full);
-      mbar_arrive_expect_tx(fb, C::kABytes + nb_chunks * C::kBChunk);
-      const CUtensorMap* am = part == 1 ? &maps.pp : &maps.ds;
+      const CUtensorMap* am = is_dv ? &maps.pp : &maps.ds;
+      const CUtensorMap* bm = rope ? &maps.qr : is_dv ? &maps.dout : &maps.q;
       const int hrow0 = row * kHeadsPad;
-      for (int c = 0; c < 2; ++c)   // keys [64c, 64c+64) of the tile, all 128 heads
-        tma_load_2d(sA + c * kHeadsPad * 128, am, fb, kt * kKeyTile3 + 64 * c, hrow0);
-      const CUtensorMap* bm = part == 0 ? &maps.q : part == 1 ? &maps.dout : &maps.qr;
-      for (int c = 0; c < nb_chunks; ++c)
-        tma_load_2d(sB + c * C::kBChunk, bm, fb, 64 * c, row * a.N1);
-      if (mbar_wait(fb, 0, a.err, &failed)) {
+      auto load_a = [&](int t, int s) {
+        const uint32_t fb = smem_u32(&bars.a_full[s]);
+        mbar_arrive_expect_tx(fb, C::kATile);
+        for (int c = 0; c < 2; ++c)   // keys [64c, 64c+64) of the tile, all 128 heads
+          tma_load_2d(sA + s * C::kATile + c * kHeadsPad * 128, am, fb,
+                      t * kKeyTile3 + 64 * c, hrow0);
+      };
+      {
+        const uint32_t fb = smem_u32(&bars.b_full);
+        mbar_arrive_expect_tx(fb, (W / 64) * C::kBChunk);
+        for (int c = 0; c < W / 64; ++c)
+          tma_load_2d(sB + c * C::kBChunk, bm, fb, col0 + 64 * c, row * a.N1);
+      }
+      int loaded = 0, consumed = 0, issued = 0;
+      for (; loaded < 2 && loaded < ntiles; ++loaded) load_a(loaded, loaded);
+      const bool bf16 = ElemTraits<T>::kIsBf16;
+      const uint32_t id = idesc_f16(128, W, bf16, true, true);
+      const uint64_t db = smem_desc_sw128(sB, C::kBChunk, 1024);
+      bool b_ready = mbar_wait(smem_u32(&bars.b_full), 0, a.err, &failed);
+      for (int t = 0; t < ntiles && b_ready; ++t) {
+        const int s = t & 1;
+        const uint32_t ph = (uint32_t)(t >> 1) & 1u;
+        if (!mbar_wait(smem_u32(&bars.a_full[s]), ph, a.err, &failed)) break;
+        ++consumed;
+        if (!mbar_wait(smem_u32(&bars.t_empty[s]), ph ^ 1u, a.err, &failed)) break;
         tc_fence_after();
-        const bool bf16 = ElemTraits<T>::kIsBf16;
-        const int n = ncols < 256 ? ncols : 256;
-        const uint32_t id = idesc_f16(128, n, bf16, true, true);
-        const uint64_t da = smem_desc_sw128(sA, kHeadsPad * 128, 1024);
-        const uint64_t db = smem_desc_sw128(sB, C::kBChunk, 1024);
-        for (int j = 0; j < ncols / n; ++j)
-          for (int k = 0; k < kHeadsPad / 16; ++k)
-            umma_f16<1>(tmem + j * n, da + (uint64_t)((k * 2048) >> 4),
-                        db + (uint64_t)((j * (n / 64) * C::kBChunk + k * 2048) >> 4), id, k != 0);
-        umma_commit(smem_u32(&bars.done));
+        const uint64_t da = smem_desc_sw128(sA + s * C::kATile, kHeadsPad * 128, 1024);
+        for (int k = 0; k < kHeadsPad / 16; ++k)
+          umma_f16<1>(tmem + s * 256, da + (uint64_t)((k * 2048) >> 4),
+                      db + (uint64_t)((k * 2048) >> 4), id, k != 0);
+        umma_commit(smem_u32(&bars.t_full[s]));
+        umma_commit(smem_u32(&bars.a_empty[s]));
+        ++issued;
+        if (t + 2 < ntiles) {
+          if (!mbar_wait(smem_u32(&bars.a_empty[s]), ph, a.err, &failed)) break;
+          load_a(t + 2, s);
+          ++loaded;
+        }
+      }
+      // on a failure, let the copies and MMAs already in flight land before the exit
+      if (failed) {
+        bool f2 = false;
+        for (int t = consumed; t < loaded; ++t)
+          mbar_wait(smem_u32(&bars.a_full[t & 1]), (uint32_t)(t >> 1) & 1u, a.err, &f2);
+        if (issued > 0)
+          mbar_wait(smem_u32(&bars.t_full[(issued - 1) & 1]), (uint32_t)((issued - 1) >> 1) & 1u,
+                    a.err, &f2);
+        if (!b_ready) mbar_wait(smem_u32(&bars.b_full), 0, a.err, &f2);
       }
     }
     __syncwarp();
   } else {
-    // ---- drain: TMEM row = key; coalesced vector reductions into the fp32 accumulator ----
-    float* acc = part == 0 ? a.dk_acc : part == 1 ? a.dv_acc : a.dkr_acc;
-    const int ld = ncols;
-    float* stage = reinterpret_cast<float*>(smem_raw + C::kOffStage) + warp * 32 * 33;
-    const int key0 = kt * kKeyTile3 + 32 * warp;
+    // ---- drain: TMEM row = key; vector reductions into the fp32 accumulator ----
+    const int q = warp & 3;                  // TMEM lane quadrant this warp may access
+    const int cg = (warp - 1) >> 2;          // column group 0..3
+    const int cw = W / 4;                    // 64 (W = 256), 32 (W = 128) or 16 (rope)
+    float* stage = reinterpret_cast<float*>(smem_raw + C::kOffStage) + (warp - 1) * 32 * 33;
     const int32_t* rows = a.ws_rows + (size_t)row * a.topk * a.block;
-    // row of the key matrix for each of this warp's 32 keys (or -1)
-    const int my_key = key0 + lane;
-    const int my_row = my_key < nvalid ? __ldg(rows + my_key) : -1;
-    mbar_wait(smem_u32(&bars.done), 0, a.err, &failed);
-    const bool wfail = __any_sync(0xffffffffu, failed);
-    tc_fence_after();
-    if (!wfail) {
-      for (int c0 = 0; c0 < ncols; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + c0, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) stage[lane * 33 + i] = __uint_as_float(r[i]);
-        __syncwarp();
-        // 4 keys x 128 bytes per instruction: lane -> (key 4*it + lane/8, cols 4*(lane%8))
-#pragma unroll
-        for (int it = 0; it < 8; ++it) {
-          const int kr = 4 * it + (lane >> 3), cc = 4 * (lane & 7);
-          const int dst_row = __shfl_sync(0xffffffffu, my_row, kr);
-          if (dst_row >= 0) {
-            const float* sp = stage + kr * 33 + cc;
-            float* gp = acc + (size_t)dst_row * ld + c0 + cc;
-            asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(gp), "f"(sp[0]),
-                         "f"(sp[1]), "f"(sp[2]), "f"(sp[3])
-                         : "memory");
-          }
-        }
-        __syncwarp();
-      }
+    for (int t = 0; t < ntiles; ++t) {
+      const int s = t & 1;
+      const uint32_t ph = (uint32_t)(t >> 1) & 1u;
+      const int my_key = t * kKeyTile3 + 32 * q + lane;
+      const int my_row = my_key < nvalid ? __ldg(rows + my_key) : -1;
+      mbar_wait(smem_u32(&bars.t_full[s]), ph, a.err, &failed);
+      if (__any_sync(0xffffffffu, failed)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + s * 256 + cg * cw;
+      float* gbase = acc + col0 + cg * cw;
+      const uint32_t t_empty = smem_u32(&bars.t_empty[s]);
+      if (cw == 64)
+        dkv_drain<64>(taddr, t_empty, stage, gbase, ld, my_row, lane);
+      else if (cw == 32)
+        dkv_drain<32>(taddr, t_empty, stage, gbase, ld, my_row, lane);
+      else
+        dkv_drain<16>(taddr, t_empty, stage, gbase, ld, my_row, lane);
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) tmem_dealloc<1>(tmem, 512);
+  if (warp == 0) tmem_dealloc<1>(tmem, 512);
 }
 
 // =====================================================================================
@@ -804,8 +889,7 @@ int launch(const DsaSfaBwdParams* p, cudaStream_t stream) {
     const int smem = Cfg3<D>::kOffBars + (int)sizeof(Bars3);
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return DSA_ERR_CUDA;
-    const int tiles = (int)(kp / kKeyTile3);
-    k<<<dim3((unsigned)(p->num_rows * tiles), 3), dim3(kThreads3), smem, stream>>>(m3, a, tiles);
+    k<<<dim3((unsigned)(p->num_rows * Cfg3<D>::kParts)), dim3(kThreads3), smem, stream>>>(m3, a);
   }
   if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
   if (p->defer_cast) return DSA_OK;
