@@ -204,6 +204,18 @@ __device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from this CTA's
+// shared memory to shared memory of a CTA of the cluster (`dst_cluster` from mapa_shared,
+// or an own address); completion is counted in bytes on `bar_cluster`, an mbarrier in the
+// destination CTA. Not a multicast: one destination.
+__device__ __forceinline__ void bulk_copy_s2c(uint32_t dst_cluster, uint32_t src, uint32_t bytes,
+                                              uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(dst_cluster), "r"(src), "r"(bytes), "r"(bar_cluster)
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_gather4_pair(uint32_t dst, const CUtensorMap* map,
                                                  uint32_t leader_bar, int32_t x, int32_t y0,
                                                  int32_t y1, int32_t y2, int32_t y3) {
