@@ -93,17 +93,20 @@ struct Cfg1 {
 };
 
 struct Maps1 {
-  CUtensorMap q, qr, dout;
+  CUtensorMap q, qr, dout, k, kr;
 };
 
+// The key ring is kept per 64-dim chunk: xf/xe[s][c] track chunk c of tile stage s, so a
+// chunk is refilled with the next-but-one tile's chunk as soon as the S and dP MMAs that
+// read it have completed, not when the whole tile has.
 struct __align__(16) Bars1 {
   uint64_t q_full;
-  uint64_t x_full[2], x_empty[2], s_full[2], s_free[2];
+  uint64_t xf[2][9], xe[2][9], s_full[2], s_free[2];
   uint32_t tmem_slot;
   float red[4][32];
 };
 
-constexpr int kThreads1 = 320;   // 0: Q/dO TMA, 1: MMA, 2-5: elementwise, 6-9: key loaders
+constexpr int kThreads1 = 320;   // 0: Q/dO TMA, 1: MMA, 2-5: elementwise, 6-9: key gathers
 
 template <int D, typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads1, 1)
@@ -130,8 +133,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads1, 1)
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(&bars.q_full), 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(smem_u32(&bars.x_full[s]), 2 * 128);
-      mbar_init(smem_u32(&bars.x_empty[s]), 1);
+      for (int c = 0; c < C::kChunks; ++c) {
+        mbar_init(smem_u32(&bars.xf[s][c]), 1);
+        mbar_init(smem_u32(&bars.xe[s][c]), 1);
+      }
       mbar_init(smem_u32(&bars.s_full[s]), 1);
       mbar_init(smem_u32(&bars.s_free[s]), 2);
     }
@@ -165,47 +170,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads1, 1)
       }
     }
   } else if (warp >= 6) {
-    // ---- own 32 keys of each tile, all dims (cp.async), as in the forward ----
-    const int i = threadIdx.x - 6 * 32;
-    const int kk = i >> 2, q4 = i & 3;
-    const char* kbase = static_cast<const char*>(a.key);
-    const char* rbase = static_cast<const char*>(a.key_rope);
+    // ---- own 32 keys of each tile, all dims: TMA gather4 into this CTA's chunk ring,
+    // completing on the leader's barrier (2-SM form), so no thread waits for data ----
+    // warp w handles chunks c with c % 4 == w - 6; lanes 0-7 issue the chunk's 8 gathers
+    // (4 keys each).
+    const int wq = warp - 6;
     const int filler = nvalid > 0 ? __ldg(rows) : 0;
-    auto fetch = [&](int t) {
-      int j = kTile * t + kOwn * (int)cta + kk;
-      return j < nvalid ? __ldg(rows + j) : filler;
-    };
-    const uint32_t lead0 = mapa_shared(smem_u32(&bars.x_full[0]), 0);
-    const uint32_t lead1 = mapa_shared(smem_u32(&bars.x_full[1]), 0);
-    auto publish = [&](int t) {
-      fence_proxy_async_smem();
-      mbar_arrive_cluster((t & 1) ? lead1 : lead0);
-    };
-    int nxt = ntiles > 0 ? fetch(0) : 0;
     for (int t = 0; t < ntiles && !failed; ++t) {
       const int s = t & 1;
-      const int r = nxt;
-      if (t + 1 < ntiles) nxt = fetch(t + 1);
-      mbar_wait(smem_u32(&bars.x_empty[s]), ((t >> 1) & 1) ^ 1, a.err, &failed);
-      if (failed) break;
-      const char* krow = kbase + (size_t)r * (D * 2);
-      const char* rrow = rbase + (size_t)r * 128;
-      const uint32_t xdst = sX + s * C::kXBytes + kk * 128;
+      const uint32_t ph = (uint32_t)(t >> 1) & 1u;
+      const int j = kTile * t + kOwn * (int)cta + lane;
+      const int my_row = j < nvalid ? __ldg(rows + j) : filler;
+      int r4[4];
 #pragma unroll
-      for (int j = 0; j < 2 * C::kChunks; ++j) {
-        const int chunk = j >> 1, sub = q4 + 4 * (j & 1);
-        const char* src = chunk < C::kNope ? krow + chunk * 128 + sub * 16 : rrow + sub * 16;
-        const uint32_t dst = xdst + chunk * kChunk + ((sub ^ (kk & 7)) << 4);
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-      }
-      asm volatile("cp.async.commit_group;" ::: "memory");
-      if (t >= 1) {
-        asm volatile("cp.async.wait_group 1;" ::: "memory");
-        publish(t - 1);
+      for (int e = 0; e < 4; ++e) r4[e] = __shfl_sync(0xffffffffu, my_row, 4 * (lane & 7) + e);
+      for (int c = wq; c < C::kChunks; c += 4) {
+        mbar_wait(smem_u32(&bars.xe[s][c]), ph ^ 1u, a.err, &failed);
+        if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
+        const uint32_t full = smem_u32(&bars.xf[s][c]);
+        if (cta == 0 && lane == 0) mbar_arrive_expect_tx(full, 2 * kChunk);
+        if (lane < 8) {
+          const CUtensorMap* m = c < C::kNope ? &maps.k : &maps.kr;
+          tma_gather4_pair(sX + s * C::kXBytes + c * kChunk + lane * 512, m, mapa_shared(full, 0),
+                           c < C::kNope ? 64 * c : 0, r4[0], r4[1], r4[2], r4[3]);
+        }
+        __syncwarp();
       }
     }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    if (ntiles > 0 && !failed) publish(ntiles - 1);
   } else if (warp == 1) {
     // ---- UMMA issue (pair leader) ----
     if (cta == 0 && ntiles > 0 && lane == 0) {
@@ -214,29 +205,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads1, 1)
       const uint64_t dq = smem_desc_sw128(sQ, 16, 1024);
       const uint64_t dd = smem_desc_sw128(sO, 16, 1024);
       const uint64_t dx0 = smem_desc_sw128(sX, 16, 1024);
-      const uint64_t dx1 = smem_desc_sw128(sX + C::kXBytes, 16, 1024);
       mbar_wait(smem_u32(&bars.q_full), 0, a.err, &failed);
       for (int t = 0; t < ntiles && !failed; ++t) {
         const int s = t & 1;
-        if (t >= 2) mbar_wait(smem_u32(&bars.s_free[s]), ((t >> 1) - 1) & 1, a.err, &failed, true);
-        mbar_wait(smem_u32(&bars.x_full[s]), (t >> 1) & 1, a.err, &failed, true);
-        if (failed) break;
-        tc_fence_after();
-        const uint64_t bx = s ? dx1 : dx0;
+        const uint32_t ph = (uint32_t)(t >> 1) & 1u;
+        if (t >= 2) mbar_wait(smem_u32(&bars.s_free[s]), ph ^ 1u, a.err, &failed, true);
+        const uint64_t bx = dx0 + (uint64_t)((s * C::kXBytes) >> 4);
         const uint32_t d_s = tmem + 32 * s, d_p = tmem + 64 + 32 * s;
 #pragma unroll
-        for (int c = 0; c < C::kChunks; ++c)
+        for (int c = 0; c < C::kChunks; ++c) {
+          if (!mbar_wait(smem_u32(&bars.xf[s][c]), ph, a.err, &failed, true)) break;
+          tc_fence_after();
 #pragma unroll
           for (int u = 0; u < 4; ++u)
             umma_f16<2>(d_s, dq + (uint64_t)((c * kHeads * 128 + u * 32) >> 4),
                         bx + (uint64_t)((c * kChunk + u * 32) >> 4), id, (c | u) != 0);
+          if (c < C::kNope) {
 #pragma unroll
-        for (int c = 0; c < C::kNope; ++c)
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            umma_f16<2>(d_p, dd + (uint64_t)((c * kHeads * 128 + u * 32) >> 4),
-                        bx + (uint64_t)((c * kChunk + u * 32) >> 4), id, (c | u) != 0);
-        umma_commit_pair(smem_u32(&bars.x_empty[s]), 3);
+            for (int u = 0; u < 4; ++u)
+              umma_f16<2>(d_p, dd + (uint64_t)((c * kHeads * 128 + u * 32) >> 4),
+                          bx + (uint64_t)((c * kChunk + u * 32) >> 4), id, (c | u) != 0);
+          }
+          umma_commit_pair(smem_u32(&bars.xe[s][c]), 3);
+        }
+        if (failed) break;
         umma_commit_pair(smem_u32(&bars.s_full[s]), 3);
       }
     }
@@ -852,6 +844,8 @@ int launch(const DsaSfaBwdParams* p, cudaStream_t stream) {
   if (!make_tmap_2d_16b(&m1.q, p->q, bf16, qrows, D, (uint64_t)D * 2, 64, 64) ||
       !make_tmap_2d_16b(&m1.qr, p->q_rope, bf16, qrows, 64, 128, 64, 64) ||
       !make_tmap_2d_16b(&m1.dout, p->d_out, bf16, qrows, D, (uint64_t)D * 2, 64, 64) ||
+      !make_tmap_2d_16b(&m1.k, p->key, bf16, p->kv_rows, D, (uint64_t)D * 2, 64, 1) ||
+      !make_tmap_2d_16b(&m1.kr, p->key_rope, bf16, p->kv_rows, 64, 128, 64, 1) ||
       !make_tmap_2d_16b(&m2.ds, a.ds, bf16, srows, kp, kp * 2, 64, 64) ||
       !make_tmap_2d_16b(&m2.k, p->key, bf16, p->kv_rows, D, (uint64_t)D * 2, 64, 1) ||
       !make_tmap_2d_16b(&m2.kr, p->key_rope, bf16, p->kv_rows, 64, 128, 64, 1) ||
