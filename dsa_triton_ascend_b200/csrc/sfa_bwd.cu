@@ -68,12 +68,39 @@ struct Args {
   const int32_t* ws_count;
   void* ds;        // [num_rows][128][kp] scratch, dtype of the inputs
   void* pp;        // [num_rows][128][kp]
+  const float* delta;   // [num_rows][N1] rowsum(dO * O), from sfa_bwd_delta_kernel
   int kp;          // keys per row in the scratch (multiple of 128)
   int* err;
 };
 
 __device__ __forceinline__ void named_bar(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+// =====================================================================================
+// K0: delta = rowsum(dO * O) per (query row, head), coalesced: one warp per head row
+// =====================================================================================
+template <int D, typename T>
+__global__ void __launch_bounds__(256) sfa_bwd_delta_kernel(const T* __restrict__ dout,
+                                                            const T* __restrict__ out,
+                                                            float* __restrict__ delta, int64_t n) {
+  const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= n) return;
+  const uint4* a = reinterpret_cast<const uint4*>(dout + w * D);
+  const uint4* b = reinterpret_cast<const uint4*>(out + w * D);
+  float acc = 0.f;
+#pragma unroll
+  for (int i = lane; i < D / 8; i += 32) {
+    const uint4 u0 = __ldg(a + i), u1 = __ldg(b + i);
+    const T* x0 = reinterpret_cast<const T*>(&u0);
+    const T* x1 = reinterpret_cast<const T*>(&u1);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc += ElemTraits<T>::to_f(x0[e]) * ElemTraits<T>::to_f(x1[e]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) delta[w] = acc;
 }
 
 // =====================================================================================
@@ -103,7 +130,6 @@ struct __align__(16) Bars1 {
   uint64_t q_full;
   uint64_t xf[2][9], xe[2][9], s_full[2], s_free[2];
   uint32_t tmem_slot;
-  float red[4][32];
 };
 
 constexpr int kThreads1 = 320;   // 0: Q/dO TMA, 1: MMA, 2-5: elementwise, 6-9: key gathers
@@ -248,20 +274,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads1, 1)
       off = __ldg(a.smax + hidx) * 1.4426950408889634f;
       const float sm = __ldg(a.ssum + hidx);
       inv_sum = 1.f / (sm > 0.f ? sm : 1.f);
-      const T* dor = reinterpret_cast<const T*>(a.dout) + hidx * D + half * (D / 2);
-      const T* orr = reinterpret_cast<const T*>(a.out) + hidx * D + half * (D / 2);
-      for (int d = 0; d < D / 2; d += 8) {
-        const uint4 u0 = *reinterpret_cast<const uint4*>(dor + d);
-        const uint4 u1 = *reinterpret_cast<const uint4*>(orr + d);
-        const T* x0 = reinterpret_cast<const T*>(&u0);
-        const T* x1 = reinterpret_cast<const T*>(&u1);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) delta += ElemTraits<T>::to_f(x0[e]) * ElemTraits<T>::to_f(x1[e]);
-      }
+      delta = __ldg(a.delta + hidx);
     }
-    bars.red[q][lane] = delta;
-    named_bar(1, 128);
-    delta += bars.red[q ^ 2][lane];
     const uint32_t lead_f0 = mapa_shared(smem_u32(&bars.s_free[0]), 0);
     const uint32_t lead_f1 = mapa_shared(smem_u32(&bars.s_free[1]), 0);
     T* ds_row = reinterpret_cast<T*>(a.ds) + ((size_t)row * kHeadsPad + head) * a.kp;
@@ -835,6 +849,8 @@ int launch(const DsaSfaBwdParams* p, cudaStream_t stream) {
   a.ds = ws;
   ws += align256(p->num_rows * kHeadsPad * kp * 2);
   a.pp = ws;
+  ws += align256(p->num_rows * kHeadsPad * kp * 2);
+  a.delta = reinterpret_cast<const float*>(ws);
   a.kp = (int)kp;
 
   Maps1 m1;
@@ -863,6 +879,12 @@ int launch(const DsaSfaBwdParams* p, cudaStream_t stream) {
     return DSA_ERR_CUDA;
   sfa_prep_kernel<Args><<<dim3((unsigned)((p->num_rows + 3) / 4)), dim3(128), 0, stream>>>(
       a, const_cast<int32_t*>(a.ws_rows), const_cast<int32_t*>(a.ws_count));
+  {
+    const int64_t n = p->num_rows * p->n1;
+    sfa_bwd_delta_kernel<D, T><<<dim3((unsigned)((n + 7) / 8)), dim3(256), 0, stream>>>(
+        static_cast<const T*>(p->d_out), static_cast<const T*>(p->out),
+        const_cast<float*>(a.delta), n);
+  }
 
   {
     auto k = sfa_bwd_probs_kernel<D, T>;
@@ -898,7 +920,7 @@ extern "C" int64_t dsa_sfa_bwd_workspace_size(int64_t num_rows, int64_t topk, in
   if (num_rows < 0 || topk < 0 || sparse_block_size < 1) return -1;
   const int64_t nent = topk * sparse_block_size;
   return align256(4 * num_rows * nent) + align256(4 * num_rows) +
-         2 * align256(num_rows * kHeadsPad * padded_keys(nent) * 2);
+         2 * align256(num_rows * kHeadsPad * padded_keys(nent) * 2) + align256(4 * num_rows * kHeadsPad);
 }
 
 extern "C" int dsa_sfa_bwd(const DsaSfaBwdParams* p, void* stream_) {
