@@ -280,27 +280,19 @@ def main():
     tokens_per_s = S1 / (ms_step * 1e-3)
 
     # ---- end to end through the public API with host buffers (pinned) ----
+    # Inputs in pinned host memory; the public streaming entry point copies them in, runs
+    # the forward and backward in row chunks and copies every result out, with the copies
+    # of one chunk overlapping the kernels of the next.
     host_in = [x.cpu().pin_memory() for x in (q, qr, k, kr, si, dout)]
     h2d = sum(x.numel() * x.element_size() for x in host_in)
-    outs_h = None
+    hq, hqr, hk, hkr, hsi, hdo = host_in
+    outs_h = dsa.host_outputs(hq, hk, hqr, hkr)
+    red = (lambda accs: [dist.all_reduce(t) for t in accs]) if world > 1 else None
 
     def e2e_step():
-        nonlocal outs_h
-        dq_, dqr_, dk_, dkr_, dsi_, ddo_ = (x.to(dev, non_blocking=True) for x in host_in)
-        o, m, s_ = dsa.sparse_flash_attention_triton(
-            dq_, dk_, dk_, dsi_, scale, actual_seq_lengths_query=aq, query_rope=dqr_,
-            key_rope=dkr_, sparse_mode=3, return_softmax_lse=True)
-        accs, finish = dsa.sparse_flash_attention_grad_partial(
-            dq_, dk_, dk_, dsi_, ddo_, o, m, s_, scale, query_rope=dqr_, key_rope=dkr_,
-            actual_seq_lengths_query=aq, sparse_mode=3)
-        if world > 1:
-            for t in accs:
-                dist.all_reduce(t)
-        res = [o] + list(finish())
-        if outs_h is None:
-            outs_h = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in res]
-        for h, t in zip(outs_h, res):
-            h.copy_(t, non_blocking=True)
+        dsa.sfa_fwd_bwd_from_host(hq, hk, hsi, hdo, scale, hqr, hkr, sparse_mode=3, chunks=8,
+                                  host_out=outs_h, actual_seq_length_query=aq[0],
+                                  reduce_key_grads=red)
 
     for _ in range(2):
         e2e_step()
@@ -369,7 +361,7 @@ def main():
             "fwd_roofline_frac": fwd_roof_frac,
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
-            "gpu_launches": args.steps * (2 + 6),   # per step: prep + fwd; prep, 3 bwd kernels, 3 casts
+            "gpu_launches": args.steps * (2 + 8),   # per step: prep + fwd; prep, delta, 3 bwd kernels, 3 casts
             "roofline": roof,
             "cpu_baseline": cpu,
             "clocks": clocks,

@@ -7,6 +7,9 @@ Drop-in for the operators of 18851871668/dsa_triton_ascend, on CUDA torch tensor
 * :func:`lightning_indexer_triton` / :class:`LightningIndexerTriton`
 * :func:`sparse_lightning_indexer_grad_kl_loss_triton` /
   :class:`SparseLightningIndexerGradKLLossTriton`
+
+plus :func:`sfa_fwd_bwd_from_host` (forward + backward of host-resident inputs, with the
+copies overlapped with the kernels).
 """
 from ._lib import check_device_errors, lib as _load_library  # noqa: F401
 from .sparse_flash_attention import (  # noqa: F401
@@ -23,6 +26,7 @@ from .sparse_flash_attention_grad import (  # noqa: F401
     sparse_flash_attention_grad_partial,
     sparse_flash_attention_grad_triton,
 )
+from .streaming import host_outputs, sfa_fwd_bwd_from_host  # noqa: F401
 
 __all__ = [
     "sparse_flash_attention_triton",

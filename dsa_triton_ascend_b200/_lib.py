@@ -60,7 +60,7 @@ class SfaBwdParams(ctypes.Structure):
         ("sparse_block_size", _i64), ("kv_rows", _i64), ("page_size", _i64),
         ("max_blocks", _i64), ("s2_cap", _i64),
         ("scale", ctypes.c_float), ("sparse_mode", ctypes.c_int32), ("dtype", ctypes.c_int32),
-        ("defer_cast", ctypes.c_int32),
+        ("defer_cast", ctypes.c_int32), ("accumulate", ctypes.c_int32),
     ]
 
 

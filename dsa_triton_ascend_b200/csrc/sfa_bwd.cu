@@ -872,10 +872,12 @@ int launch(const DsaSfaBwdParams* p, cudaStream_t stream) {
       !make_tmap_2d_16b(&m3.dout, p->d_out, bf16, qrows, D, (uint64_t)D * 2, 64, 128))
     return DSA_ERR_TMA_DESCRIPTOR;
 
-  // fp32 accumulators start at zero; the prep pass compacts the valid keys of each row
-  if (cudaMemsetAsync(p->dk_acc, 0, sizeof(float) * p->kv_rows * D, stream) != cudaSuccess ||
-      cudaMemsetAsync(p->dkr_acc, 0, sizeof(float) * p->kv_rows * 64, stream) != cudaSuccess ||
-      cudaMemsetAsync(p->dv_acc, 0, sizeof(float) * p->kv_rows * D, stream) != cudaSuccess)
+  // fp32 accumulators start at zero unless the caller adds several calls into them; the
+  // prep pass compacts the valid keys of each row
+  if (!p->accumulate &&
+      (cudaMemsetAsync(p->dk_acc, 0, sizeof(float) * p->kv_rows * D, stream) != cudaSuccess ||
+       cudaMemsetAsync(p->dkr_acc, 0, sizeof(float) * p->kv_rows * 64, stream) != cudaSuccess ||
+       cudaMemsetAsync(p->dv_acc, 0, sizeof(float) * p->kv_rows * D, stream) != cudaSuccess))
     return DSA_ERR_CUDA;
   sfa_prep_kernel<Args><<<dim3((unsigned)((p->num_rows + 3) / 4)), dim3(128), 0, stream>>>(
       a, const_cast<int32_t*>(a.ws_rows), const_cast<int32_t*>(a.ws_count));

@@ -25,7 +25,7 @@ _VALID_N1 = (1, 2, 4, 8, 16, 32, 64, 128)
 def _sfa_grad(query, key, value, sparse_indices, d_out, out, softmax_max, softmax_sum,
               scale_value, query_rope, key_rope, actual_seq_lengths_query,
               actual_seq_lengths_kv, sparse_block_size, layout, sparse_mode, pre_tokens,
-              next_tokens, deterministic, defer_cast):
+              next_tokens, deterministic, defer_cast, accumulators=None):
     # guards: sparse_flash_attention_grad_triton.py:428-438
     if pre_tokens != INT64_MAX or next_tokens != INT64_MAX:
         raise ValueError("pre_tokens/next_tokens only support default INT64_MAX")
@@ -92,9 +92,17 @@ def _sfa_grad(query, key, value, sparse_indices, d_out, out, softmax_max, softma
 
     dq = torch.empty_like(q)
     dqr = torch.empty_like(qr)
-    dk_acc = torch.empty((kv_rows, D), dtype=torch.float32, device=dev)
-    dkr_acc = torch.empty((kv_rows, D_ROPE), dtype=torch.float32, device=dev)
-    dv_acc = torch.empty((kv_rows, D), dtype=torch.float32, device=dev)
+    if accumulators is None:
+        dk_acc = torch.empty((kv_rows, D), dtype=torch.float32, device=dev)
+        dkr_acc = torch.empty((kv_rows, D_ROPE), dtype=torch.float32, device=dev)
+        dv_acc = torch.empty((kv_rows, D), dtype=torch.float32, device=dev)
+    else:
+        dk_acc, dkr_acc, dv_acc = accumulators
+        for t, n in ((dk_acc, D), (dkr_acc, D_ROPE), (dv_acc, D)):
+            if (t.dtype != torch.float32 or not t.is_contiguous() or t.device != dev
+                    or t.numel() != kv_rows * n):
+                raise ValueError("accumulators must be contiguous fp32 [kv_rows, dim] on the "
+                                 "query's device")
     kshape = key.shape
     dk = torch.empty(kshape, dtype=key.dtype, device=dev)
     dv = torch.empty(kshape, dtype=value.dtype if value is not None else key.dtype, device=dev)
@@ -118,11 +126,13 @@ def _sfa_grad(query, key, value, sparse_indices, d_out, out, softmax_max, softma
     p.sparse_mode = int(sparse_mode)
     p.dtype = H.dtype_code(query)
     p.defer_cast = 1 if defer_cast else 0
+    p.accumulate = 0 if accumulators is None else 1
     check(lib().dsa_sfa_bwd(p, stream_ptr(dev)), "dsa_sfa_bwd")
     if defer_cast:
         def finish():
             check(lib().dsa_sfa_bwd_cast(p, stream_ptr(dev)), "dsa_sfa_bwd_cast")
             return dq, dk, dv, dqr, dkr
+        finish.query_grads = (dq, dqr)   # ready before the cast (they need no reduction)
         return (dk_acc, dkr_acc, dv_acc), finish
     return dq, dk, dv, dqr, dkr
 
@@ -160,14 +170,17 @@ def sparse_flash_attention_grad_partial(query, key, value, sparse_indices, d_out
                                         softmax_max, softmax_sum, scale_value=1.0, **kw):
     """Backward for a caller that reduces the key gradients itself (e.g. across GPUs).
 
-    Same arguments as :func:`sparse_flash_attention_grad_triton`.  Returns
-    ``((dk_acc, dkr_acc, dv_acc), finish)``: the fp32 key-gradient accumulators, which the
-    caller may all-reduce in place, and ``finish()`` which casts them to the key dtype and
-    returns the usual 5-tuple.
+    Same arguments as :func:`sparse_flash_attention_grad_triton`, plus ``accumulators``:
+    optional fp32 ``(dk_acc, dkr_acc, dv_acc)`` to add this call's key gradients into
+    (query rows processed in several calls); without it they are fresh and zeroed.
+    Returns ``((dk_acc, dkr_acc, dv_acc), finish)``: the fp32 key-gradient accumulators,
+    which the caller may all-reduce in place, and ``finish()`` which casts them to the key
+    dtype and returns the usual 5-tuple.
     """
     args = dict(query_rope=None, key_rope=None, actual_seq_lengths_query=None,
                 actual_seq_lengths_kv=None, sparse_block_size=1, layout="BSND", sparse_mode=3,
-                pre_tokens=INT64_MAX, next_tokens=INT64_MAX, deterministic=False)
+                pre_tokens=INT64_MAX, next_tokens=INT64_MAX, deterministic=False,
+                accumulators=None)
     args.update(kw)
     return _sfa_grad(query, key, value, sparse_indices, d_out, out, softmax_max, softmax_sum,
                      scale_value, defer_cast=True, **args)

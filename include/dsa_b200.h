@@ -131,7 +131,7 @@ int dsa_sfa_fwd_noalloc(const DsaSfaFwdParams* params, void* stream);
  * d_out and out ([num_rows][n1][d]), softmax_max / softmax_sum ([num_rows][n1], the forward's
  * statistics).  Outputs: dq [num_rows][n1][d], dqr [num_rows][n1][64] (query dtype); the key
  * gradients are accumulated in caller-provided fp32 buffers dk_acc [kv_rows][d],
- * dkr_acc [kv_rows][64], dv_acc [kv_rows][d] (zeroed by the call) and, unless defer_cast is
+ * dkr_acc [kv_rows][64], dv_acc [kv_rows][d] (zeroed by the call unless accumulate is set) and, unless defer_cast is
  * set, cast into dk / dkr / dv (key dtype, NULL to skip).  With defer_cast a caller (e.g. a
  * multi-GPU one that all-reduces the fp32 buffers) finishes with dsa_sfa_bwd_cast().
  * The key gradients are scatter-added with fp32 vector reductions, so their summation order
@@ -177,6 +177,8 @@ typedef struct DsaSfaBwdParams {
   int32_t sparse_mode;
   int32_t dtype;
   int32_t defer_cast;            /* 1: leave the key gradients in the fp32 buffers */
+  int32_t accumulate;            /* 1: add into dk_acc / dkr_acc / dv_acc instead of zeroing
+                                    them first (query rows processed in several calls) */
 } DsaSfaBwdParams;
 
 int dsa_sfa_bwd(const DsaSfaBwdParams* params, void* stream);
