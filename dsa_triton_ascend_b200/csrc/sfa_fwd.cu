@@ -7,24 +7,26 @@
 // with M=128 gives each CTA 64 of the 128 query heads (rows) while both CTAs feed
 // half of the B operand:
 //   * QK^T : B = gathered keys, split by token (CTA r owns tokens [32r, 32r+32) of
-//            each 64-token tile, all 576 latent+rope dims)      -> "X" ring (3 tiles)
+//            each 64-token tile, all 576 latent+rope dims)      -> "X" ring (2 tiles)
 //   * P V  : B = V (= key[:, :D]) split by head dim (CTA r provides D/2 dims for
-//            all 64 tokens of the tile)                          -> "H" buffer
-// Every key row crosses L2 -> SM once: each CTA gathers only its own 32 tokens into X,
-// then fills the V slices of H from X with shared-memory bulk copies -- its own
-// tokens' slices into its own H, the partner's slices straight into the partner's H
-// (distributed shared memory) -- instead of gathering the partner's tokens again.
+//            all 64 tokens of the tile)                          -> "H" ring (2 tiles)
+// Every key row crosses L2 -> SM once: each CTA gathers only its own 32 tokens into X
+// (TMA gather4 in the 2-SM form, so the bytes of both CTAs are counted on the leader's
+// barrier), and once QK^T of the tile is done, two copy warps move the V slices out of X
+// -- its own tokens' slices into its own H, the partner's slices straight into the
+// partner's H (distributed shared memory stores) -- instead of gathering the partner's
+// tokens again.  Copies are done by threads, not by the TMA unit, because there they
+// would queue behind the gathers.  P and H are double-buffered so that the slow
+// cross-CTA signals (a cluster-scope arrive waits for the CTA's in-flight TMA traffic)
+// overlap the next tile instead of stalling it.
 // S (64 heads x 64 tokens) and O (64 heads x D) live in TMEM in the 2x2 layout of
 // the M=128 pair MMA: lanes 0-63 hold the first half of the columns, lanes 64-127
 // the second half.  Valid indices are compacted by sfa_prep_kernel, so causal rows
 // with fewer than topK visible keys only pay for their valid keys.
 //
-// Warp roles (608 threads): warp 0 loads Q and then copies X -> H; warp 1 issues UMMA
-// (pair leader) and owns TMEM, or in the second CTA tells the leader that its H is
-// full; warps 2-5 run the online softmax, the lazy O rescale and the epilogue; warp 6
-// tells the leader that this CTA's X tile landed; warps 7-18 gather the QK^T keys with
-// cp.async. One CTA keeps about 30 GB/s of scattered 128-byte row pieces in flight from
-// L2 only with that many load threads.
+// Warp roles (352 threads): warps 0 and 6 copy X -> H (warp 0 first loads Q); warp 1
+// issues UMMA (pair leader) and owns TMEM; warps 2-5 run the online softmax, the lazy O
+// rescale and the epilogue; warps 7-10 gather the QK^T keys with TMA gather4.
 
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -46,10 +48,9 @@ constexpr int kOwn = 32;           // keys per CTA in the QK B operand
 constexpr int kHeads = 64;         // heads per CTA
 constexpr int kChunkBytesX = kOwn * 128;     // one 64-dim chunk of 32 own keys
 constexpr int kChunkBytesH = kOwn * 128;     // one 64-dim chunk of 32 keys (a token half)
-constexpr int kXStages = 3;
 constexpr int kLoadWarp0 = 7;
-constexpr int kLoadWarps = 12;               // two groups of 6, alternate tiles
-constexpr int kXLoaders = 32 * kLoadWarps;   // cp.async threads gathering the QK^T keys
+constexpr int kLoadWarps = 4;                // TMA gather4 issuers (chunks c % 4 == w)
+constexpr int kCopyThreads = 64;             // warps 0 and 6
 constexpr int kThreads = 32 * (kLoadWarp0 + kLoadWarps);
 constexpr float kRescaleLog2 = 8.0f;         // lazy rescale threshold (log2 units)
 
@@ -69,9 +70,9 @@ struct Cfg {
   // smem carve-up (from a 1 KiB aligned base)
   static constexpr int kOffQ = 0;
   static constexpr int kOffX = kOffQ + kQBytes;
-  static constexpr int kOffH = kOffX + kXStages * kXBytes;
-  static constexpr int kOffP = kOffH + kHBytes;
-  static constexpr int kOffBars = kOffP + kPBytes;
+  static constexpr int kOffH = kOffX + 2 * kXBytes;
+  static constexpr int kOffP = kOffH + 2 * kHBytes;
+  static constexpr int kOffBars = kOffP + 2 * kPBytes;
   // the Bars struct follows at kOffBars; total = kOffBars + sizeof(Bars)
   static constexpr int kTmemO = 256;                        // O columns start
   static constexpr int kTmemCols = 512;
@@ -107,24 +108,26 @@ struct Args {
   float scale;
 };
 
-// Barrier protocol (t = tile, s = t % kXStages):
-//   x_local[s]  this CTA's loaders -> its copy thread and forwarder: own tokens landed
-//   x_full[s]   (leader) both forwarders: X of tile t ready for QK^T
-//   x_empty[s]  PV(t) commit, both CTAs: X stage s may be refilled (QK^T and the
-//               X -> H copies of tile t are both complete once PV(t) is)
-//   h_full      byte count of this CTA's H (own + partner copies) for tile t
-//   h_peer      (leader) second CTA's H of tile t is full
-//   s_full[t&1] QK^T(t) commit: S ready;  p_full (leader) both CTAs wrote P(t)
-//   pv_done     PV(t) commit, both CTAs: O updated, P and H free again
+// Barrier protocol (t = tile, b = t & 1 selects the X stage, H slot, S and P buffer):
+//   x_full[b]   (leader) bytes of both CTAs' gathers of tile t: X ready for QK^T
+//   x_empty[b]  (each CTA) QK^T(t) done and this CTA's copy warps have read X(t)
+//   s_full[b]   QK^T(t) commit, both CTAs: S ready (and X(t) read by the tensor core)
+//   h_full[b]   (leader) both CTAs' copy warps finished the H slot of tile t
+//   p_full[b]   (leader) both CTAs wrote P(t)
+//   pv_done[b]  PV(t) commit, both CTAs: O updated, P buffer and H slot b free again
 struct __align__(16) Bars {
   uint64_t q_full;
-  uint64_t x_local[kXStages], x_full[kXStages], x_empty[kXStages];
-  uint64_t h_full, h_peer;
-  uint64_t s_full[2], p_full, pv_done;
+  uint64_t x_full[2], x_empty[2], s_full[2], h_full[2], p_full[2], pv_done[2];
   uint32_t tmem_slot;
   float red_max[2][4][32];
   float red_sum[4][32];
 };
+
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x),
+               "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
 
 template <int D, typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
@@ -157,17 +160,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(&bars.q_full), 1);
-    for (int s = 0; s < kXStages; ++s) {
-      mbar_init(smem_u32(&bars.x_local[s]), kXLoaders / 2);   // one loader group per tile
-      mbar_init(smem_u32(&bars.x_full[s]), 2);
-      mbar_init(smem_u32(&bars.x_empty[s]), 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&bars.x_full[b]), 1);
+      mbar_init(smem_u32(&bars.x_empty[b]), 1);
+      mbar_init(smem_u32(&bars.s_full[b]), 1);
+      mbar_init(smem_u32(&bars.h_full[b]), 2);
+      mbar_init(smem_u32(&bars.p_full[b]), 2);
+      mbar_init(smem_u32(&bars.pv_done[b]), 1);
     }
-    mbar_init(smem_u32(&bars.h_full), 1);
-    mbar_init(smem_u32(&bars.h_peer), 1);
-    mbar_init(smem_u32(&bars.s_full[0]), 1);
-    mbar_init(smem_u32(&bars.s_full[1]), 1);
-    mbar_init(smem_u32(&bars.p_full), 2);
-    mbar_init(smem_u32(&bars.pv_done), 1);
     fence_mbarrier_init();
   }
   if (warp == 1) {
@@ -181,9 +181,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t tmem = bars.tmem_slot;
   bool failed = false;
 
-  if (warp == 0) {
-    // ====== Q of this CTA's 64 heads (once), then the X -> H copies of every tile ======
-    if (ntiles > 0) {
+  if (warp == 0 || warp == 6) {
+    // ====== warp 0: Q of this CTA's 64 heads (once); warps 0 and 6: X -> H copies ======
+    if (warp == 0 && ntiles > 0) {
       const uint32_t lead_q = mapa_shared(smem_u32(&bars.q_full), 0);
       if (cta == 0 && lane == 0) mbar_arrive_expect_tx(smem_u32(&bars.q_full), 2 * C::kQBytes);
       __syncwarp();
@@ -194,93 +194,75 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tma_load_2d_pair(sQ + lane * kHeads * 128, m, lead_q, x, qrow0);
       }
     }
-    if (lane == 0) {
-      const uint32_t peer = cta ^ 1u;
-      const uint32_t h_own = smem_u32(&bars.h_full);
-      const uint32_t h_remote = mapa_shared(h_own, peer);
-      const uint32_t sH_remote = mapa_shared(sH, peer);
-      for (int t = 0; t < ntiles && !failed; ++t) {
-        const int s = t % kXStages;
-        if (!mbar_wait(smem_u32(&bars.x_local[s]), (uint32_t)(t / kXStages) & 1u, a.err, &failed))
-          break;
-        // H is single-buffered: PV(t-1) must be done (in both CTAs: one pair MMA)
-        if (!mbar_wait(smem_u32(&bars.pv_done), (uint32_t)(t & 1) ^ 1u, a.err, &failed)) break;
-        mbar_arrive_expect_tx(h_own, C::kHBytes);
-        const uint32_t xs = sX + s * C::kXBytes;
-        const uint32_t hoff = cta * C::kHHalf;       // this CTA's tokens: half `cta` of H
+    const int ci = (warp == 0 ? 0 : 32) + lane;         // copy thread 0..63
+    const uint32_t peer = cta ^ 1u;
+    const uint32_t lead_h0 = mapa_shared(smem_u32(&bars.h_full[0]), 0);
+    const uint32_t lead_h1 = mapa_shared(smem_u32(&bars.h_full[1]), 0);
+    for (int t = 0; t < ntiles; ++t) {
+      const int b = t & 1;
+      const uint32_t ph = (uint32_t)(t >> 1) & 1u;
+      // QK^T(t) done (so X(t) landed in both CTAs) and PV(t-2) done (H slot b free in
+      // both CTAs: one pair MMA)
+      mbar_wait(smem_u32(&bars.s_full[b]), ph, a.err, &failed);
+      mbar_wait(smem_u32(&bars.pv_done[b]), ph ^ 1u, a.err, &failed);
+      if (!failed) {
+        const uint32_t xs = C::kOffX + b * C::kXBytes;
+        const uint32_t hs = C::kOffH + b * C::kHBytes + cta * C::kHHalf;   // my tokens' half
 #pragma unroll
         for (int sl = 0; sl < C::kSlots; ++sl) {
-          bulk_copy_s2c(sH + hoff + sl * kChunkBytesH, xs + C::slot_chunk(sl, cta) * kChunkBytesX,
-                        kChunkBytesX, h_own);
-          bulk_copy_s2c(sH_remote + hoff + sl * kChunkBytesH,
-                        xs + C::slot_chunk(sl, peer) * kChunkBytesX, kChunkBytesX, h_remote);
-        }
-      }
-    }
-    __syncwarp();
-  } else if (warp == 6) {
-    // ====== both CTAs: tell the leader's MMA thread that this CTA's X of tile t landed ======
-    // (a thread of its own, so QK^T(t+1) never waits behind the H copies of tile t)
-    if (lane == 0) {
-      for (int t = 0; t < ntiles; ++t) {
-        const int s = t % kXStages;
-        if (!mbar_wait(smem_u32(&bars.x_local[s]), (uint32_t)(t / kXStages) & 1u, a.err, &failed))
-          break;
-        mbar_arrive_cluster(mapa_shared(smem_u32(&bars.x_full[s]), 0));
-      }
-    }
-    __syncwarp();
-  } else if (warp >= kLoadWarp0) {
-    // ====== X loaders: own 32 keys x all dims for QK^T (cp.async) ======
-    // Two groups of kLoadWarps/2 warps take alternate tiles, so each group publishes
-    // a tile as soon as its copies land while the other group's tile is in flight.
-    // In a group, thread i serves key i / kTpk and the 16-byte pieces (i % kTpk) +
-    // kTpk * j of its 1152-byte row (8 pieces per 64-dim chunk, 9 chunks).
-    constexpr int kGroup = kXLoaders / 2;
-    constexpr int kTpk = kGroup / kOwn;                     // threads per key
-    constexpr int kPieces = 8 * C::kChunks;
-    constexpr int kPer = (kPieces + kTpk - 1) / kTpk;       // pieces per thread
-    const int i = threadIdx.x - kLoadWarp0 * 32;
-    const int grp = i / kGroup;
-    const int kk = (i % kGroup) / kTpk, q0 = (i % kGroup) % kTpk;
-    const char* kbase = static_cast<const char*>(a.key);
-    const char* rbase = static_cast<const char*>(a.key_rope);
-    const int filler = nvalid > 0 ? __ldg(rows) : 0;
-    for (int t = grp; t < ntiles && !failed; t += 2) {
-      const int s = t % kXStages;
-      const int j0 = kTile * t + kOwn * (int)cta + kk;
-      const int r = j0 < nvalid ? __ldg(rows + j0) : filler;
-      mbar_wait(smem_u32(&bars.x_empty[s]), ((uint32_t)(t / kXStages) & 1u) ^ 1u, a.err, &failed);
-      if (failed) break;
-      const char* krow = kbase + (size_t)r * (D * 2);
-      const char* rrow = rbase + (size_t)r * 128;
-      const uint32_t xdst = sX + s * C::kXBytes + kk * 128;
+          const uint32_t src_own = xs + C::slot_chunk(sl, cta) * kChunkBytesX;
+          const uint32_t src_peer = xs + C::slot_chunk(sl, peer) * kChunkBytesX;
+          const uint32_t dst = hs + sl * kChunkBytesH;
+          uint4 v[8];
 #pragma unroll
-      for (int j = 0; j < kPer; ++j) {
-        const int pc = q0 + kTpk * j;
-        if (pc < kPieces) {
-          const int chunk = pc >> 3, sub = pc & 7;
-          const char* src = chunk < C::kNopeChunks ? krow + chunk * 128 + sub * 16 : rrow + sub * 16;
-          const uint32_t dst = xdst + chunk * kChunkBytesX + ((sub ^ (kk & 7)) << 4);
-          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+          for (int j = 0; j < 4; ++j) {
+            v[j] = *reinterpret_cast<const uint4*>(smem_raw + src_own + 16 * (ci + 64 * j));
+            v[4 + j] = *reinterpret_cast<const uint4*>(smem_raw + src_peer + 16 * (ci + 64 * j));
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            *reinterpret_cast<uint4*>(smem_raw + dst + 16 * (ci + 64 * j)) = v[j];
+            st_cluster_v4(mapa_shared(sbase + dst + 16 * (ci + 64 * j), peer), v[4 + j]);
+          }
         }
       }
-      asm volatile("cp.async.commit_group;" ::: "memory");
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
-      fence_proxy_async_smem();   // this thread's pieces of tile t landed
-      mbar_arrive(smem_u32(&bars.x_local[s]));
+      fence_proxy_async_smem();
+      asm volatile("fence.proxy.async.shared::cluster;" ::: "memory");
+      named_bar_sync(2, kCopyThreads);
+      if (ci == 0) {
+        mbar_arrive(smem_u32(&bars.x_empty[b]));             // X(t) read: refill it
+        mbar_arrive_cluster(b ? lead_h1 : lead_h0);           // H slot b of tile t written
+      }
     }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
+  } else if (warp >= kLoadWarp0) {
+    // ====== X loaders: own 32 keys x all dims for QK^T, TMA gather4 (4 keys x 128 B) ======
+    // warp w issues chunks c with c % 4 == w, lanes 0-7 the chunk's 8 gathers; the bytes
+    // of both CTAs are counted on the leader's x_full, so no thread waits for the data.
+    const int wq = warp - kLoadWarp0;
+    const int filler = nvalid > 0 ? __ldg(rows) : 0;
+    for (int t = 0; t < ntiles && !failed; ++t) {
+      const int b = t & 1;
+      const int j = kTile * t + kOwn * (int)cta + lane;
+      const int my_row = j < nvalid ? __ldg(rows + j) : filler;
+      int r4[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) r4[e] = __shfl_sync(0xffffffffu, my_row, 4 * (lane & 7) + e);
+      mbar_wait(smem_u32(&bars.x_empty[b]), ((uint32_t)(t >> 1) & 1u) ^ 1u, a.err, &failed);
+      if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
+      const uint32_t full = smem_u32(&bars.x_full[b]);
+      if (cta == 0 && wq == 0 && lane == 0) mbar_arrive_expect_tx(full, 2 * C::kXBytes);
+      if (lane < 8) {
+        const uint32_t lead = mapa_shared(full, 0);
+        for (int c = wq; c < C::kChunks; c += kLoadWarps) {
+          const CUtensorMap* m = c < C::kNopeChunks ? &maps.k : &maps.kr;
+          tma_gather4_pair(sX + b * C::kXBytes + c * kChunkBytesX + lane * 512, m, lead,
+                           c < C::kNopeChunks ? 64 * c : 0, r4[0], r4[1], r4[2], r4[3]);
+        }
+      }
+      __syncwarp();
+    }
   } else if (warp == 1) {
     // ======================= MMA issuer (pair leader) =======================
-    // In the second CTA this warp forwards "my H is full" to the leader instead.
-    if (cta == 1 && lane == 0) {
-      const uint32_t lead = mapa_shared(smem_u32(&bars.h_peer), 0);
-      for (int t = 0; t < ntiles; ++t) {
-        if (!mbar_wait(smem_u32(&bars.h_full), (uint32_t)t & 1u, a.err, &failed)) break;
-        mbar_arrive_cluster(lead);
-      }
-    }
     if (cta == 0 && ntiles > 0 && lane == 0) {
       const bool bf16 = ElemTraits<T>::kIsBf16;
       const uint32_t id_qk = idesc_f16(128, kTile, bf16, false, false);
@@ -290,33 +272,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       // (>> 4) to the start-address field, which cannot carry: shared addresses < 2^18.
       const uint64_t dq = smem_desc_sw128(sQ, 16, 1024);
       const uint64_t dx0 = smem_desc_sw128(sX, 16, 1024);
-      const uint64_t dp = smem_desc_sw128(sP, 16, 1024);
-      const uint64_t dh = smem_desc_sw128(sH, kChunkBytesH, 1024);
+      const uint64_t dp0 = smem_desc_sw128(sP, 16, 1024);
+      const uint64_t dh0 = smem_desc_sw128(sH, kChunkBytesH, 1024);
       auto issue_qk = [&](int t) {
-        const int s = t % kXStages;
-        if (!mbar_wait(smem_u32(&bars.x_full[s]), (uint32_t)(t / kXStages) & 1u, a.err, &failed,
-                       true))
+        const int b = t & 1;
+        if (!mbar_wait(smem_u32(&bars.x_full[b]), (uint32_t)(t >> 1) & 1u, a.err, &failed, true))
           return;
         tc_fence_after();
-        const uint32_t d = tmem + 32 * (t & 1);
-        const uint64_t bx = dx0 + (uint64_t)((s * C::kXBytes) >> 4);
+        const uint32_t d = tmem + 32 * b;
+        const uint64_t bx = dx0 + (uint64_t)((b * C::kXBytes) >> 4);
 #pragma unroll
         for (int c = 0; c < C::kChunks; ++c)
 #pragma unroll
           for (int u = 0; u < 4; ++u)
             umma_f16<2>(d, dq + (uint64_t)((c * kHeads * 128 + u * 32) >> 4),
                         bx + (uint64_t)((c * kChunkBytesX + u * 32) >> 4), id_qk, (c | u) != 0);
-        umma_commit_pair(smem_u32(&bars.s_full[t & 1]), 3);
+        umma_commit_pair(smem_u32(&bars.s_full[b]), 3);
       };
       if (!failed) issue_qk(0);
       for (int t = 0; t < ntiles && !failed; ++t) {
         if (t + 1 < ntiles) issue_qk(t + 1);
-        const uint32_t par = (uint32_t)t & 1u;
-        mbar_wait(smem_u32(&bars.p_full), par, a.err, &failed, true);
-        mbar_wait(smem_u32(&bars.h_full), par, a.err, &failed);
-        mbar_wait(smem_u32(&bars.h_peer), par, a.err, &failed, true);
+        const int b = t & 1;
+        const uint32_t par = (uint32_t)(t >> 1) & 1u;
+        mbar_wait(smem_u32(&bars.p_full[b]), par, a.err, &failed, true);
+        mbar_wait(smem_u32(&bars.h_full[b]), par, a.err, &failed, true);
         if (failed) break;
         tc_fence_after();
+        const uint64_t dp = dp0 + (uint64_t)((b * C::kPBytes) >> 4);
+        const uint64_t dh = dh0 + (uint64_t)((b * C::kHBytes) >> 4);
 #pragma unroll
         for (int j = 0; j < C::kNumPV; ++j)
 #pragma unroll
@@ -325,8 +308,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         dh + (uint64_t)(((k >> 1) * C::kHHalf + j * C::kCpj * kChunkBytesH +
                                          (k & 1) * 2048) >> 4),
                         id_pv, (t | k) != 0);
-        umma_commit_pair(smem_u32(&bars.x_empty[t % kXStages]), 3);
-        umma_commit_pair(smem_u32(&bars.pv_done), 3);
+        umma_commit_pair(smem_u32(&bars.pv_done[b]), 3);
       }
     }
     __syncwarp();
@@ -337,7 +319,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int half = q >> 1;                 // key half of the tile / O column half
     const uint32_t lane_addr = (uint32_t)(32 * q) << 16;
     const float c2 = a.scale * 1.4426950408889634f;
-    const uint32_t lead_p = mapa_shared(smem_u32(&bars.p_full), 0);
+    const uint32_t lead_p0 = mapa_shared(smem_u32(&bars.p_full[0]), 0);
+    const uint32_t lead_p1 = mapa_shared(smem_u32(&bars.p_full[1]), 0);
     float m_run = -INFINITY, m_ref = -INFINITY, l_part = 0.f;
 
     for (int t = 0; t < ntiles; ++t) {
@@ -384,10 +367,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         l_part += p0 + p1;
         pk[i] = ElemTraits<T>::pack2(p0, p1);
       }
-      // P (single buffer) was last read by PV(t-1), and O may only be rescaled once
-      // PV(t-1) is done.
-      if (t >= 1) mbar_wait(smem_u32(&bars.pv_done), (uint32_t)(t - 1) & 1u, a.err, &failed);
+      // P buffer s was last read by PV(t-2); O may be touched only once PV(t-1) is done.
+      if (t >= 2) mbar_wait(smem_u32(&bars.pv_done[s]), par ^ 1u, a.err, &failed);
       if (__any_sync(0xffffffffu, rescale)) {
+        if (t >= 1)
+          mbar_wait(smem_u32(&bars.pv_done[s ^ 1]), (uint32_t)((t - 1) >> 1) & 1u, a.err, &failed);
         l_part *= factor;
         if (!__any_sync(0xffffffffu, failed)) {
           tc_fence_after();
@@ -402,7 +386,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           tmem_st_wait();
         }
       }
-      uint8_t* prow = gP + hrow * 128;
+      uint8_t* prow = gP + s * C::kPBytes + hrow * 128;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         int chunk = 4 * half + i;
@@ -412,14 +396,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       fence_proxy_async_smem();
       tc_fence_before();
       named_bar_sync(1, 128);
-      if (warp == 2 && lane == 0) mbar_arrive_cluster(lead_p);
+      if (warp == 2 && lane == 0) {
+        if (cta == 0) mbar_arrive(smem_u32(&bars.p_full[s]));   // leader: a local arrive
+        else mbar_arrive_cluster(s ? lead_p1 : lead_p0);
+      }
     }
 
     // ------------------------------ epilogue ------------------------------
     bars.red_sum[q][lane] = l_part;
     if (ntiles > 0) {
       const int tl = ntiles - 1;
-      mbar_wait(smem_u32(&bars.pv_done), (uint32_t)tl & 1u, a.err, &failed);
+      mbar_wait(smem_u32(&bars.pv_done[tl & 1]), (uint32_t)(tl >> 1) & 1u, a.err, &failed);
     }
     const bool read_o = ntiles > 0 && !__any_sync(0xffffffffu, failed);
     named_bar_sync(1, 128);
