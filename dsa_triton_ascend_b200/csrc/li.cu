@@ -80,7 +80,10 @@ struct __align__(16) Bars {
   int qrow[256];
 };
 
-template <int DP, typename T>
+// GF > 0: the head-group size G is the compile-time GF (32, 64 or 128) and N = 256, so
+// every 32-column TMEM load belongs to one token and the epilogue is straight-line code;
+// GF == 0 handles any G.
+template <int DP, typename T, int GF>
 __global__ void __launch_bounds__(kThreads, 1)
     li_score_kernel(const __grid_constant__ CUtensorMap kmap, const Args a) {
   using C = Cfg<DP>;
@@ -211,8 +214,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool wfail = __any_sync(0xffffffffu, failed);
       tc_fence_after();
       const int key = kKeys * t + 32 * qd + lane;
-      int tok = 0, gcount = 0;
-      float acc = 0.f;
       auto emit = [&](int tq, float v) {
         const int lim = bars.lim[tq];
         if (lim >= 0 && key < a.s2_row) {
@@ -220,24 +221,58 @@ __global__ void __launch_bounds__(kThreads, 1)
           *dst = key < lim ? v : -INFINITY;
         }
       };
-      for (int c0 = 0; c0 < N; c0 += 32) {
-        uint32_t r[32];
-        if (!wfail) {
-          tmem_ld32(tmem + lane_addr + 256 * buf + c0, r);
-          tmem_ld_wait();
-        } else {
+      if constexpr (GF > 0) {
+        // 256 columns = 256 / GF tokens x GF heads; four independent partial sums per
+        // 32-column load, weights read four at a time (the same for every thread)
+        float acc = 0.f;
+#pragma unroll 1
+        for (int c0 = 0; c0 < 256; c0 += 32) {
+          uint32_t r[32];
+          if (!wfail) {
+            tmem_ld32(tmem + lane_addr + 256 * buf + c0, r);
+            tmem_ld_wait();
+          } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = 0u;
+            for (int i = 0; i < 32; ++i) r[i] = 0u;
+          }
+          const float4* w4 = reinterpret_cast<const float4*>(w_s + c0);
+          float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            const float4 w = w4[i / 4];
+            p0 = fmaf(fmaxf(__uint_as_float(r[i]), 0.f), w.x, p0);
+            p1 = fmaf(fmaxf(__uint_as_float(r[i + 1]), 0.f), w.y, p1);
+            p2 = fmaf(fmaxf(__uint_as_float(r[i + 2]), 0.f), w.z, p2);
+            p3 = fmaf(fmaxf(__uint_as_float(r[i + 3]), 0.f), w.w, p3);
+          }
+          acc += (p0 + p1) + (p2 + p3);
+          if ((c0 + 32) % GF == 0) {
+            emit(c0 / GF, acc);
+            acc = 0.f;
+          }
         }
+      } else {
+        int tok = 0, gcount = 0;
+        float acc = 0.f;
+        for (int c0 = 0; c0 < N; c0 += 32) {
+          uint32_t r[32];
+          if (!wfail) {
+            tmem_ld32(tmem + lane_addr + 256 * buf + c0, r);
+            tmem_ld_wait();
+          } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          if (tok < Tq) {
-            acc = fmaf(fmaxf(__uint_as_float(r[i]), 0.f), w_s[c0 + i], acc);
-            if (++gcount == G) {
-              emit(tok, acc);
-              ++tok;
-              gcount = 0;
-              acc = 0.f;
+            for (int i = 0; i < 32; ++i) r[i] = 0u;
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if (tok < Tq) {
+              acc = fmaf(fmaxf(__uint_as_float(r[i]), 0.f), w_s[c0 + i], acc);
+              if (++gcount == G) {
+                emit(tok, acc);
+                ++tok;
+                gcount = 0;
+                acc = 0.f;
+              }
             }
           }
         }
@@ -303,6 +338,71 @@ __device__ __forceinline__ int block_scan(int v, int* warp_sums, int* total) {
   __syncthreads();
   *total = tot;
   return base + x - v;
+}
+
+// Bitonic sort (descending) of E * kTopkThreads 64-bit keys, thread t holding positions
+// [E t, E t + E) in registers: strides below E are exchanged inside the thread, strides
+// below 32 E between the lanes of a warp (shuffles), and only the wider ones go through
+// shared memory with a block barrier.
+template <int E>
+__device__ __forceinline__ void bitonic_desc(unsigned long long* sel) {
+  constexpr int kN = E * kTopkThreads;
+  const int t = threadIdx.x;
+  unsigned long long v[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) v[e] = sel[E * t + e];
+  for (int size = 2; size <= kN; size <<= 1) {
+    for (int stride = size >> 1; stride >= E; stride >>= 1) {
+      if (stride >= 32 * E) {
+        // through shared memory
+#pragma unroll
+        for (int e = 0; e < E; ++e) sel[E * t + e] = v[e];
+        __syncthreads();
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const int p = E * t + e, q = p ^ stride;
+          const unsigned long long y = sel[q];
+          const bool desc = (p & size) == 0;
+          const bool lo = p < q;
+          const unsigned long long mx = v[e] > y ? v[e] : y, mn = v[e] > y ? y : v[e];
+          v[e] = (desc == lo) ? mx : mn;
+        }
+        __syncthreads();
+      } else {
+        const int lx = stride / E;   // partner lane distance
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const int p = E * t + e, q = p ^ stride;
+          const unsigned long long y = __shfl_xor_sync(0xffffffffu, v[e], lx);
+          const bool desc = (p & size) == 0;
+          const bool lo = p < q;
+          const unsigned long long mx = v[e] > y ? v[e] : y, mn = v[e] > y ? y : v[e];
+          v[e] = (desc == lo) ? mx : mn;
+        }
+      }
+    }
+    // strides inside the thread (compile-time, so v stays in registers)
+#pragma unroll
+    for (int st = E >> 1; st > 0; st >>= 1) {
+      if (st < size) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+          const int f = e ^ st;
+          if (f > e) {
+            const int p = E * t + e;
+            const bool desc = (p & size) == 0;
+            const unsigned long long x = v[e], y = v[f];
+            const bool swap = desc ? (x < y) : (x > y);
+            v[e] = swap ? y : x;
+            v[f] = swap ? x : y;
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e) sel[E * t + e] = v[e];
+  __syncthreads();
 }
 
 template <typename T>
@@ -383,20 +483,29 @@ __global__ void __launch_bounds__(kTopkThreads) li_topk_kernel(const TopkArgs a)
   for (int i = nsel + threadIdx.x; i < a.KP; i += kTopkThreads) sel[i] = 0ull;
   __syncthreads();
   // bitonic sort, descending
-  for (int size = 2; size <= a.KP; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = threadIdx.x; i < a.KP; i += kTopkThreads) {
-        const int j = i ^ stride;
-        if (j > i) {
-          const bool desc = (i & size) == 0;
-          const unsigned long long x = sel[i], y = sel[j];
-          if (desc ? (x < y) : (x > y)) {
-            sel[i] = y;
-            sel[j] = x;
+  if (a.KP >= kTopkThreads) {
+    switch (a.KP / kTopkThreads) {
+      case 1: bitonic_desc<1>(sel); break;
+      case 2: bitonic_desc<2>(sel); break;
+      case 4: bitonic_desc<4>(sel); break;
+      default: bitonic_desc<8>(sel); break;
+    }
+  } else {
+    for (int size = 2; size <= a.KP; size <<= 1) {
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        for (int i = threadIdx.x; i < a.KP; i += kTopkThreads) {
+          const int j = i ^ stride;
+          if (j > i) {
+            const bool desc = (i & size) == 0;
+            const unsigned long long x = sel[i], y = sel[j];
+            if (desc ? (x < y) : (x > y)) {
+              sel[i] = y;
+              sel[j] = x;
+            }
           }
         }
+        __syncthreads();
       }
-      __syncthreads();
     }
   }
   int32_t* oi = a.out_idx + ((size_t)row * a.N2 + n2) * K;
@@ -411,6 +520,19 @@ __global__ void __launch_bounds__(kTopkThreads) li_topk_kernel(const TopkArgs a)
       if (ov) ov[j] = ElemTraits<T>::from_f(-INFINITY);
     }
   }
+}
+
+template <int DP, typename T, int GF>
+int launch_score(const CUtensorMap& kmap, const Args& a, int64_t batch, int64_t n2,
+                 cudaStream_t stream) {
+  using C = Cfg<DP>;
+  auto k = li_score_kernel<DP, T, GF>;
+  const int smem = C::kOffBars + (int)sizeof(Bars);
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return DSA_ERR_CUDA;
+  if (a.nblk > 0)
+    k<<<dim3((unsigned)(batch * a.nblk), (unsigned)n2), dim3(kThreads), smem, stream>>>(kmap, a);
+  return DSA_OK;
 }
 
 template <int DP, typename T>
@@ -449,12 +571,12 @@ int launch(const DsaLiParams* p, cudaStream_t stream) {
   a.sparse_mode = p->sparse_mode;
   a.w_dtype = p->weights_dtype;
   a.q_len_dense = (int)p->q_len_dense;
-  auto k = li_score_kernel<DP, T>;
-  const int smem = C::kOffBars + (int)sizeof(Bars);
-  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-    return DSA_ERR_CUDA;
-  if (a.nblk > 0)
-    k<<<dim3((unsigned)(p->batch * a.nblk), (unsigned)p->n2), dim3(kThreads), smem, stream>>>(kmap, a);
+  int rc;
+  if (N == 256 && G == 64) rc = launch_score<DP, T, 64>(kmap, a, p->batch, p->n2, stream);
+  else if (N == 256 && G == 32) rc = launch_score<DP, T, 32>(kmap, a, p->batch, p->n2, stream);
+  else if (N == 256 && G == 128) rc = launch_score<DP, T, 128>(kmap, a, p->batch, p->n2, stream);
+  else rc = launch_score<DP, T, 0>(kmap, a, p->batch, p->n2, stream);
+  if (rc != DSA_OK) return rc;
 
   TopkArgs t;
   t.scores = a.scores;
