@@ -11,13 +11,28 @@ import torch
 
 INT64_MAX = 9223372036854775807
 
+# Small constant index tensors (row bases, default lengths) are cached per device: a
+# decode step would otherwise spend more host time launching their fill kernels than
+# the GPU spends on attention.  They are internal and never written after creation.
+_const_cache: dict = {}
+
+
+def _cached(key, make):
+    t = _const_cache.get(key)
+    if t is None:
+        if len(_const_cache) > 256:
+            _const_cache.clear()
+        t = make()
+        _const_cache[key] = t
+    return t
+
 
 def lens_tensor(lens, batch: int, default: int, device) -> torch.Tensor:
     """None -> [default]*batch; list/tuple/int -> int32 tensor; tensor -> int32 on device."""
-    if lens is None:
-        return torch.full((batch,), int(default), dtype=torch.int32, device=device)
-    if isinstance(lens, int):
-        return torch.full((batch,), lens, dtype=torch.int32, device=device)
+    if lens is None or isinstance(lens, int):
+        v = int(default) if lens is None else int(lens)
+        return _cached(("full", batch, v, str(device)),
+                       lambda: torch.full((batch,), v, dtype=torch.int32, device=device))
     if isinstance(lens, (list, tuple)):
         if len(lens) != batch:
             raise ValueError(f"expected {batch} sequence lengths, got {len(lens)}")
@@ -46,7 +61,8 @@ def tnd_offsets(cum: torch.Tensor):
 
 
 def row_bases(batch: int, stride: int, device) -> torch.Tensor:
-    return torch.arange(batch, dtype=torch.int32, device=device) * int(stride)
+    return _cached(("bases", batch, int(stride), str(device)),
+                   lambda: torch.arange(batch, dtype=torch.int32, device=device) * int(stride))
 
 
 def dtype_code(t: torch.Tensor) -> int:

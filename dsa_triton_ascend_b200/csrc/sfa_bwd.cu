@@ -879,8 +879,8 @@ int launch(const DsaSfaBwdParams* p, cudaStream_t stream) {
        cudaMemsetAsync(p->dkr_acc, 0, sizeof(float) * p->kv_rows * 64, stream) != cudaSuccess ||
        cudaMemsetAsync(p->dv_acc, 0, sizeof(float) * p->kv_rows * D, stream) != cudaSuccess))
     return DSA_ERR_CUDA;
-  sfa_prep_kernel<Args><<<dim3((unsigned)((p->num_rows + 3) / 4)), dim3(128), 0, stream>>>(
-      a, const_cast<int32_t*>(a.ws_rows), const_cast<int32_t*>(a.ws_count));
+  launch_prep(a, const_cast<int32_t*>(a.ws_rows), const_cast<int32_t*>(a.ws_count), p->num_rows,
+              stream);
   {
     const int64_t n = p->num_rows * p->n1;
     sfa_bwd_delta_kernel<D, T><<<dim3((unsigned)((n + 7) / 8)), dim3(256), 0, stream>>>(

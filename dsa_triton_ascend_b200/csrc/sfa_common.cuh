@@ -6,6 +6,7 @@
 // kv_rows, page, max_blocks, s2_cap and sparse_mode.
 #pragma once
 
+#include <cuda_runtime.h>
 #include <stdint.h>
 
 namespace dsa {
@@ -95,6 +96,69 @@ __global__ void __launch_bounds__(128) sfa_prep_kernel(const A a, int32_t* ws_ro
   if (lane == 0) ws_count[row] = have;
 }
 
+
+// The same compaction with one 512-thread block per query row, for calls with few rows
+// (decode): the warp-per-row kernel would walk a 2048-entry row in 64 dependent steps
+// (index, then page table) on a handful of SMs.  Two passes over the row: count the valid
+// entries of each warp's segment, then write them at the warp's offset, in index order.
+constexpr int kPrepBlockThreads = 512;
+
+template <class A>
+__global__ void __launch_bounds__(kPrepBlockThreads) sfa_prep_block_kernel(const A a, int32_t* ws_rows,
+                                                                           int32_t* ws_count) {
+  __shared__ int cnt[kPrepBlockThreads / 32];
+  const int row = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const RowInfo ri = row_info(a, row);
+  const int nent = a.topk * a.block;
+  constexpr int kWarps = kPrepBlockThreads / 32;
+  const int seg = ((nent + kPrepBlockThreads - 1) / kPrepBlockThreads) * 32;   // per warp
+  const int j0 = warp * seg, j1 = min(nent, j0 + seg);
+  const int32_t* row_idx = a.idx + (size_t)row * a.topk;
+  int have = 0;
+  if (ri.active) {
+#pragma unroll 4
+    for (int base = j0; base < j1; base += 32) {
+      const int j = base + lane;
+      const int kp = j < j1 ? key_at(a, ri, row_idx, j) : -1;
+      have += __popc(__ballot_sync(0xffffffffu, kp >= 0));
+    }
+  }
+  if (lane == 0) cnt[warp] = have;
+  __syncthreads();
+  int off = 0, total = 0;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) {
+    off += w < warp ? cnt[w] : 0;
+    total += cnt[w];
+  }
+  if (ri.active) {
+    int32_t* out = ws_rows + (size_t)row * nent + off;
+    int done = 0;
+#pragma unroll 4
+    for (int base = j0; base < j1; base += 32) {
+      const int j = base + lane;
+      const int kp = j < j1 ? key_at(a, ri, row_idx, j) : -1;
+      const unsigned m = __ballot_sync(0xffffffffu, kp >= 0);
+      if (kp >= 0) out[done + __popc(m & ((1u << lane) - 1u))] = key_row(a, ri.b, kp);
+      done += __popc(m);
+    }
+  }
+  if (threadIdx.x == 0) ws_count[row] = ri.active ? total : 0;
+}
+
+// Compaction pre-pass for `num_rows` rows: one block per row when there are few rows,
+// one warp per row otherwise.
+template <class A>
+inline void launch_prep(const A& a, int32_t* ws_rows, int32_t* ws_count, int64_t num_rows,
+                        cudaStream_t stream) {
+  if (num_rows <= 1024)
+    sfa_prep_block_kernel<A><<<dim3((unsigned)num_rows), dim3(kPrepBlockThreads), 0, stream>>>(
+        a, ws_rows, ws_count);
+  else
+    sfa_prep_kernel<A><<<dim3((unsigned)((num_rows + 3) / 4)), dim3(128), 0, stream>>>(
+        a, ws_rows, ws_count);
+}
 
 }  // namespace sfa
 }  // namespace dsa

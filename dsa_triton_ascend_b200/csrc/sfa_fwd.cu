@@ -495,8 +495,8 @@ int launch(const DsaSfaFwdParams* p, cudaStream_t stream) {
   a.scale = p->scale;
   a.ws_rows = static_cast<const int32_t*>(p->workspace);
   a.ws_count = static_cast<const int32_t*>(p->workspace) + (size_t)p->num_rows * p->topk * p->sparse_block_size;
-  sfa_prep_kernel<<<dim3((unsigned)((p->num_rows + 3) / 4)), dim3(128), 0, stream>>>(
-      a, const_cast<int32_t*>(a.ws_rows), const_cast<int32_t*>(a.ws_count));
+  launch_prep(a, const_cast<int32_t*>(a.ws_rows), const_cast<int32_t*>(a.ws_count), p->num_rows,
+              stream);
   auto kern = sfa_fwd_kernel<D, T>;
   constexpr int kSmem = smem_bytes<D>();
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)

@@ -150,11 +150,14 @@ def sparse_flash_attention_triton(
     kr = key_rope.contiguous()
 
     out = torch.empty(query.shape, dtype=query.dtype, device=dev)
+    # the kernel writes every statistic (zeros for rows without keys); zeros are only
+    # needed when they are not requested
+    alloc = torch.empty if return_softmax_lse else torch.zeros
     if is_tnd_q:
-        smax = torch.zeros((1, num_rows, N1), dtype=torch.float32, device=dev)
+        smax = alloc((1, num_rows, N1), dtype=torch.float32, device=dev)
     else:
-        smax = torch.zeros((B, 1, S1, N1), dtype=torch.float32, device=dev)
-    ssum = torch.zeros_like(smax)
+        smax = alloc((B, 1, S1, N1), dtype=torch.float32, device=dev)
+    ssum = alloc(smax.shape, dtype=torch.float32, device=dev)
 
     ws_bytes = lib().dsa_sfa_fwd_workspace_size(num_rows, topk, int(sparse_block_size))
     ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=dev)
