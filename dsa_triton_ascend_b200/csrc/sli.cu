@@ -89,7 +89,7 @@ __device__ __forceinline__ int key_row_of(const Args& a, int b, int row, int e) 
 // =====================================================================================
 constexpr int kTKeys = 128;        // keys per CTA per tile (pair tile: 256)
 constexpr int kTStages = 6;        // ring of 64-dim key chunks
-constexpr int kTThreads = 320;     // 0: Q/stats, 1: MMA, 2-5: epilogue, 6-9: key loaders
+constexpr int kTThreads = 320;     // 0: Q/stats, 1: MMA, 2-5: epilogue, 6-9: key gathers
 
 template <int D>
 struct TCfg {
@@ -103,7 +103,7 @@ struct TCfg {
 };
 
 struct TMaps {
-  CUtensorMap q, qr;
+  CUtensorMap q, qr, k, kr;   // k / kr: box 64 x 1 (gather4 rows)
 };
 
 struct __align__(16) TBars {
@@ -146,7 +146,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(&bars.q_full), 1);
     for (int s = 0; s < kTStages; ++s) {
-      mbar_init(smem_u32(&bars.full[s]), 2 * 128);
+      mbar_init(smem_u32(&bars.full[s]), 1);   // bytes of both CTAs' gathers
       mbar_init(smem_u32(&bars.empty[s]), 1);
     }
     for (int s = 0; s < 2; ++s) {
@@ -177,38 +177,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTThreads, 1)
                          lane < C::kNope ? 64 * lane : 0, qrow0);
     }
   } else if (warp >= 6) {
-    // one key per thread; its 1152-byte row arrives chunk by chunk
-    const int kk = threadIdx.x - 6 * 32;
-    const char* kb = static_cast<const char*>(a.k);
-    const char* rb = static_cast<const char*>(a.kr);
+    // the CTA's 128 keys of each tile, chunk by chunk, by TMA gather4 in the 2-SM form:
+    // warp w gathers keys [32w, 32w+32) (8 gathers of 4 rows), and the bytes of both CTAs
+    // are counted on the leader's barrier, so no thread waits for the data
+    const int w = warp - 6;
     const int filler = n > 0 ? key_row_of(a, b, row, 0) : 0;
-    int r = 0;
+    int r4[4] = {0, 0, 0, 0};
     for (int j = 0; j < nsteps && !failed; ++j) {
       const int t = j / C::kChunks, c = j % C::kChunks, s = j % kTStages;
       if (c == 0) {
-        const int e = 2 * kTKeys * t + kTKeys * (int)cta + kk;
-        r = e < n ? key_row_of(a, b, row, e) : filler;
+        const int e = 2 * kTKeys * t + kTKeys * (int)cta + 32 * w + lane;
+        const int my_row = e < n ? key_row_of(a, b, row, e) : filler;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) r4[q] = __shfl_sync(0xffffffffu, my_row, 4 * (lane & 7) + q);
       }
       mbar_wait(smem_u32(&bars.empty[s]), ((j / kTStages) & 1) ^ 1, a.err, &failed);
-      if (failed) break;
-      const char* src = c < C::kNope ? kb + (size_t)r * (D * 2) + c * 128 : rb + (size_t)r * 128;
-      const uint32_t dst = sK + s * C::kStage + kk * 128;
-#pragma unroll
-      for (int sub = 0; sub < 8; ++sub)
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst + ((sub ^ (kk & 7)) << 4)),
-                     "l"(src + sub * 16)
-                     : "memory");
-      asm volatile("cp.async.commit_group;" ::: "memory");
-      if (j >= 1) {
-        asm volatile("cp.async.wait_group 1;" ::: "memory");
-        fence_proxy_async_smem();
-        mbar_arrive_cluster(mapa_shared(smem_u32(&bars.full[(j - 1) % kTStages]), 0));
-      }
-    }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    if (nsteps > 0 && !failed) {
-      fence_proxy_async_smem();
-      mbar_arrive_cluster(mapa_shared(smem_u32(&bars.full[(nsteps - 1) % kTStages]), 0));
+      if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
+      const uint32_t full = smem_u32(&bars.full[s]);
+      if (cta == 0 && w == 0 && lane == 0) mbar_arrive_expect_tx(full, 2 * C::kStage);
+      if (lane < 8)
+        tma_gather4_pair(sK + s * C::kStage + (32 * w + 4 * lane) * 128,
+                         c < C::kNope ? &maps.k : &maps.kr, mapa_shared(full, 0),
+                         c < C::kNope ? 64 * c : 0, r4[0], r4[1], r4[2], r4[3]);
+      __syncwarp();
     }
   } else if (warp == 1) {
     if (cta == 0 && ntiles > 0 && lane == 0) {
@@ -675,6 +666,8 @@ int launch(const DsaSliParams* p, cudaStream_t stream) {
   IMaps im;
   if (!make_tmap_2d_16b(&tm.q, p->query, bf16, qrows, D, (uint64_t)D * 2, 64, 64) ||
       !make_tmap_2d_16b(&tm.qr, p->query_rope, bf16, qrows, 64, 128, 64, 64) ||
+      !make_tmap_2d_16b(&tm.k, p->key, bf16, krows, D, (uint64_t)D * 2, 64, 1) ||
+      !make_tmap_2d_16b(&tm.kr, p->key_rope, bf16, krows, 64, 128, 64, 1) ||
       !make_tmap_2d_16b(&im.ki, p->key_index, bf16, krows, kDi, kDi * 2, 64, 1))
     return DSA_ERR_TMA_DESCRIPTOR;
   if (cudaMemsetAsync(p->dki_acc, 0, sizeof(float) * krows * kDi, stream) != cudaSuccess ||
