@@ -9,7 +9,7 @@ Drop-in for the operators of 18851871668/dsa_triton_ascend, on CUDA torch tensor
   :class:`SparseLightningIndexerGradKLLossTriton`
 
 plus :func:`sfa_fwd_bwd_from_host` (forward + backward of host-resident inputs, with the
-copies overlapped with the kernels).
+copies overlapped with the kernels) and the autograd functions of :mod:`.autograd`.
 """
 from ._lib import check_device_errors, lib as _load_library  # noqa: F401
 from .sparse_flash_attention import (  # noqa: F401
@@ -27,6 +27,11 @@ from .sparse_flash_attention_grad import (  # noqa: F401
     sparse_flash_attention_grad_triton,
 )
 from .streaming import host_outputs, sfa_fwd_bwd_from_host  # noqa: F401
+from .autograd import (  # noqa: F401
+    IndexerKLLossFunction,
+    SparseAttentionWithIndexer,
+    SparseFlashAttentionFunction,
+)
 
 __all__ = [
     "sparse_flash_attention_triton",
