@@ -270,8 +270,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTThreads, 1)
 constexpr int kIKeys = 128;      // keys per tile (UMMA M)
 constexpr int kNip = 64;         // index heads padded to 64
 constexpr int kDi = 128;         // index head dim
-constexpr int kIStages = 2;
-constexpr int kIThreads = 192;   // 0: gathers, 1: MMA, 2-5: epilogue
+constexpr int kIStages = 3;
+constexpr int kIDrain0 = 6;      // first dKI drain warp
+constexpr int kIDrainWarps = 8;  // two per TMEM lane quadrant, 64 columns each
+constexpr int kIThreads = 32 * (kIDrain0 + kIDrainWarps);   // 0: gathers, 1: MMA, 2-5: epilogue
 
 struct ICfg {
   static constexpr int kQiBytes = 2 * kNip * 128;           // [dim chunk][64 heads][128 B]
@@ -280,9 +282,12 @@ struct ICfg {
   static constexpr int kOffQi = 0;
   static constexpr int kOffK = kQiBytes;
   static constexpr int kOffC = kOffK + kIStages * kStage;
-  static constexpr int kOffStage = kOffC + 2 * kCBytes;       // drain staging, 4 x 32 x 33 floats
-  static constexpr int kOffRed = kOffStage + 4 * 32 * 33 * 4; // dW column sums, 128 x 65 floats
-  static constexpr int kOffI = kOffRed + 128 * 65 * 4;        // I then dI: topk floats
+  static constexpr int kOffStage = kOffC + 2 * kCBytes;       // drain staging, 32 x 33 floats per drain warp
+  // dW column sums (128 x 65 floats) reuse the key ring: they are formed after the last
+  // tile's MMAs, when no gather or MMA touches the ring any more
+  static constexpr int kOffRed = kOffK;
+  static_assert(128 * 65 * 4 <= kIStages * kStage, "dW sums fit the key ring");
+  static constexpr int kOffI = kOffStage + kIDrainWarps * 32 * 33 * 4;   // I then dI: topk floats
 };
 
 struct IMaps {
@@ -290,7 +295,7 @@ struct IMaps {
 };
 
 struct __align__(16) IBars {
-  uint64_t full[kIStages], empty[kIStages], rfull[2], rfree[2], cready[2], cfree[2], dfull, dfree, qdone;
+  uint64_t full[kIStages], empty[kIStages], rfull[2], rfree[2], cready[2], cfree[2], dfull[2], dfree[2], qdone;
   uint32_t tmem_slot;
   int rows[2][kIKeys];
   float w[kNip];
@@ -349,8 +354,10 @@ __global__ void __launch_bounds__(kIThreads, 1)
       mbar_init(smem_u32(&bars.cready[s]), 1);
       mbar_init(smem_u32(&bars.cfree[s]), 1);
     }
-    mbar_init(smem_u32(&bars.dfull), 1);
-    mbar_init(smem_u32(&bars.dfree), 4);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(smem_u32(&bars.dfull[s]), 1);
+      mbar_init(smem_u32(&bars.dfree[s]), kIDrainWarps);
+    }
     mbar_init(smem_u32(&bars.qdone), 1);
     fence_mbarrier_init();
   }
@@ -363,7 +370,7 @@ __global__ void __launch_bounds__(kIThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars.tmem_slot;
-  // TMEM: R[2] at cols 0 / 64, dQI^T at 128, dKI tile at 256
+  // TMEM: R[2] at cols 0 / 64, dQI^T at 128, dKI tiles (double buffer) at 256 / 384
   const uint32_t tR = tmem, tQ = tmem + 128, tD = tmem + 256;
   bool failed = false;
   const int nsteps = 2 * ntiles;   // pass A then pass B, one KI tile per step
@@ -420,7 +427,8 @@ __global__ void __launch_bounds__(kIThreads, 1)
         // pass B: wait for C of this tile, then dQI^T and dKI
         const int tb = t, cb = tb & 1;
         if (!mbar_wait(smem_u32(&bars.cready[cb]), (tb >> 1) & 1, a.err, &failed)) break;
-        if (tb >= 1 && !mbar_wait(smem_u32(&bars.dfree), (tb - 1) & 1, a.err, &failed)) break;
+        const int db = tb & 1;
+        if (tb >= 2 && !mbar_wait(smem_u32(&bars.dfree[db]), ((tb >> 1) - 1) & 1, a.err, &failed)) break;
         tc_fence_after();
         const uint64_t dc_k = smem_desc_sw128(sC + cb * C::kCBytes, 16, 1024);
         const uint64_t dc_mn = smem_desc_sw128(sC + cb * C::kCBytes, 16, 1024);
@@ -434,23 +442,65 @@ __global__ void __launch_bounds__(kIThreads, 1)
                         dc_mn + (uint64_t)((po + k * 2048) >> 4), id_q, (tb | k | part) != 0);
 #pragma unroll
           for (int u = 0; u < kNip / 16; ++u)     // K = index heads
-            umma_f16<1>(tD, dc_k + (uint64_t)((po + u * 32) >> 4),
+            umma_f16<1>(tD + 128 * db, dc_k + (uint64_t)((po + u * 32) >> 4),
                         dqi_mn + (uint64_t)((u * 2048) >> 4), id_d, (u | part) != 0);
         }
         umma_commit(smem_u32(&bars.empty[s]));
         umma_commit(smem_u32(&bars.cfree[cb]));
-        umma_commit(smem_u32(&bars.dfull));
+        umma_commit(smem_u32(&bars.dfull[db]));
       }
       if (!failed) umma_commit(smem_u32(&bars.qdone));
     }
     __syncwarp();
+  } else if (warp >= kIDrain0) {
+    // ---- dKI drain: warp = (TMEM lane quadrant, 64-column half); thread = key row ----
+    // Eight warps keep enough fp32 vector reductions in flight (one SM needs about 16 for
+    // its share of the L2 reduction rate; four left the drain the slowest stage), and the
+    // double-buffered TMEM tile lets the next tile's C and MMAs run meanwhile.
+    const int qd = warp & 3, half = (warp - kIDrain0) >> 2;
+    const uint32_t lane_addr = (uint32_t)(32 * qd) << 16;
+    float* stage = reinterpret_cast<float*>(smem_raw + C::kOffStage) + (warp - kIDrain0) * 32 * 33;
+    float* acc_out = a.dki_acc;
+    for (int t = 0; t < ntiles; ++t) {
+      const int db = t & 1;
+      mbar_wait(smem_u32(&bars.dfull[db]), (t >> 1) & 1, a.err, &failed);
+      const bool dfail = __any_sync(0xffffffffu, failed);
+      tc_fence_after();
+      const int my_key = kIKeys * t + 32 * qd + lane;
+      const int my_row = my_key < n ? key_row_of(a, b, row, my_key) : -1;
+      if (!dfail) {
+        for (int c0 = 64 * half; c0 < 64 * half + 64; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld32(tD + 128 * db + lane_addr + c0, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) stage[lane * 33 + i] = __uint_as_float(r[i]);
+          __syncwarp();
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int kr = 4 * it + (lane >> 3), cc = 4 * (lane & 7);
+            const int dst = __shfl_sync(0xffffffffu, my_row, kr);
+            if (dst >= 0) {
+              const float* sp = stage + kr * 33 + cc;
+              asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(
+                               acc_out + (size_t)dst * kDi + c0 + cc),
+                           "f"(sp[0]), "f"(sp[1]), "f"(sp[2]), "f"(sp[3])
+                           : "memory");
+            }
+          }
+          __syncwarp();
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bars.dfree[db]));
+    }
   } else {
     // ---- epilogue (128 threads, thread = key of the tile / dim of dQI) ----
     // TMEM lane quadrant of this warp; et = TMEM row (key of the tile / dim of dQI^T)
     const int qd = warp & 3, et = 32 * qd + lane;
     const uint32_t lane_addr = (uint32_t)(32 * qd) << 16;
     float* red = reinterpret_cast<float*>(smem_raw + C::kOffRed);
-    float* stage = reinterpret_cast<float*>(smem_raw + C::kOffStage) + qd * 32 * 33;
     float dw[kNip];
 #pragma unroll
     for (int g = 0; g < kNip; ++g) dw[g] = 0.f;
@@ -509,7 +559,6 @@ __global__ void __launch_bounds__(kIThreads, 1)
     named_bar(1, 128);
     if (et == 0 && n > 0) atomicAdd(a.loss, bars.red[4] + bars.red[5] + bars.red[6] + bars.red[7]);
     // ---------------- pass B: C, dW, dQI, dKI ----------------
-    float* acc_out = a.dki_acc;
     for (int t = 0; t < ntiles; ++t) {
       const int j = ntiles + t, rb = j & 1, cb = t & 1;
       mbar_wait(smem_u32(&bars.rfull[rb]), (j >> 1) & 1, a.err, &failed);
@@ -556,39 +605,9 @@ __global__ void __launch_bounds__(kIThreads, 1)
       named_bar(1, 128);
       if (et == 0) mbar_arrive(smem_u32(&bars.cready[cb]));
       if (lane == 0) mbar_arrive(smem_u32(&bars.rfree[rb]));
-      // drain the dKI tile: thread = key row of the tile
-      mbar_wait(smem_u32(&bars.dfull), t & 1, a.err, &failed);
-      const bool dfail = __any_sync(0xffffffffu, failed);
-      tc_fence_after();
-      const int my_key = kIKeys * t + 32 * qd + lane;
-      const int my_row = my_key < n ? key_row_of(a, b, row, my_key) : -1;
-      if (!dfail) {
-        for (int c0 = 0; c0 < kDi; c0 += 32) {
-          uint32_t r[32];
-          tmem_ld32(tD + lane_addr + c0, r);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) stage[lane * 33 + i] = __uint_as_float(r[i]);
-          __syncwarp();
-#pragma unroll
-          for (int it = 0; it < 8; ++it) {
-            const int kr = 4 * it + (lane >> 3), cc = 4 * (lane & 7);
-            const int dst = __shfl_sync(0xffffffffu, my_row, kr);
-            if (dst >= 0) {
-              const float* sp = stage + kr * 33 + cc;
-              asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(
-                               acc_out + (size_t)dst * kDi + c0 + cc),
-                           "f"(sp[0]), "f"(sp[1]), "f"(sp[2]), "f"(sp[3])
-                           : "memory");
-            }
-          }
-          __syncwarp();
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&bars.dfree));
     }
+    // the last tile's MMAs are done: the key ring is free for the dW sums, dQI is final
+    if (ntiles > 0) mbar_wait(smem_u32(&bars.qdone), 0, a.err, &failed);
     // ---------------- dW: column sums of the per-thread partials ----------------
     for (int g = 0; g < kNip; ++g) red[et * 65 + g] = dw[g];
     named_bar(1, 128);
@@ -601,7 +620,6 @@ __global__ void __launch_bounds__(kIThreads, 1)
       else static_cast<__half*>(a.dw)[wi] = __float2half_rn(s);
     }
     // ---------------- dQI: TMEM lanes = dims, columns = index heads ----------------
-    if (ntiles > 0) mbar_wait(smem_u32(&bars.qdone), 0, a.err, &failed);
     const bool qfail = ntiles == 0 || __any_sync(0xffffffffu, failed);
     tc_fence_after();
     T* dq = static_cast<T*>(a.dqi) + (size_t)row * a.Ni * kDi;
