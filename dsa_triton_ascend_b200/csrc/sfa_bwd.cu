@@ -66,10 +66,10 @@ struct Args {
   float* dv_acc;
   const int32_t* ws_rows;
   const int32_t* ws_count;
-  void* ds;        // [num_rows][128][kp] scratch, dtype of the inputs
-  void* pp;        // [num_rows][128][kp]
+  void* ds;        // [num_rows][kp][128 heads] scratch (key-major), dtype of the inputs
+  void* pp;        // [num_rows][kp][128 heads]
   const float* delta;   // [num_rows][N1] rowsum(dO * O), from sfa_bwd_delta_kernel
-  int kp;          // keys per row in the scratch (multiple of 128)
+  int kp;          // key slots per row in the scratch (multiple of 256)
   int* err;
 };
 
@@ -106,30 +106,40 @@ __global__ void __launch_bounds__(256) sfa_bwd_delta_kernel(const T* __restrict_
 // =====================================================================================
 // K1: probabilities and dS
 // =====================================================================================
+// One CTA pair per query row with the keys as the MMA's M dimension: a pair tile is 256
+// keys (128 gathered by each CTA) and N = the 128 heads, so S^T = K Q^T and dP^T = V dO^T
+// run at the full 2-SM rate (M = 256, N = 128) and both read the same gathered key chunk.
+// Each CTA keeps its 64 heads of Q and dO resident as the B operands; the keys stream
+// through a ring of 64-dim chunks (TMA gather4 in the 2-SM form).  In TMEM every CTA holds
+// its 128 keys (lanes) x all 128 heads (columns), so P = exp(s scale - max_h) / sum_h and
+// dS = P (dP - delta_h) scale need only per-head constants, no reduction across threads.
+// P and dS go to the scratch key-major: [row][key][128 heads].
+constexpr int kKeys1 = 128;     // keys per CTA per pair tile
+constexpr int kStages1 = 5;     // key chunk ring (16 KB each)
+
 template <int D>
 struct Cfg1 {
   static constexpr int kNope = D / 64;
   static constexpr int kChunks = kNope + 1;
-  static constexpr int kQBytes = kChunks * kHeads * 128;
-  static constexpr int kOBytes = kNope * kHeads * 128;       // dO
-  static constexpr int kXBytes = kChunks * kChunk;
+  static constexpr int kQBytes = kChunks * kHeads * 128;      // this CTA's 64 heads of Q
+  static constexpr int kOBytes = kNope * kHeads * 128;        // and of dO
+  static constexpr int kStage = kKeys1 * 128;                 // 128 keys x 64 dims
   static constexpr int kOffQ = 0;
   static constexpr int kOffO = kOffQ + kQBytes;
   static constexpr int kOffX = kOffO + kOBytes;
-  static constexpr int kOffBars = kOffX + 2 * kXBytes;
+  static constexpr int kOffBars = kOffX + kStages1 * kStage;
 };
 
 struct Maps1 {
   CUtensorMap q, qr, dout, k, kr;
 };
 
-// The key ring is kept per 64-dim chunk: xf/xe[s][c] track chunk c of tile stage s, so a
-// chunk is refilled with the next-but-one tile's chunk as soon as the S and dP MMAs that
-// read it have completed, not when the whole tile has.
 struct __align__(16) Bars1 {
-  uint64_t q_full;
-  uint64_t xf[2][9], xe[2][9], s_full[2], s_free[2];
+  uint64_t q_full, full[kStages1], empty[kStages1], tfull[2], tfree[2];
   uint32_t tmem_slot;
+  float mxl[128];   // softmax_max * log2(e) per head (+inf for padded heads)
+  float inv[128];   // 1 / softmax_sum (0 for padded heads)
+  float dlt[128];   // rowsum(dO * O)
 };
 
 constexpr int kThreads1 = 320;   // 0: Q/dO TMA, 1: MMA, 2-5: elementwise, 6-9: key gathers
@@ -152,24 +162,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads1, 1)
   const RowInfo ri = row_info(a, row);
   const bool abort = a.err != nullptr && *reinterpret_cast<volatile int*>(a.err) != 0;
   const int nvalid = (ri.active && !abort) ? __ldg(a.ws_count + row) : 0;
-  // an even number of tiles, so K3's 128-key tiles only ever read written (zeroed) slots
-  const int ntiles = nvalid > 0 ? 2 * ((nvalid + 2 * kTile - 1) / (2 * kTile)) : 0;
+  const int ntiles = (nvalid + 2 * kKeys1 - 1) / (2 * kKeys1);
+  const int nsteps = ntiles * C::kChunks;
   const int32_t* rows = a.ws_rows + (size_t)row * a.topk * a.block;
 
+  for (int h = threadIdx.x; h < 128; h += kThreads1) {
+    if (h < a.N1 && ntiles > 0) {
+      const size_t hidx = (size_t)row * a.N1 + h;
+      bars.mxl[h] = __ldg(a.smax + hidx) * 1.4426950408889634f;
+      const float sm = __ldg(a.ssum + hidx);
+      bars.inv[h] = 1.f / (sm > 0.f ? sm : 1.f);
+      bars.dlt[h] = __ldg(a.delta + hidx);
+    } else {   // padded heads: exp2(s - inf) = 0, so P = dS = 0
+      bars.mxl[h] = INFINITY;
+      bars.inv[h] = 0.f;
+      bars.dlt[h] = 0.f;
+    }
+  }
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(&bars.q_full), 1);
+    for (int s = 0; s < kStages1; ++s) {
+      mbar_init(smem_u32(&bars.full[s]), 1);   // bytes of both CTAs' gathers
+      mbar_init(smem_u32(&bars.empty[s]), 1);
+    }
     for (int s = 0; s < 2; ++s) {
-      for (int c = 0; c < C::kChunks; ++c) {
-        mbar_init(smem_u32(&bars.xf[s][c]), 1);
-        mbar_init(smem_u32(&bars.xe[s][c]), 1);
-      }
-      mbar_init(smem_u32(&bars.s_full[s]), 1);
-      mbar_init(smem_u32(&bars.s_free[s]), 2);
+      mbar_init(smem_u32(&bars.tfull[s]), 1);
+      mbar_init(smem_u32(&bars.tfree[s]), 2);
     }
     fence_mbarrier_init();
   }
   if (warp == 1) {
-    tmem_alloc<2>(smem_u32(&bars.tmem_slot), 128);
+    tmem_alloc<2>(smem_u32(&bars.tmem_slot), 512);
     tmem_relinquish<2>();
   }
   tc_fence_before();
@@ -196,137 +219,123 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads1, 1)
       }
     }
   } else if (warp >= 6) {
-    // ---- own 32 keys of each tile, all dims: TMA gather4 into this CTA's chunk ring,
-    // completing on the leader's barrier (2-SM form), so no thread waits for data ----
-    // warp w handles chunks c with c % 4 == w - 6; lanes 0-7 issue the chunk's 8 gathers
-    // (4 keys each).
-    const int wq = warp - 6;
+    // ---- the CTA's 128 keys of each tile, chunk by chunk (TMA gather4, 2-SM form):
+    // warp w gathers keys [32w, 32w+32), lanes 0-7 four rows each ----
+    const int w = warp - 6;
     const int filler = nvalid > 0 ? __ldg(rows) : 0;
-    for (int t = 0; t < ntiles && !failed; ++t) {
-      const int s = t & 1;
-      const uint32_t ph = (uint32_t)(t >> 1) & 1u;
-      const int j = kTile * t + kOwn * (int)cta + lane;
-      const int my_row = j < nvalid ? __ldg(rows + j) : filler;
-      int r4[4];
+    int r4[4] = {0, 0, 0, 0};
+    for (int j = 0; j < nsteps && !failed; ++j) {
+      const int t = j / C::kChunks, c = j % C::kChunks, s = j % kStages1;
+      if (c == 0) {
+        const int e = 2 * kKeys1 * t + kKeys1 * (int)cta + 32 * w + lane;
+        const int my_row = e < nvalid ? __ldg(rows + e) : filler;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) r4[e] = __shfl_sync(0xffffffffu, my_row, 4 * (lane & 7) + e);
-      for (int c = wq; c < C::kChunks; c += 4) {
-        mbar_wait(smem_u32(&bars.xe[s][c]), ph ^ 1u, a.err, &failed);
-        if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
-        const uint32_t full = smem_u32(&bars.xf[s][c]);
-        if (cta == 0 && lane == 0) mbar_arrive_expect_tx(full, 2 * kChunk);
-        if (lane < 8) {
-          const CUtensorMap* m = c < C::kNope ? &maps.k : &maps.kr;
-          tma_gather4_pair(sX + s * C::kXBytes + c * kChunk + lane * 512, m, mapa_shared(full, 0),
-                           c < C::kNope ? 64 * c : 0, r4[0], r4[1], r4[2], r4[3]);
-        }
-        __syncwarp();
+        for (int q = 0; q < 4; ++q) r4[q] = __shfl_sync(0xffffffffu, my_row, 4 * (lane & 7) + q);
       }
+      mbar_wait(smem_u32(&bars.empty[s]), ((j / kStages1) & 1) ^ 1, a.err, &failed);
+      if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
+      const uint32_t full = smem_u32(&bars.full[s]);
+      if (cta == 0 && w == 0 && lane == 0) mbar_arrive_expect_tx(full, 2 * C::kStage);
+      if (lane < 8)
+        tma_gather4_pair(sX + s * C::kStage + (32 * w + 4 * lane) * 128,
+                         c < C::kNope ? &maps.k : &maps.kr, mapa_shared(full, 0),
+                         c < C::kNope ? 64 * c : 0, r4[0], r4[1], r4[2], r4[3]);
+      __syncwarp();
     }
   } else if (warp == 1) {
-    // ---- UMMA issue (pair leader) ----
+    // ---- UMMA issue (pair leader): S^T and dP^T, M = 256 keys, N = 128 heads ----
     if (cta == 0 && ntiles > 0 && lane == 0) {
       const bool bf16 = ElemTraits<T>::kIsBf16;
-      const uint32_t id = idesc_f16(128, kTile, bf16, false, false);
+      const uint32_t id = idesc_f16(256, 128, bf16, false, false);
       const uint64_t dq = smem_desc_sw128(sQ, 16, 1024);
       const uint64_t dd = smem_desc_sw128(sO, 16, 1024);
       const uint64_t dx0 = smem_desc_sw128(sX, 16, 1024);
       mbar_wait(smem_u32(&bars.q_full), 0, a.err, &failed);
       for (int t = 0; t < ntiles && !failed; ++t) {
-        const int s = t & 1;
-        const uint32_t ph = (uint32_t)(t >> 1) & 1u;
-        if (t >= 2) mbar_wait(smem_u32(&bars.s_free[s]), ph ^ 1u, a.err, &failed, true);
-        const uint64_t bx = dx0 + (uint64_t)((s * C::kXBytes) >> 4);
-        const uint32_t d_s = tmem + 32 * s, d_p = tmem + 64 + 32 * s;
-#pragma unroll
-        for (int c = 0; c < C::kChunks; ++c) {
-          if (!mbar_wait(smem_u32(&bars.xf[s][c]), ph, a.err, &failed, true)) break;
+        const int b = t & 1;
+        if (t >= 2)
+          mbar_wait(smem_u32(&bars.tfree[b]), (uint32_t)((t >> 1) - 1) & 1u, a.err, &failed, true);
+        const uint32_t d_s = tmem + 256 * b, d_p = tmem + 256 * b + 128;
+        for (int c = 0; c < C::kChunks && !failed; ++c) {
+          const int j = t * C::kChunks + c, s = j % kStages1;
+          if (!mbar_wait(smem_u32(&bars.full[s]), (uint32_t)(j / kStages1) & 1u, a.err, &failed, true))
+            break;
           tc_fence_after();
+          const uint64_t bx = dx0 + (uint64_t)((s * C::kStage) >> 4);
 #pragma unroll
           for (int u = 0; u < 4; ++u)
-            umma_f16<2>(d_s, dq + (uint64_t)((c * kHeads * 128 + u * 32) >> 4),
-                        bx + (uint64_t)((c * kChunk + u * 32) >> 4), id, (c | u) != 0);
+            umma_f16<2>(d_s, bx + (uint64_t)((u * 32) >> 4),
+                        dq + (uint64_t)((c * kHeads * 128 + u * 32) >> 4), id, (c | u) != 0);
           if (c < C::kNope) {
 #pragma unroll
             for (int u = 0; u < 4; ++u)
-              umma_f16<2>(d_p, dd + (uint64_t)((c * kHeads * 128 + u * 32) >> 4),
-                          bx + (uint64_t)((c * kChunk + u * 32) >> 4), id, (c | u) != 0);
+              umma_f16<2>(d_p, bx + (uint64_t)((u * 32) >> 4),
+                          dd + (uint64_t)((c * kHeads * 128 + u * 32) >> 4), id, (c | u) != 0);
           }
-          umma_commit_pair(smem_u32(&bars.xe[s][c]), 3);
+          umma_commit_pair(smem_u32(&bars.empty[s]), 3);
         }
         if (failed) break;
-        umma_commit_pair(smem_u32(&bars.s_full[s]), 3);
+        umma_commit_pair(smem_u32(&bars.tfull[b]), 3);
       }
     }
     __syncwarp();
   } else {
-    // ---- elementwise: P, dS -> scratch (both CTAs) ----
-    const int q = warp & 3;
-    const int hrow = 32 * (q & 1) + lane;
-    const int half = q >> 1;
-    const int head = kHeads * (int)cta + hrow;
-    const bool hvalid = head < a.N1;
-    const uint32_t lane_addr = (uint32_t)(32 * q) << 16;
+    // ---- elementwise: thread = key (TMEM lane), 128 heads in the columns ----
+    const int qd = warp & 3;
+    const int kk = 32 * qd + lane;
+    const uint32_t lane_addr = (uint32_t)(32 * qd) << 16;
     const float c2 = a.scale * 1.4426950408889634f;
-    float off = 0.f, inv_sum = 1.f, delta = 0.f;
-    if (hvalid && ntiles > 0) {
-      const size_t hidx = (size_t)row * a.N1 + head;
-      off = __ldg(a.smax + hidx) * 1.4426950408889634f;
-      const float sm = __ldg(a.ssum + hidx);
-      inv_sum = 1.f / (sm > 0.f ? sm : 1.f);
-      delta = __ldg(a.delta + hidx);
-    }
-    const uint32_t lead_f0 = mapa_shared(smem_u32(&bars.s_free[0]), 0);
-    const uint32_t lead_f1 = mapa_shared(smem_u32(&bars.s_free[1]), 0);
-    T* ds_row = reinterpret_cast<T*>(a.ds) + ((size_t)row * kHeadsPad + head) * a.kp;
-    T* p_row = reinterpret_cast<T*>(a.pp) + ((size_t)row * kHeadsPad + head) * a.kp;
+    const uint32_t lead_f0 = mapa_shared(smem_u32(&bars.tfree[0]), 0);
+    const uint32_t lead_f1 = mapa_shared(smem_u32(&bars.tfree[1]), 0);
     for (int t = 0; t < ntiles; ++t) {
-      const int s = t & 1;
-      mbar_wait(smem_u32(&bars.s_full[s]), (t >> 1) & 1, a.err, &failed);
+      const int b = t & 1;
+      mbar_wait(smem_u32(&bars.tfull[b]), (uint32_t)(t >> 1) & 1u, a.err, &failed);
       const bool wfail = __any_sync(0xffffffffu, failed);
       tc_fence_after();
-      uint32_t sr[32], pr[32];
-      if (!wfail) {
-        tmem_ld32(tmem + lane_addr + 32 * s, sr);
-        tmem_ld32(tmem + lane_addr + 64 + 32 * s, pr);
-        tmem_ld_wait();
-      } else {
+      const int e = 2 * kKeys1 * t + kKeys1 * (int)cta + kk;   // key slot of the row
+      const bool valid = e < nvalid;
+      uint4* ds_row = reinterpret_cast<uint4*>(static_cast<T*>(a.ds) + ((size_t)row * a.kp + e) * kHeadsPad);
+      uint4* p_row = reinterpret_cast<uint4*>(static_cast<T*>(a.pp) + ((size_t)row * a.kp + e) * kHeadsPad);
+#pragma unroll 1
+      for (int h0 = 0; h0 < 128; h0 += 32) {
+        uint32_t sr[32], pr[32];
+        if (!wfail) {
+          tmem_ld32(tmem + lane_addr + 256 * b + h0, sr);
+          tmem_ld32(tmem + lane_addr + 256 * b + 128 + h0, pr);
+          tmem_ld_wait();
+        } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) sr[i] = pr[i] = 0u;
+          for (int i = 0; i < 32; ++i) sr[i] = pr[i] = 0u;
+        }
+        uint32_t pk_p[16], pk_s[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float p[2], g[2];
+#pragma unroll
+          for (int x = 0; x < 2; ++x) {
+            const int h = h0 + 2 * i + x;
+            const float pe = valid ? ex2(fmaf(__uint_as_float(sr[2 * i + x]), c2, -bars.mxl[h])) * bars.inv[h] : 0.f;
+            p[x] = pe;
+            g[x] = valid ? pe * (__uint_as_float(pr[2 * i + x]) - bars.dlt[h]) * a.scale : 0.f;
+          }
+          pk_p[i] = ElemTraits<T>::pack2(p[0], p[1]);
+          pk_s[i] = ElemTraits<T>::pack2(g[0], g[1]);
+        }
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          ds_row[h0 / 8 + v] = make_uint4(pk_s[4 * v], pk_s[4 * v + 1], pk_s[4 * v + 2], pk_s[4 * v + 3]);
+          p_row[h0 / 8 + v] = make_uint4(pk_p[4 * v], pk_p[4 * v + 1], pk_p[4 * v + 2], pk_p[4 * v + 3]);
+        }
       }
       tc_fence_before();
       named_bar(1, 128);
-      if (warp == 2 && lane == 0) mbar_arrive_cluster(s ? lead_f1 : lead_f0);
-      const int nv = min(kTile, nvalid - kTile * t) - kOwn * half;
-      uint32_t pk_p[16], pk_s[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        float p[2], g[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int k = 2 * i + e;
-          const bool v = hvalid && k < nv;
-          const float pe = v ? ex2(fmaf(__uint_as_float(sr[k]), c2, -off)) * inv_sum : 0.f;
-          p[e] = pe;
-          g[e] = v ? pe * (__uint_as_float(pr[k]) - delta) * a.scale : 0.f;
-        }
-        pk_p[i] = ElemTraits<T>::pack2(p[0], p[1]);
-        pk_s[i] = ElemTraits<T>::pack2(g[0], g[1]);
-      }
-      const int kcol = kTile * t + kOwn * half;
-      uint4* dst_s = reinterpret_cast<uint4*>(ds_row + kcol);
-      uint4* dst_p = reinterpret_cast<uint4*>(p_row + kcol);
-#pragma unroll
-      for (int v = 0; v < 4; ++v) {
-        dst_s[v] = make_uint4(pk_s[4 * v], pk_s[4 * v + 1], pk_s[4 * v + 2], pk_s[4 * v + 3]);
-        dst_p[v] = make_uint4(pk_p[4 * v], pk_p[4 * v + 1], pk_p[4 * v + 2], pk_p[4 * v + 3]);
-      }
+      if (warp == 2 && lane == 0) mbar_arrive_cluster(b ? lead_f1 : lead_f0);
     }
   }
   tc_fence_before();
   __syncthreads();
   cluster_sync();
-  if (warp == 1) tmem_dealloc<2>(tmem, 128);
+  if (warp == 1) tmem_dealloc<2>(tmem, 512);
 }
 
 // =====================================================================================
@@ -412,8 +421,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
         if (!mbar_wait(smem_u32(&bars.a_empty[s]), ((t >> 1) & 1) ^ 1, a.err, &failed)) break;
         const uint32_t lead = mapa_shared(smem_u32(&bars.a_full[s]), 0);
         if (cta == 0) mbar_arrive_expect_tx(smem_u32(&bars.a_full[s]), 2 * C::kABytes);
-        tma_load_2d_pair(sA + s * C::kABytes, &maps.ds, lead, kTile * t,
-                         row * kHeadsPad + kHeads * (int)cta);
+        // key-major scratch: box of 64 heads (this CTA's) x 64 keys -> A is MN-major
+        tma_load_2d_pair(sA + s * C::kABytes, &maps.ds, lead, kHeads * (int)cta,
+                         row * a.kp + kTile * t);
       }
     }
     __syncwarp();
@@ -453,9 +463,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
   } else if (warp == 1) {
     if (cta == 0 && ntiles > 0 && lane == 0) {
       const bool bf16 = ElemTraits<T>::kIsBf16;
-      const uint32_t id_n = idesc_f16(128, C::kNPV, bf16, false, true);
-      const uint32_t id_r = idesc_f16(128, 128, bf16, false, true);
-      const uint64_t da0 = smem_desc_sw128(sA, 16, 1024), da1 = smem_desc_sw128(sA + C::kABytes, 16, 1024);
+      const uint32_t id_n = idesc_f16(128, C::kNPV, bf16, true, true);
+      const uint32_t id_r = idesc_f16(128, 128, bf16, true, true);
+      const uint64_t da0 = smem_desc_sw128(sA, kHeads * 128, 1024);
+      const uint64_t da1 = smem_desc_sw128(sA + C::kABytes, kHeads * 128, 1024);
       const uint64_t dh0 = smem_desc_sw128(sH, kChunk, 1024);
       const uint64_t dh1 = smem_desc_sw128(sH + C::kHBytes, kChunk, 1024);
       for (int t = 0; t < ntiles && !failed; ++t) {
@@ -469,14 +480,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
         for (int j = 0; j < C::kNumPV; ++j)
 #pragma unroll
           for (int k = 0; k < kTile / 16; ++k)
-            umma_f16<2>(tmem + j * (C::kNPV / 2), ba + (uint64_t)((k * 32) >> 4),
+            umma_f16<2>(tmem + j * (C::kNPV / 2), ba + (uint64_t)((k * 2048) >> 4),
                         bh + (uint64_t)(((k >> 1) * C::kHHalf + j * C::kCpj * kChunk + (k & 1) * 2048) >> 4),
                         id_n, (t | k) != 0);
         // rope: N=128 with the leader's B half holding the 64 rope dims; the other half
         // is never read back (it lands in TMEM lanes 64-127)
 #pragma unroll
         for (int k = 0; k < kTile / 16; ++k)
-          umma_f16<2>(tmem + C::kTmemRope, ba + (uint64_t)((k * 32) >> 4),
+          umma_f16<2>(tmem + C::kTmemRope, ba + (uint64_t)((k * 2048) >> 4),
                       bh + (uint64_t)((C::kHNope + k * 2048) >> 4), id_r, (t | k) != 0);
         umma_commit_pair(smem_u32(&bars.a_empty[s]), 3);
         umma_commit_pair(smem_u32(&bars.h_empty[s]), 3);
@@ -571,7 +582,7 @@ struct Cfg3 {
   static constexpr int kW = D < 256 ? D : 256;           // output columns per part
   static constexpr int kDParts = D / kW;
   static constexpr int kParts = 2 * kDParts + 1;
-  static constexpr int kATile = kHeadsPad * kKeyTile3 * 2; // 128 heads x 128 keys, MN-major
+  static constexpr int kATile = kHeadsPad * kKeyTile3 * 2; // 128 keys x 128 heads, K-major
   static constexpr int kBChunk = kHeadsPad * 128;          // 64 columns x 128 heads
   static constexpr int kOffA = 0;
   static constexpr int kOffB = 2 * kATile;
@@ -687,13 +698,13 @@ __global__ void __launch_bounds__(kThreads3, 1)
     if (lane == 0) {
       const CUtensorMap* am = is_dv ? &maps.pp : &maps.ds;
       const CUtensorMap* bm = rope ? &maps.qr : is_dv ? &maps.dout : &maps.q;
-      const int hrow0 = row * kHeadsPad;
+      const int krow0 = row * a.kp;   // first scratch row (key slot) of this query row
       auto load_a = [&](int t, int s) {
         const uint32_t fb = smem_u32(&bars.a_full[s]);
         mbar_arrive_expect_tx(fb, C::kATile);
-        for (int c = 0; c < 2; ++c)   // keys [64c, 64c+64) of the tile, all 128 heads
-          tma_load_2d(sA + s * C::kATile + c * kHeadsPad * 128, am, fb,
-                      t * kKeyTile3 + 64 * c, hrow0);
+        for (int c = 0; c < 2; ++c)   // heads [64c, 64c+64) of the tile's 128 keys
+          tma_load_2d(sA + s * C::kATile + c * kKeyTile3 * 128, am, fb, 64 * c,
+                      krow0 + t * kKeyTile3);
       };
       {
         const uint32_t fb = smem_u32(&bars.b_full);
@@ -704,7 +715,7 @@ __global__ void __launch_bounds__(kThreads3, 1)
       int loaded = 0, consumed = 0, issued = 0;
       for (; loaded < 2 && loaded < ntiles; ++loaded) load_a(loaded, loaded);
       const bool bf16 = ElemTraits<T>::kIsBf16;
-      const uint32_t id = idesc_f16(128, W, bf16, true, true);
+      const uint32_t id = idesc_f16(128, W, bf16, false, true);
       const uint64_t db = smem_desc_sw128(sB, C::kBChunk, 1024);
       bool b_ready = mbar_wait(smem_u32(&bars.b_full), 0, a.err, &failed);
       for (int t = 0; t < ntiles && b_ready; ++t) {
@@ -714,9 +725,10 @@ __global__ void __launch_bounds__(kThreads3, 1)
         ++consumed;
         if (!mbar_wait(smem_u32(&bars.t_empty[s]), ph ^ 1u, a.err, &failed)) break;
         tc_fence_after();
-        const uint64_t da = smem_desc_sw128(sA + s * C::kATile, kHeadsPad * 128, 1024);
-        for (int k = 0; k < kHeadsPad / 16; ++k)
-          umma_f16<1>(tmem + s * 256, da + (uint64_t)((k * 2048) >> 4),
+        const uint64_t da = smem_desc_sw128(sA + s * C::kATile, 16, 1024);
+        for (int k = 0; k < kHeadsPad / 16; ++k)   // K = heads: 4 steps per 64-head chunk
+          umma_f16<1>(tmem + s * 256,
+                      da + (uint64_t)(((k >> 2) * kKeyTile3 * 128 + (k & 3) * 32) >> 4),
                       db + (uint64_t)((k * 2048) >> 4), id, k != 0);
         umma_commit(smem_u32(&bars.t_full[s]));
         umma_commit(smem_u32(&bars.a_empty[s]));
@@ -802,7 +814,8 @@ int cast_all(const DsaSfaBwdParams* p, cudaStream_t stream) {
   return cudaGetLastError() == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
 }
 
-inline int64_t padded_keys(int64_t nent) { return (nent + kKeyTile3 - 1) / kKeyTile3 * kKeyTile3; }
+// key slots per row in the P / dS scratch: whole K1 pair tiles (256 keys)
+inline int64_t padded_keys(int64_t nent) { return (nent + 255) / 256 * 256; }
 inline int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 
 template <int D, typename T>
@@ -856,17 +869,17 @@ int launch(const DsaSfaBwdParams* p, cudaStream_t stream) {
   Maps1 m1;
   Maps2 m2;
   Maps3 m3;
-  const uint64_t srows = (uint64_t)p->num_rows * kHeadsPad;
+  const uint64_t krows_s = (uint64_t)p->num_rows * kp;   // scratch rows: one per key slot
   if (!make_tmap_2d_16b(&m1.q, p->q, bf16, qrows, D, (uint64_t)D * 2, 64, 64) ||
       !make_tmap_2d_16b(&m1.qr, p->q_rope, bf16, qrows, 64, 128, 64, 64) ||
       !make_tmap_2d_16b(&m1.dout, p->d_out, bf16, qrows, D, (uint64_t)D * 2, 64, 64) ||
       !make_tmap_2d_16b(&m1.k, p->key, bf16, p->kv_rows, D, (uint64_t)D * 2, 64, 1) ||
       !make_tmap_2d_16b(&m1.kr, p->key_rope, bf16, p->kv_rows, 64, 128, 64, 1) ||
-      !make_tmap_2d_16b(&m2.ds, a.ds, bf16, srows, kp, kp * 2, 64, 64) ||
+      !make_tmap_2d_16b(&m2.ds, a.ds, bf16, krows_s, kHeadsPad, kHeadsPad * 2, 64, 64) ||
       !make_tmap_2d_16b(&m2.k, p->key, bf16, p->kv_rows, D, (uint64_t)D * 2, 64, 1) ||
       !make_tmap_2d_16b(&m2.kr, p->key_rope, bf16, p->kv_rows, 64, 128, 64, 1) ||
-      !make_tmap_2d_16b(&m3.ds, a.ds, bf16, srows, kp, kp * 2, 64, 128) ||
-      !make_tmap_2d_16b(&m3.pp, a.pp, bf16, srows, kp, kp * 2, 64, 128) ||
+      !make_tmap_2d_16b(&m3.ds, a.ds, bf16, krows_s, kHeadsPad, kHeadsPad * 2, 64, 128) ||
+      !make_tmap_2d_16b(&m3.pp, a.pp, bf16, krows_s, kHeadsPad, kHeadsPad * 2, 64, 128) ||
       !make_tmap_2d_16b(&m3.q, p->q, bf16, qrows, D, (uint64_t)D * 2, 64, 128) ||
       !make_tmap_2d_16b(&m3.qr, p->q_rope, bf16, qrows, 64, 128, 64, 128) ||
       !make_tmap_2d_16b(&m3.dout, p->d_out, bf16, qrows, D, (uint64_t)D * 2, 64, 128))

@@ -187,7 +187,7 @@ int dsa_sfa_bwd(const DsaSfaBwdParams* params, void* stream);
 int dsa_sfa_bwd_cast(const DsaSfaBwdParams* params, void* stream);
 
 /* Workspace of dsa_sfa_bwd: compacted key rows and counts, bf16/fp16 scratch for P and
- * dS ([num_rows][128][keys padded to 128] each) and fp32 rowsum(dO * O) per (row, head)
+ * dS ([num_rows][keys padded to 256][128 heads] each) and fp32 rowsum(dO * O) per (row, head)
  * ([num_rows][128]).  Returns -1 for invalid sizes. */
 int64_t dsa_sfa_bwd_workspace_size(int64_t num_rows, int64_t topk, int64_t sparse_block_size);
 
