@@ -11,15 +11,16 @@
 //
 // Four kernels (the per-query working set -- Q, dO, dQ, 128 heads x 576 dims -- does not
 // fit one SM, and the dK/dV products need the heads as their reduction dimension):
-//   K1 probs : CTA pair per query row (as the forward): S = Q K^T, dP = dO V^T on
-//              tcgen05 (2-SM, heads split 64/64), then P and dS -> bf16 scratch.
+//   K1 probs : CTA pair per query row: S^T = K Q^T and dP^T = V dO^T on tcgen05 (2-SM,
+//              M = 256 keys, 128 per CTA, N = 128 heads; one gathered key chunk feeds
+//              both products), then P and dS -> key-major bf16 scratch [row][key][head].
 //   K2 dq    : CTA pair per query row: dQ = dS K (nope dims split across the pair like
 //              the forward's P V; rope dims on a padded N=128 MMA).
-//   K3 dkv   : one CTA per (query row, column part), looping over the row's 128-key
-//              tiles: dK = dS^T Q, dV = P^T dO, dKr = dS^T Qr on tcgen05 (M = 128 keys,
-//              K = 128 heads), double-buffered in TMEM and drained into fp32
-//              accumulators with coalesced vector reductions (red.global.add.v4.f32),
-//              the scatter-add of the reference (:289-300).
+//   K3 dkv   : persistent; work items (query row, column part) walk the row's 128-key
+//              tiles: dK^T = Q^T dS^T, dV^T = dO^T P^T, dKr^T = Qr^T dS^T on tcgen05
+//              (M = 128 output columns, N = 128 keys, K = 128 heads), double-buffered in
+//              TMEM and drained into fp32 accumulators with whole-row vector reductions
+//              (red.global.add.v2.f32), the scatter-add of the reference (:289-300).
 //   K4 cast  : fp32 accumulators -> key dtype (separate entry point so a multi-GPU
 //              caller can all-reduce the fp32 accumulators first).
 
@@ -566,29 +567,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
 // =====================================================================================
 // K3: dK = dS^T Q, dV = P^T dO, dKr = dS^T Qr  (scatter-add into fp32)
 // =====================================================================================
-// One CTA per (query row, part); it walks the row's 128-key tiles. Parts split the output
-// columns so that a CTA's B operand (the row's Q / dO / Qr columns, K = 128 heads) stays
-// resident: for D = 512, parts 0-1 are dK columns [0,256) and [256,512) (A = dS, B = Q),
-// parts 2-3 the same columns of dV (A = P, B = dO) and part 4 is dKr (A = dS, B = Qr).
-// The parts of one row are adjacent in the grid, so they run together and their dS / P
-// tile reads hit L2. Per tile: warp 0 (one lane) streams the A tiles through a 2-stage TMA
-// ring and issues M=128 (keys) x N=W MMAs into one of two TMEM buffers; 16 drain warps
-// (4 per TMEM lane quadrant, each owning W/4 columns) move the finished buffer through a
-// shared-memory transpose into red.global.add.v4.f32 while the next tile's MMAs run. The
-// reductions are the bound (4352 bytes per valid pair at D=512), and one SM needs about 16
-// warps in flight to keep its share of the L2 reduction rate.
+// Work items are (query row, part) pairs.  Parts split the output columns so that a part's
+// slice of the row's Q / dO / Qr (K = 128 heads) is loaded once per item: for D = 512,
+// parts 0-1 are dK columns [0,256) and [256,512) (Q slice, dS tiles), parts 2-3 the same
+// columns of dV (dO slice, P tiles) and part 4 is dKr (Qr, dS tiles).  The kernel is
+// persistent (one CTA per SM, items strided by the grid; the parts of one row are
+// adjacent items, so they run together and their dS / P tiles are read from L2).
+//
+// Per 128-key tile it computes the transposed products, dK^T = Q^T dS^T and so on:
+// M = 128 output columns (TMEM lanes), N = 128 keys (TMEM columns), K = 128 heads.  With
+// one output column per lane, a warp holds 32 consecutive columns of every key; one
+// shuffle per key pair turns that into two whole 128-byte rows per
+// red.global.add.v2.f32 (even lanes carry key 2j, odd lanes key 2j+1).  That reduction
+// form runs at the L2 reduction ceiling, and no shared-memory transpose is needed.
+// The reductions are the bound (4352 bytes per valid pair at D = 512).
+//
+// Roles: warp 0 (one lane) loads the item slices into two slots and the dS / P tiles
+// through a 3-stage ring, so the next item's slice arrives while the current item's last
+// tiles run; warp 1 (one lane) issues the MMAs into two TMEM buffers; warps 2-17 drain
+// a finished buffer (4 warps per TMEM lane quadrant, each owning a quarter of its columns)
+// while the MMAs of the next tile run.
+constexpr int kStages3 = 3;
+
 template <int D>
 struct Cfg3 {
-  static constexpr int kW = D < 256 ? D : 256;           // output columns per part
+  static constexpr int kW = D < 256 ? D : 256;              // output columns per part
   static constexpr int kDParts = D / kW;
   static constexpr int kParts = 2 * kDParts + 1;
-  static constexpr int kATile = kHeadsPad * kKeyTile3 * 2; // 128 keys x 128 heads, K-major
-  static constexpr int kBChunk = kHeadsPad * 128;          // 64 columns x 128 heads
+  static constexpr int kBox = 128 * 128;                    // 64 columns x 128 heads, MN-major
+  static constexpr int kSlice = (kW / 64) * kBox;           // one slot: a part's slice
+  static constexpr int kTileB = kHeadsPad * kKeyTile3 * 2;  // 128 keys x 128 heads, K-major
   static constexpr int kOffA = 0;
-  static constexpr int kOffB = 2 * kATile;
-  static constexpr int kOffStage = kOffB + (kW / 64) * kBChunk;
-  static constexpr int kStageWarp = 32 * 33 * 4;
-  static constexpr int kOffBars = kOffStage + 16 * kStageWarp;
+  static constexpr int kOffB = 2 * kSlice;
+  static constexpr int kOffBars = kOffB + kStages3 * kTileB;
 };
 
 struct Maps3 {
@@ -596,53 +607,74 @@ struct Maps3 {
 };
 
 struct __align__(16) Bars3 {
-  uint64_t b_full;
   uint64_t a_full[2], a_empty[2];
+  uint64_t b_full[kStages3], b_empty[kStages3];
   uint64_t t_full[2], t_empty[2];
   uint32_t tmem_slot;
 };
 
-constexpr int kThreads3 = 17 * 32;   // warp 0: TMA + MMA; warps 1-16: drain
+constexpr int kThreads3 = 18 * 32;   // warp 0: TMA, 1: MMA, 2-17: drain
 
-// One drain warp's share of a finished K3 tile: its 32 keys (TMEM lanes) x CW columns.
-// The columns are read into registers first and the TMEM buffer released at once, then
-// staged through shared memory (row stride 33 floats, conflict-free both ways) so that each
-// reduction instruction covers whole 128-byte (CW >= 32) or 64-byte (CW = 16) row pieces.
-template <int CW>
-__device__ __forceinline__ void dkv_drain(uint32_t taddr, uint32_t t_empty, float* stage,
-                                          float* gbase, int ld, int my_row, int lane) {
-  uint32_t r[CW];
-  if constexpr (CW >= 32) {
-    tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-    if constexpr (CW == 64) tmem_ld32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
-  } else {
-    tmem_ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
-  }
-  tmem_ld_wait();
-  tc_fence_before();
-  __syncwarp();
-  if (lane == 0) mbar_arrive(t_empty);
-  constexpr int kN = CW < 32 ? CW : 32;   // columns per staging pass
-  constexpr int kLpk = kN / 4;            // lanes per key in one instruction
-  constexpr int kKpi = 32 / kLpk;         // keys per instruction
+// One K3 work item; every role walks the same sequence.
+struct Item3 {
+  int row, part, nvalid, ntiles;
+};
+
+template <int D>
+__device__ __forceinline__ Item3 item3(const Args& a, int it) {
+  Item3 x;
+  x.row = it / Cfg3<D>::kParts;
+  x.part = it % Cfg3<D>::kParts;
+  const RowInfo ri = row_info(a, x.row);
+  x.nvalid = ri.active ? __ldg(a.ws_count + x.row) : 0;
+  x.ntiles = (x.nvalid + kKeyTile3 - 1) / kKeyTile3;
+  return x;
+}
+
+// One drain warp's share of a finished tile: NK keys (TMEM columns) x 32 output columns
+// (its TMEM lanes), read 16 keys at a time; the buffer is released after the last read
+// (the MMAs of the next tile go to the other buffer, and the drain is the slower side).
+// Lane l holds column c0 + l of every key; for keys (2j, 2j+1) the lanes swap one value
+// with their neighbour so that even lanes hold columns (l, l+1) of key 2j and odd lanes
+// columns (l-1, l) of key 2j+1: each red.v2 then covers two whole 128-byte rows.
+// rows[i]: accumulator row of key 32i + l of the share (-1 = no key).
+template <int NK>
+__device__ __forceinline__ void dkv_drain(uint32_t taddr, uint32_t t_empty, bool lanes_ok,
+                                          float* gcol, int ld, const int (&rows)[NK / 32],
+                                          int lane) {
+  const int odd = lane & 1;
 #pragma unroll
-  for (int c0 = 0; c0 < CW; c0 += kN) {
+  for (int h = 0; h < NK / 16; ++h) {
+    uint32_t r[16];
+    if (lanes_ok) {
+      tmem_ld16(taddr + 16 * h, r);
+      tmem_ld_wait();
+    }
+    if (h == NK / 16 - 1) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(t_empty);
+    }
+    if (!lanes_ok) continue;
+    // all exchanges first (independent shuffles in flight), then the reductions back to back
+    int dst_row[8];
 #pragma unroll
-    for (int i = 0; i < kN; ++i) stage[lane * 33 + i] = __uint_as_float(r[c0 + i]);
-    __syncwarp();
+    for (int j = 0; j < 8; ++j) {
+      const float x0 = __uint_as_float(r[2 * j]), x1 = __uint_as_float(r[2 * j + 1]);
+      const float recv = __shfl_xor_sync(0xffffffffu, odd ? x0 : x1, 1);
+      r[2 * j] = __float_as_uint(odd ? recv : x0);
+      r[2 * j + 1] = __float_as_uint(odd ? x1 : recv);
+      dst_row[j] = __shfl_sync(0xffffffffu, rows[h >> 1], 16 * (h & 1) + 2 * j + odd);
+    }
 #pragma unroll
-    for (int it = 0; it < 32 / kKpi; ++it) {
-      const int kr = kKpi * it + lane / kLpk, cc = 4 * (lane % kLpk);
-      const int dst_row = __shfl_sync(0xffffffffu, my_row, kr);
-      if (dst_row >= 0) {
-        const float* sp = stage + kr * 33 + cc;
-        float* gp = gbase + (size_t)dst_row * ld + c0 + cc;
-        asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(gp), "f"(sp[0]),
-                     "f"(sp[1]), "f"(sp[2]), "f"(sp[3])
+    for (int j = 0; j < 8; ++j) {
+      if (dst_row[j] >= 0) {
+        float* gp = gcol + (size_t)dst_row[j] * ld;
+        asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(gp),
+                     "f"(__uint_as_float(r[2 * j])), "f"(__uint_as_float(r[2 * j + 1]))
                      : "memory");
       }
     }
-    __syncwarp();
   }
 }
 
@@ -655,36 +687,28 @@ __global__ void __launch_bounds__(kThreads3, 1)
   const uint32_t sbase = smem_u32(smem_raw);
   const uint32_t sA = sbase + C::kOffA, sB = sbase + C::kOffB;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x / C::kParts;
-  const int part = blockIdx.x % C::kParts;
   if (sbase & 1023u) {
     if (threadIdx.x == 0) report_error(a.err, kErrMisaligned);
     return;
   }
-  const RowInfo ri = row_info(a, row);
+  // uniform across the CTA: an error flagged by an earlier kernel skips the work
   const bool abort = a.err != nullptr && *reinterpret_cast<volatile int*>(a.err) != 0;
-  const int nvalid = (ri.active && !abort) ? __ldg(a.ws_count + row) : 0;
-  const int ntiles = (nvalid + kKeyTile3 - 1) / kKeyTile3;
-  if (ntiles == 0) return;   // uniform across the CTA
-
-  const bool rope = part == 2 * C::kDParts;
-  const bool is_dv = !rope && part >= C::kDParts;
-  const int W = rope ? 64 : C::kW;                         // columns of this part
-  const int col0 = rope ? 0 : (part % C::kDParts) * C::kW;  // first output column
-  float* acc = rope ? a.dkr_acc : is_dv ? a.dv_acc : a.dk_acc;
-  const int ld = rope ? 64 : D;
+  const int nitems = abort ? 0 : a.num_rows * C::kParts;
 
   if (threadIdx.x == 0) {
-    mbar_init(smem_u32(&bars.b_full), 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(smem_u32(&bars.a_full[s]), 1);
       mbar_init(smem_u32(&bars.a_empty[s]), 1);
       mbar_init(smem_u32(&bars.t_full[s]), 1);
       mbar_init(smem_u32(&bars.t_empty[s]), 16);
     }
+    for (int s = 0; s < kStages3; ++s) {
+      mbar_init(smem_u32(&bars.b_full[s]), 1);
+      mbar_init(smem_u32(&bars.b_empty[s]), 1);
+    }
     fence_mbarrier_init();
   }
-  if (warp == 0) {
+  if (warp == 1) {
     tmem_alloc<1>(smem_u32(&bars.tmem_slot), 512);
     tmem_relinquish<1>();
   }
@@ -695,91 +719,138 @@ __global__ void __launch_bounds__(kThreads3, 1)
   bool failed = false;
 
   if (warp == 0) {
+    // ---- TMA: item slices (2 slots), dS / P tiles (ring) ----
     if (lane == 0) {
-      const CUtensorMap* am = is_dv ? &maps.pp : &maps.ds;
-      const CUtensorMap* bm = rope ? &maps.qr : is_dv ? &maps.dout : &maps.q;
-      const int krow0 = row * a.kp;   // first scratch row (key slot) of this query row
-      auto load_a = [&](int t, int s) {
-        const uint32_t fb = smem_u32(&bars.a_full[s]);
-        mbar_arrive_expect_tx(fb, C::kATile);
-        for (int c = 0; c < 2; ++c)   // heads [64c, 64c+64) of the tile's 128 keys
-          tma_load_2d(sA + s * C::kATile + c * kKeyTile3 * 128, am, fb, 64 * c,
-                      krow0 + t * kKeyTile3);
-      };
-      {
-        const uint32_t fb = smem_u32(&bars.b_full);
-        mbar_arrive_expect_tx(fb, (W / 64) * C::kBChunk);
-        for (int c = 0; c < W / 64; ++c)
-          tma_load_2d(sB + c * C::kBChunk, bm, fb, col0 + 64 * c, row * a.N1);
-      }
-      int loaded = 0, consumed = 0, issued = 0;
-      for (; loaded < 2 && loaded < ntiles; ++loaded) load_a(loaded, loaded);
-      const bool bf16 = ElemTraits<T>::kIsBf16;
-      const uint32_t id = idesc_f16(128, W, bf16, false, true);
-      const uint64_t db = smem_desc_sw128(sB, C::kBChunk, 1024);
-      bool b_ready = mbar_wait(smem_u32(&bars.b_full), 0, a.err, &failed);
-      for (int t = 0; t < ntiles && b_ready; ++t) {
-        const int s = t & 1;
-        const uint32_t ph = (uint32_t)(t >> 1) & 1u;
-        if (!mbar_wait(smem_u32(&bars.a_full[s]), ph, a.err, &failed)) break;
-        ++consumed;
-        if (!mbar_wait(smem_u32(&bars.t_empty[s]), ph ^ 1u, a.err, &failed)) break;
-        tc_fence_after();
-        const uint64_t da = smem_desc_sw128(sA + s * C::kATile, 16, 1024);
-        for (int k = 0; k < kHeadsPad / 16; ++k)   // K = heads: 4 steps per 64-head chunk
-          umma_f16<1>(tmem + s * 256,
-                      da + (uint64_t)(((k >> 2) * kKeyTile3 * 128 + (k & 3) * 32) >> 4),
-                      db + (uint64_t)((k * 2048) >> 4), id, k != 0);
-        umma_commit(smem_u32(&bars.t_full[s]));
-        umma_commit(smem_u32(&bars.a_empty[s]));
-        ++issued;
-        if (t + 2 < ntiles) {
-          if (!mbar_wait(smem_u32(&bars.a_empty[s]), ph, a.err, &failed)) break;
-          load_a(t + 2, s);
-          ++loaded;
+      int na = 0, nb = 0;
+      for (int it = blockIdx.x; it < nitems && !failed; it += gridDim.x) {
+        const Item3 x = item3<D>(a, it);
+        if (x.ntiles == 0) continue;
+        const bool rope = x.part == 2 * C::kDParts;
+        const bool is_dv = !rope && x.part >= C::kDParts;
+        const CUtensorMap* am = rope ? &maps.qr : is_dv ? &maps.dout : &maps.q;
+        const CUtensorMap* bm = is_dv ? &maps.pp : &maps.ds;
+        const int col0 = rope ? 0 : (x.part % C::kDParts) * C::kW;
+        const int nbox = rope ? 1 : C::kW / 64;
+        {
+          const int ab = na & 1;
+          if (!mbar_wait_sleep(smem_u32(&bars.a_empty[ab]), ((na >> 1) & 1) ^ 1, a.err, &failed)) break;
+          const uint32_t fb = smem_u32(&bars.a_full[ab]);
+          mbar_arrive_expect_tx(fb, nbox * C::kBox);
+          for (int c = 0; c < nbox; ++c)
+            tma_load_2d(sA + ab * C::kSlice + c * C::kBox, am, fb, col0 + 64 * c, x.row * a.N1);
+          ++na;
+        }
+        const int krow0 = x.row * a.kp;   // first scratch row (key slot) of this query row
+        for (int t = 0; t < x.ntiles; ++t) {
+          const int s = nb % kStages3;
+          if (!mbar_wait_sleep(smem_u32(&bars.b_empty[s]), ((nb / kStages3) & 1) ^ 1, a.err, &failed))
+            break;
+          const uint32_t fb = smem_u32(&bars.b_full[s]);
+          mbar_arrive_expect_tx(fb, C::kTileB);
+          for (int c = 0; c < 2; ++c)   // heads [64c, 64c+64) of the tile's 128 keys
+            tma_load_2d(sB + s * C::kTileB + c * kKeyTile3 * 128, bm, fb, 64 * c,
+                        krow0 + t * kKeyTile3);
+          ++nb;
         }
       }
-      // on a failure, let the copies and MMAs already in flight land before the exit
+      // on a failure, let the copies already issued land before the exit
       if (failed) {
         bool f2 = false;
-        for (int t = consumed; t < loaded; ++t)
-          mbar_wait(smem_u32(&bars.a_full[t & 1]), (uint32_t)(t >> 1) & 1u, a.err, &f2);
-        if (issued > 0)
-          mbar_wait(smem_u32(&bars.t_full[(issued - 1) & 1]), (uint32_t)((issued - 1) >> 1) & 1u,
-                    a.err, &f2);
-        if (!b_ready) mbar_wait(smem_u32(&bars.b_full), 0, a.err, &f2);
+        for (int i = na > 2 ? na - 2 : 0; i < na; ++i)
+          mbar_wait(smem_u32(&bars.a_full[i & 1]), (i >> 1) & 1, a.err, &f2);
+        for (int i = nb > kStages3 ? nb - kStages3 : 0; i < nb; ++i)
+          mbar_wait(smem_u32(&bars.b_full[i % kStages3]), (i / kStages3) & 1, a.err, &f2);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---- MMA: per tile and 128-column block, 8 K-steps of 16 heads ----
+    if (lane == 0) {
+      const bool bf16 = ElemTraits<T>::kIsBf16;
+      const uint32_t id = idesc_f16(128, kKeyTile3, bf16, true, false);
+      int na = 0, nb = 0, nt = 0;
+      for (int it = blockIdx.x; it < nitems && !failed; it += gridDim.x) {
+        const Item3 x = item3<D>(a, it);
+        if (x.ntiles == 0) continue;
+        const bool rope = x.part == 2 * C::kDParts;
+        const int nblk = rope ? 1 : C::kW / 128;
+        const int ab = na & 1;
+        if (!mbar_wait_sleep(smem_u32(&bars.a_full[ab]), (na >> 1) & 1, a.err, &failed)) break;
+        for (int t = 0; t < x.ntiles; ++t) {
+          const int s = nb % kStages3, tb = nt & 1;
+          if (!mbar_wait_sleep(smem_u32(&bars.b_full[s]), (nb / kStages3) & 1, a.err, &failed)) break;
+          if (!mbar_wait_sleep(smem_u32(&bars.t_empty[tb]), ((nt >> 1) & 1) ^ 1, a.err, &failed)) break;
+          tc_fence_after();
+          const uint64_t db = smem_desc_sw128(sB + s * C::kTileB, 16, 1024);
+          for (int m = 0; m < nblk; ++m) {
+            // A: columns [128m, 128m+128) = two 64-column boxes (lbo = box stride); the
+            // rope part has one box, and lanes 64-127 of its result are never read
+            const uint64_t da = smem_desc_sw128(sA + ab * C::kSlice + 2 * m * C::kBox, C::kBox, 1024);
+#pragma unroll
+            for (int k = 0; k < kHeadsPad / 16; ++k)
+              umma_f16<1>(tmem + tb * 256 + m * 128, da + (uint64_t)((k * 2048) >> 4),
+                          db + (uint64_t)(((k >> 2) * kKeyTile3 * 128 + (k & 3) * 32) >> 4), id,
+                          k != 0);
+          }
+          umma_commit(smem_u32(&bars.t_full[tb]));
+          umma_commit(smem_u32(&bars.b_empty[s]));
+          ++nb;
+          ++nt;
+        }
+        if (failed) break;
+        umma_commit(smem_u32(&bars.a_empty[ab]));
+        ++na;
+      }
+      // the MMAs issued last complete before the exit (their TMEM is freed afterwards)
+      if (nt > 0) {
+        bool f2 = false;
+        mbar_wait(smem_u32(&bars.t_full[(nt - 1) & 1]), ((nt - 1) >> 1) & 1, a.err, &f2);
       }
     }
     __syncwarp();
   } else {
-    // ---- drain: TMEM row = key; vector reductions into the fp32 accumulator ----
-    const int q = warp & 3;                  // TMEM lane quadrant this warp may access
-    const int cg = (warp - 1) >> 2;          // column group 0..3
-    const int cw = W / 4;                    // 64 (W = 256), 32 (W = 128) or 16 (rope)
-    float* stage = reinterpret_cast<float*>(smem_raw + C::kOffStage) + (warp - 1) * 32 * 33;
-    const int32_t* rows = a.ws_rows + (size_t)row * a.topk * a.block;
-    for (int t = 0; t < ntiles; ++t) {
-      const int s = t & 1;
-      const uint32_t ph = (uint32_t)(t >> 1) & 1u;
-      const int my_key = t * kKeyTile3 + 32 * q + lane;
-      const int my_row = my_key < nvalid ? __ldg(rows + my_key) : -1;
-      mbar_wait(smem_u32(&bars.t_full[s]), ph, a.err, &failed);
-      if (__any_sync(0xffffffffu, failed)) break;
-      tc_fence_after();
-      const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + s * 256 + cg * cw;
-      float* gbase = acc + col0 + cg * cw;
-      const uint32_t t_empty = smem_u32(&bars.t_empty[s]);
-      if (cw == 64)
-        dkv_drain<64>(taddr, t_empty, stage, gbase, ld, my_row, lane);
-      else if (cw == 32)
-        dkv_drain<32>(taddr, t_empty, stage, gbase, ld, my_row, lane);
-      else
-        dkv_drain<16>(taddr, t_empty, stage, gbase, ld, my_row, lane);
+    // ---- drain: TMEM lane = output column, column = key; red.v2 into fp32 ----
+    const int q = warp & 3;            // TMEM lane quadrant this warp may access
+    const int cg = (warp - 2) >> 2;    // column group 0..3
+    int nt = 0;
+    for (int it = blockIdx.x; it < nitems; it += gridDim.x) {
+      const Item3 x = item3<D>(a, it);
+      if (x.ntiles == 0) continue;
+      const bool rope = x.part == 2 * C::kDParts;
+      const bool is_dv = !rope && x.part >= C::kDParts;
+      float* acc = rope ? a.dkr_acc : is_dv ? a.dv_acc : a.dk_acc;
+      const int ld = rope ? 64 : D;
+      const int col0 = rope ? 0 : (x.part % C::kDParts) * C::kW;
+      const int nk = rope ? 32 : C::kW / 4;   // keys of a tile per column group: 64 or 32
+      const int c_off = cg * nk;              // TMEM column of the share within a buffer
+      const int mblk = c_off >> 7, key0 = c_off & 127;
+      const bool lanes_ok = !rope || q < 2;   // rope: 64 output columns
+      float* gcol = acc + col0 + mblk * 128 + 32 * q + lane - (lane & 1);
+      const int32_t* rows = a.ws_rows + (size_t)x.row * a.topk * a.block;
+      for (int t = 0; t < x.ntiles; ++t) {
+        const int tb = nt & 1;
+        const int k0 = t * kKeyTile3 + key0;
+        int kr[2];
+        kr[0] = k0 + lane < x.nvalid ? __ldg(rows + k0 + lane) : -1;
+        kr[1] = nk == 64 && k0 + 32 + lane < x.nvalid ? __ldg(rows + k0 + 32 + lane) : -1;
+        mbar_wait(smem_u32(&bars.t_full[tb]), (nt >> 1) & 1, a.err, &failed);
+        if (__any_sync(0xffffffffu, failed)) break;
+        tc_fence_after();
+        const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + tb * 256 + c_off;
+        const uint32_t t_empty = smem_u32(&bars.t_empty[tb]);
+        if (nk == 64)
+          dkv_drain<64>(taddr, t_empty, lanes_ok, gcol, ld, kr, lane);
+        else
+          dkv_drain<32>(taddr, t_empty, lanes_ok, gcol, ld,
+                        *reinterpret_cast<const int(*)[1]>(&kr[0]), lane);
+        ++nt;
+      }
+      if (failed) break;
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc<1>(tmem, 512);
+  if (warp == 1) tmem_dealloc<1>(tmem, 512);
 }
 
 // =====================================================================================
@@ -812,6 +883,20 @@ int cast_all(const DsaSfaBwdParams* p, cudaStream_t stream) {
         src[i], static_cast<T*>(dst[i]), n[i]);
   }
   return cudaGetLastError() == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
+}
+
+// SMs of the current device (persistent K3 grid), cached per device
+inline int sm_count() {
+  static int cached[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1)
+      n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
 }
 
 // key slots per row in the P / dS scratch: whole K1 pair tiles (256 keys)
@@ -920,7 +1005,9 @@ int launch(const DsaSfaBwdParams* p, cudaStream_t stream) {
     const int smem = Cfg3<D>::kOffBars + (int)sizeof(Bars3);
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return DSA_ERR_CUDA;
-    k<<<dim3((unsigned)(p->num_rows * Cfg3<D>::kParts)), dim3(kThreads3), smem, stream>>>(m3, a);
+    const int64_t items = p->num_rows * Cfg3<D>::kParts;
+    const int grid = (int)(items < sm_count() ? items : sm_count());
+    k<<<dim3((unsigned)grid), dim3(kThreads3), smem, stream>>>(m3, a);
   }
   if (cudaGetLastError() != cudaSuccess) return DSA_ERR_CUDA;
   if (p->defer_cast) return DSA_OK;

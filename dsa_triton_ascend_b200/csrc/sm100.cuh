@@ -123,6 +123,25 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
   }
 }
 
+// Bounded wait with a sleep between polls, for a role thread that waits long (a producer
+// for a free slot, an MMA issuer for a drained buffer): polling at full rate would take
+// issue slots from the warps that do the work on the same scheduler.
+__device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity, int* err,
+                                                bool* failed, uint32_t sleep_ns = 128) {
+  if (*failed) return false;
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    __nanosleep(sleep_ns);
+    if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      report_error(err, kErrTimeout);
+      *failed = true;
+      return false;
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // cluster helpers
 // ---------------------------------------------------------------------------
