@@ -367,10 +367,12 @@ struct Maps2 {
 struct __align__(16) Bars2 {
   uint64_t a_full[2], a_empty[2], h_full[2], h_empty[2], done;
   uint32_t tmem_slot;
-  int rows_h[2][64];
 };
 
-constexpr int kThreads2 = 256;   // 0,6: V gathers, 1: MMA, 2-5: epilogue, 7: dS tiles
+constexpr int kGatherWarp0 = 6;
+constexpr int kGatherWarps = 10;
+constexpr int kThreads2 = 32 * (kGatherWarp0 + kGatherWarps);   // 0: dS tiles, 1: MMA,
+                                                                 // 2-5: epilogue, 6-15: gathers
 
 template <int D, typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
@@ -414,7 +416,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
   const uint32_t tmem = bars.tmem_slot;
   bool failed = false;
 
-  if (warp == 7) {
+  if (warp == 0) {
     // ---- dS tiles of this CTA's 64 heads ----
     if (lane == 0) {
       for (int t = 0; t < ntiles && !failed; ++t) {
@@ -428,37 +430,43 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
       }
     }
     __syncwarp();
-  } else if (warp == 0 || warp == 6) {
+  } else if (warp >= kGatherWarp0) {
     // ---- V slices of all 64 keys (+ rope of all keys in the leader), TMA gather4 ----
-    const int part = warp == 0 ? 0 : 1;
-    const int nitems = 16 * C::kSlots;
-    int* rows_h = bars.rows_h[part];
+    // Items: 16 key groups x kSlots chunks, then (leader) 16 rope groups; item i goes to
+    // gather warp i % kGatherWarps, lane i / kGatherWarps (at most 8 per warp: a thread
+    // issues one gather4 every ~100 cycles and the lanes of a warp take turns).
+    const int lw = warp - kGatherWarp0;
+    const int nitems = 16 * C::kSlots + (cta == 0 ? 16 : 0);
+    const int item = lw + kGatherWarps * lane;
+    const bool rope_item = item >= 16 * C::kSlots;
+    const int g = rope_item ? item - 16 * C::kSlots : item & 15;   // key group: keys 4g..4g+3
     const int filler = nvalid > 0 ? __ldg(rows) : 0;
-    auto fetch = [&](int j) { return j < nvalid ? __ldg(rows + j) : filler; };
+    uint32_t dst_off = C::kHNope + g * 512;
+    int x = 0;
+    if (!rope_item) {
+      const int sl = item >> 4;
+      const int j = sl / C::kCpj;
+      const int chunk = j * 2 * C::kCpj + (int)cta * C::kCpj + sl % C::kCpj;
+      dst_off = (g >> 3) * C::kHHalf + sl * kChunk + (g & 7) * 512;
+      x = 64 * chunk;
+    }
     for (int t = 0; t < ntiles && !failed; ++t) {
       const int s = t & 1;
+      int r[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int jj = kTile * t + 4 * g + e;
+        r[e] = item < nitems && jj < nvalid ? __ldg(rows + jj) : filler;
+      }
       mbar_wait(smem_u32(&bars.h_empty[s]), ((t >> 1) & 1) ^ 1, a.err, &failed);
       failed = __any_sync(0xffffffffu, failed);
       if (failed) break;
       const uint32_t lead = mapa_shared(smem_u32(&bars.h_full[s]), 0);
-      if (part == 0 && cta == 0 && lane == 0)
+      if (lw == 0 && cta == 0 && lane == 0)
         mbar_arrive_expect_tx(smem_u32(&bars.h_full[s]), 2 * C::kHNope + C::kRope);
-      rows_h[lane] = fetch(kTile * t + lane);
-      rows_h[lane + 32] = fetch(kTile * t + 32 + lane);
-      __syncwarp();
-      for (int item = part * (nitems / 2) + lane; item < (part + 1) * (nitems / 2); item += 32) {
-        const int g = item & 15, sl = item >> 4;
-        const int j = sl / C::kCpj;
-        const int chunk = j * 2 * C::kCpj + (int)cta * C::kCpj + sl % C::kCpj;
-        const uint32_t dst = sH + s * C::kHBytes + (g >> 3) * C::kHHalf + sl * kChunk + (g & 7) * 512;
-        tma_gather4_pair(dst, &maps.k, lead, 64 * chunk, rows_h[4 * g], rows_h[4 * g + 1],
-                         rows_h[4 * g + 2], rows_h[4 * g + 3]);
-      }
-      if (part == 1 && cta == 0 && lane < 16) {
-        const int g = lane;
-        tma_gather4_pair(sH + s * C::kHBytes + C::kHNope + g * 512, &maps.kr, lead, 0,
-                         rows_h[4 * g], rows_h[4 * g + 1], rows_h[4 * g + 2], rows_h[4 * g + 3]);
-      }
+      if (item < nitems)
+        tma_gather4_pair(sH + s * C::kHBytes + dst_off, rope_item ? &maps.kr : &maps.k, lead, x,
+                         r[0], r[1], r[2], r[3]);
       __syncwarp();
     }
   } else if (warp == 1) {

@@ -49,7 +49,10 @@ constexpr int kHeads = 64;         // heads per CTA
 constexpr int kChunkBytesX = kOwn * 128;     // one 64-dim chunk of 32 own keys
 constexpr int kChunkBytesH = kOwn * 128;     // one 64-dim chunk of 32 keys (a token half)
 constexpr int kLoadWarp0 = 7;
-constexpr int kLoadWarps = 4;                // TMA gather4 issuers (chunks c % 4 == w)
+// TMA gather4 issuers, one per 64-dim chunk: a thread issues one gather4 every ~100
+// cycles and the lanes of a warp take turns, so a stage is issued about as fast as one
+// warp issues its 8 gathers only when every chunk has its own warp
+constexpr int kLoadWarps = 9;
 constexpr int kCopyThreads = 64;             // warps 0 and 6
 constexpr int kThreads = 32 * (kLoadWarp0 + kLoadWarps);
 constexpr float kRescaleLog2 = 8.0f;         // lazy rescale threshold (log2 units)
@@ -236,7 +239,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= kLoadWarp0) {
     // ====== X loaders: own 32 keys x all dims for QK^T, TMA gather4 (4 keys x 128 B) ======
-    // warp w issues chunks c with c % 4 == w, lanes 0-7 the chunk's 8 gathers; the bytes
+    // warp w issues chunk w (D < 512: some warps idle), lanes 0-7 the chunk's 8 gathers; the bytes
     // of both CTAs are counted on the leader's x_full, so no thread waits for the data.
     const int wq = warp - kLoadWarp0;
     const int filler = nvalid > 0 ? __ldg(rows) : 0;
