@@ -143,7 +143,11 @@ struct __align__(16) Bars1 {
   float dlt[128];   // rowsum(dO * O)
 };
 
-constexpr int kThreads1 = 320;   // 0: Q/dO TMA, 1: MMA, 2-5: elementwise, 6-9: key gathers
+constexpr int kGatherWarp1 = 6;
+constexpr int kGatherWarps1 = 8;   // a thread issues one gather4 every ~100 cycles and the
+                                   // lanes of a warp take turns: 4 gathers per warp
+constexpr int kThreads1 = 32 * (kGatherWarp1 + kGatherWarps1);   // 0: Q/dO TMA, 1: MMA,
+                                                                 // 2-5: elementwise, 6-13: keys
 
 template <int D, typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads1, 1)
@@ -219,26 +223,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads1, 1)
         tma_load_2d_pair(sO + c * kHeads * 128, &maps.dout, lead, 64 * c, qrow0);
       }
     }
-  } else if (warp >= 6) {
+  } else if (warp >= kGatherWarp1) {
     // ---- the CTA's 128 keys of each tile, chunk by chunk (TMA gather4, 2-SM form):
-    // warp w gathers keys [32w, 32w+32), lanes 0-7 four rows each ----
-    const int w = warp - 6;
+    // warp w gathers keys [16w, 16w+16), lanes 0-3 four rows each ----
+    const int w = warp - kGatherWarp1;
     const int filler = nvalid > 0 ? __ldg(rows) : 0;
     int r4[4] = {0, 0, 0, 0};
     for (int j = 0; j < nsteps && !failed; ++j) {
       const int t = j / C::kChunks, c = j % C::kChunks, s = j % kStages1;
       if (c == 0) {
-        const int e = 2 * kKeys1 * t + kKeys1 * (int)cta + 32 * w + lane;
+        const int e = 2 * kKeys1 * t + kKeys1 * (int)cta + 16 * w + (lane & 15);
         const int my_row = e < nvalid ? __ldg(rows + e) : filler;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) r4[q] = __shfl_sync(0xffffffffu, my_row, 4 * (lane & 7) + q);
+        for (int q = 0; q < 4; ++q) r4[q] = __shfl_sync(0xffffffffu, my_row, 4 * (lane & 3) + q);
       }
       mbar_wait(smem_u32(&bars.empty[s]), ((j / kStages1) & 1) ^ 1, a.err, &failed);
       if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
       const uint32_t full = smem_u32(&bars.full[s]);
       if (cta == 0 && w == 0 && lane == 0) mbar_arrive_expect_tx(full, 2 * C::kStage);
-      if (lane < 8)
-        tma_gather4_pair(sX + s * C::kStage + (32 * w + 4 * lane) * 128,
+      if (lane < 4)
+        tma_gather4_pair(sX + s * C::kStage + (16 * w + 4 * lane) * 128,
                          c < C::kNope ? &maps.k : &maps.kr, mapa_shared(full, 0),
                          c < C::kNope ? 64 * c : 0, r4[0], r4[1], r4[2], r4[3]);
       __syncwarp();

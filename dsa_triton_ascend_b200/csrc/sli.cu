@@ -89,7 +89,11 @@ __device__ __forceinline__ int key_row_of(const Args& a, int b, int row, int e) 
 // =====================================================================================
 constexpr int kTKeys = 128;        // keys per CTA per tile (pair tile: 256)
 constexpr int kTStages = 6;        // ring of 64-dim key chunks
-constexpr int kTThreads = 320;     // 0: Q/stats, 1: MMA, 2-5: epilogue, 6-9: key gathers
+constexpr int kTGather0 = 6;
+constexpr int kTGathers = 8;       // a thread issues one gather4 every ~100 cycles and the
+                                   // lanes of a warp take turns: 4 gathers per warp
+constexpr int kTThreads = 32 * (kTGather0 + kTGathers);   // 0: Q/stats, 1: MMA,
+                                                          // 2-5: epilogue, 6-13: key gathers
 
 template <int D>
 struct TCfg {
@@ -176,27 +180,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTThreads, 1)
         tma_load_2d_pair(sQ + lane * 64 * 128, lane < C::kNope ? &maps.q : &maps.qr, lead,
                          lane < C::kNope ? 64 * lane : 0, qrow0);
     }
-  } else if (warp >= 6) {
+  } else if (warp >= kTGather0) {
     // the CTA's 128 keys of each tile, chunk by chunk, by TMA gather4 in the 2-SM form:
-    // warp w gathers keys [32w, 32w+32) (8 gathers of 4 rows), and the bytes of both CTAs
+    // warp w gathers keys [16w, 16w+16) (4 gathers of 4 rows), and the bytes of both CTAs
     // are counted on the leader's barrier, so no thread waits for the data
-    const int w = warp - 6;
+    const int w = warp - kTGather0;
     const int filler = n > 0 ? key_row_of(a, b, row, 0) : 0;
     int r4[4] = {0, 0, 0, 0};
     for (int j = 0; j < nsteps && !failed; ++j) {
       const int t = j / C::kChunks, c = j % C::kChunks, s = j % kTStages;
       if (c == 0) {
-        const int e = 2 * kTKeys * t + kTKeys * (int)cta + 32 * w + lane;
+        const int e = 2 * kTKeys * t + kTKeys * (int)cta + 16 * w + (lane & 15);
         const int my_row = e < n ? key_row_of(a, b, row, e) : filler;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) r4[q] = __shfl_sync(0xffffffffu, my_row, 4 * (lane & 7) + q);
+        for (int q = 0; q < 4; ++q) r4[q] = __shfl_sync(0xffffffffu, my_row, 4 * (lane & 3) + q);
       }
       mbar_wait(smem_u32(&bars.empty[s]), ((j / kTStages) & 1) ^ 1, a.err, &failed);
       if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
       const uint32_t full = smem_u32(&bars.full[s]);
       if (cta == 0 && w == 0 && lane == 0) mbar_arrive_expect_tx(full, 2 * C::kStage);
-      if (lane < 8)
-        tma_gather4_pair(sK + s * C::kStage + (32 * w + 4 * lane) * 128,
+      if (lane < 4)
+        tma_gather4_pair(sK + s * C::kStage + (16 * w + 4 * lane) * 128,
                          c < C::kNope ? &maps.k : &maps.kr, mapa_shared(full, 0),
                          c < C::kNope ? 64 * c : 0, r4[0], r4[1], r4[2], r4[3]);
       __syncwarp();
@@ -273,7 +277,12 @@ constexpr int kDi = 128;         // index head dim
 constexpr int kIStages = 3;
 constexpr int kIDrain0 = 6;      // first dKI drain warp
 constexpr int kIDrainWarps = 8;  // two per TMEM lane quadrant, 64 columns each
-constexpr int kIThreads = 32 * (kIDrain0 + kIDrainWarps);   // 0: gathers, 1: MMA, 2-5: epilogue
+constexpr int kIGather1 = kIDrain0 + kIDrainWarps;   // extra gather warps after the drains
+constexpr int kIGathers = 3;     // warp 0 + 2: a thread issues one gather4 every ~100 cycles
+                                 // and the lanes of a warp take turns (16 warps keep the
+                                 // 128-register budget)
+constexpr int kIThreads = 32 * (kIGather1 + kIGathers - 1);   // 0, 14-16: gathers, 1: MMA,
+                                                               // 2-5: epilogue, 6-13: drains
 
 struct ICfg {
   static constexpr int kQiBytes = 2 * kNip * 128;           // [dim chunk][64 heads][128 B]
@@ -297,7 +306,6 @@ struct IMaps {
 struct __align__(16) IBars {
   uint64_t full[kIStages], empty[kIStages], rfull[2], rfree[2], cready[2], cfree[2], dfull[2], dfree[2], qdone;
   uint32_t tmem_slot;
-  int rows[2][kIKeys];
   float w[kNip];
   float red[8];
   float stat[4];
@@ -375,27 +383,29 @@ __global__ void __launch_bounds__(kIThreads, 1)
   bool failed = false;
   const int nsteps = 2 * ntiles;   // pass A then pass B, one KI tile per step
 
-  if (warp == 0) {
-    // ---- KI tiles (TMA gather4), for both passes ----
+  if (warp == 0 || warp >= kIGather1) {
+    // ---- KI tiles (TMA gather4), for both passes: 64 gathers per step (2 dim chunks x
+    // 32 key groups), item i on gather warp i % 3, lane i / 3 ----
+    const int lw = warp == 0 ? 0 : warp - kIGather1 + 1;
+    const int item = lw + kIGathers * lane;
+    const bool issuer = item < 2 * (kIKeys / 4);
+    const int c = item / (kIKeys / 4), g = item % (kIKeys / 4);
+    const int filler = key_row_of(a, b, row, 0);
     for (int j = 0; j < nsteps && !failed; ++j) {
-      const int t = j % ntiles, s = j % kIStages, rb = j & 1;
-      const int e0 = kIKeys * t;
-      const int filler = key_row_of(a, b, row, 0);
-      for (int i = lane; i < kIKeys; i += 32)
-        bars.rows[rb][i] = e0 + i < n ? key_row_of(a, b, row, e0 + i) : filler;
-      __syncwarp();
+      const int t = j % ntiles, s = j % kIStages;
+      const int e0 = kIKeys * t + 4 * g;
+      int rr[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        rr[e] = issuer && e0 + e < n ? key_row_of(a, b, row, e0 + e) : filler;
       mbar_wait(smem_u32(&bars.empty[s]), ((j / kIStages) & 1) ^ 1, a.err, &failed);
       failed = __any_sync(0xffffffffu, failed);
       if (failed) break;
       const uint32_t fb = smem_u32(&bars.full[s]);
-      if (lane == 0) mbar_arrive_expect_tx(fb, C::kStage);
-      __syncwarp();
-      for (int item = lane; item < 2 * (kIKeys / 4); item += 32) {
-        const int c = item / (kIKeys / 4), g = item % (kIKeys / 4);
-        const int* rr = bars.rows[rb] + 4 * g;
+      if (lw == 0 && lane == 0) mbar_arrive_expect_tx(fb, C::kStage);
+      if (issuer)
         tma_gather4(sK + s * C::kStage + c * kIKeys * 128 + g * 512, &maps.ki, fb, 64 * c, rr[0],
                     rr[1], rr[2], rr[3]);
-      }
       __syncwarp();
     }
   } else if (warp == 1) {
