@@ -35,6 +35,14 @@ BWD_FLOP_PER_PAIR = N1 * (3 * 2 * (D + DR) + 2 * 2 * D)        # S, dQ, dK (576)
 GATHER_BYTES_PER_PAIR = (D + DR) * 2                           # one bf16 key row
 # backward: the key row gathered twice (scores, dQ) + the fp32 dK/dKr/dV scatter
 BWD_BYTES_PER_PAIR = 2 * GATHER_BYTES_PER_PAIR + 4 * (2 * D + DR)
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per valid pair, from one
+# `ncu --set full` capture of the last 256 query rows of config 4 (524,288 pairs; command and
+# figures in profiles/sfa_kernels_config4_rows256_full.md), scaled to a launch by its pairs.
+# Backward: K1 + K2 + K3, plus the delta kernel's read of dO and O (2 x N1 x D x 2 B a row).
+PROFILE_PAIRS = 524288
+BWD_DRAM_BYTES_PER_PAIR = (94.85 + 215.33 + 146.08 + 20.42 + 396.22 + 26.15) * 1e6 / PROFILE_PAIRS
+BWD_DRAM_BYTES_PER_ROW = 2 * N1 * D * 2
+FWD_DRAM_BYTES_PER_PAIR = (49.38 + 2.23) * 1e6 / PROFILE_PAIRS
 
 
 def load_peaks():
@@ -320,9 +328,11 @@ def main():
     if bwd_ms >= fwd_ms:
         kname, kms = "dsa_sfa_bwd", bwd_ms
         kflops, kbytes = my_pairs * BWD_FLOP_PER_PAIR, my_pairs * BWD_BYTES_PER_PAIR
+        ktraffic = my_pairs * BWD_DRAM_BYTES_PER_PAIR + (r1 - r0) * BWD_DRAM_BYTES_PER_ROW
     else:
         kname, kms = "dsa_sfa_fwd", fwd_ms
         kflops, kbytes = my_pairs * FWD_FLOP_PER_PAIR, my_pairs * GATHER_BYTES_PER_PAIR
+        ktraffic = my_pairs * FWD_DRAM_BYTES_PER_PAIR
     t_bytes = kbytes / (hbm_peak * 1e9)
     t_flops = kflops / (tf_peak * 1e12)
     bound = "hbm" if t_bytes >= t_flops else "tensor"
@@ -331,7 +341,8 @@ def main():
             "peak": hbm_peak if bound == "hbm" else tf_peak,
             "unit": "GB/s" if bound == "hbm" else "TFLOP/s",
             "frac": max(t_bytes, t_flops) / (kms * 1e-3),
-            "traffic": None,
+            "traffic": ktraffic,
+            "traffic_source": "ncu dram bytes of the last 256 rows, scaled by pairs",
             "kernel": kname,
             "peak_source": peak_kind,
             "tensor_frac": t_flops / (kms * 1e-3),
