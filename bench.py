@@ -298,7 +298,7 @@ def main():
     red = (lambda accs: [dist.all_reduce(t) for t in accs]) if world > 1 else None
 
     def e2e_step():
-        dsa.sfa_fwd_bwd_from_host(hq, hk, hsi, hdo, scale, hqr, hkr, sparse_mode=3, chunks=8,
+        dsa.sfa_fwd_bwd_from_host(hq, hk, hsi, hdo, scale, hqr, hkr, sparse_mode=3,
                                   host_out=outs_h, actual_seq_length_query=aq[0],
                                   reduce_key_grads=red)
 

@@ -4,11 +4,19 @@ A caller whose activations are kept in (pinned) host memory -- CPU offload of a 
 prefill, or a data pipeline that hands over host tensors -- would otherwise copy every
 input to the GPU, run the forward and backward, and copy every result back, one after the
 other; at config-4 sizes the copies (about 4.7 GB) take longer than the kernels.
-:func:`sfa_fwd_bwd_from_host` splits the query rows into chunks of about equal valid-pair
-counts and runs three streams: host-to-device copies of chunk i+1, the forward and backward
-kernels of chunk i, and device-to-host copies of chunk i-1's results. The key gradients of
-all chunks of a batch are added into one set of fp32 accumulators (``accumulate`` in the C
-ABI) and cast once after the batch's last chunk.
+:func:`sfa_fwd_bwd_from_host` splits the query rows into chunks and runs three streams:
+host-to-device copies of chunk i+1, the forward and backward kernels of chunk i, and
+device-to-host copies of chunk i-1's results. The copies, not the kernels, bound the step
+(every row moves its query, query_rope and dO in and its output, dq and dq_rope out: about
+570 KB a row at N1 = 128, D = 512, against a few microseconds of kernel time), so chunks
+hold equal numbers of rows. More chunks shorten the pipeline's fill and drain (the first
+chunk's input copies and the last chunk's kernels and output copies, which nothing
+overlaps) but each costs about half a millisecond of launches and allocations; about 512
+rows a chunk, 8 to 16 chunks, measured best at config-4 sizes (65 ms a step against 68 ms
+for 8 chunks balanced by valid pairs and 71 ms for 32 chunks, on 55 GB/s H2D and 51 GB/s
+D2H PCIe links). The key
+gradients of all chunks of a batch are added into one set of fp32 accumulators
+(``accumulate`` in the C ABI) and cast once after the batch's last chunk.
 
 A contiguous row range [r0, r1) of one batch of a causal (sparse_mode 3) BSND query is
 itself a BSND query of r1 - r0 rows with actual query length S1 - r0 (the kernels' window
@@ -25,14 +33,9 @@ from .sparse_flash_attention import sparse_flash_attention_triton
 from .sparse_flash_attention_grad import sparse_flash_attention_grad_partial
 
 
-def _row_pairs(S1: int, act_q: int, topk: int, sparse_mode: int, act_k: int) -> np.ndarray:
-    """Valid keys per row if every index is used (for balancing only: no scan of the ids)."""
-    s1 = np.arange(S1, dtype=np.int64)
-    if sparse_mode == 3:
-        vis = np.clip(act_k - act_q + s1 + 1, 0, act_k)
-    else:
-        vis = np.full(S1, act_k, dtype=np.int64)
-    return np.minimum(vis, topk)
+def default_chunks(S1: int) -> int:
+    """Chunks of about 512 rows, at least 8 and at most 16."""
+    return max(8, min(16, S1 // 512))
 
 
 def host_outputs(query, key, query_rope, key_rope):
@@ -42,7 +45,7 @@ def host_outputs(query, key, query_rope, key_rope):
 
 
 def sfa_fwd_bwd_from_host(query, key, sparse_indices, d_out, scale_value, query_rope, key_rope,
-                          sparse_mode: int = 3, chunks: int = 8, device=None, host_out=None,
+                          sparse_mode: int = 3, chunks=None, device=None, host_out=None,
                           actual_seq_length_query=None, reduce_key_grads=None):
     """Sparse flash attention forward and backward of BSND host tensors, streamed.
 
@@ -53,7 +56,8 @@ def sfa_fwd_bwd_from_host(query, key, sparse_indices, d_out, scale_value, query_
     [r0, r0 + S1) of a longer causal query, as in a multi-GPU shard).  Returns host tensors
     ``(out, dq, dk, dv, dq_rope, dk_rope)``, the values of sparse_flash_attention_triton and
     sparse_flash_attention_grad_triton on the same inputs; pass ``host_out`` (from
-    :func:`host_outputs`) to reuse pinned buffers.  ``reduce_key_grads(accs)``, if given, is
+    :func:`host_outputs`) to reuse pinned buffers; ``chunks`` sets the number of row chunks
+    (default :func:`default_chunks`).  ``reduce_key_grads(accs)``, if given, is
     called with each batch's fp32 key-gradient accumulators before their cast (e.g. an
     all-reduce across the ranks that share the keys).
     Asynchronous like a non_blocking copy: the results are complete once the caller's
@@ -65,7 +69,6 @@ def sfa_fwd_bwd_from_host(query, key, sparse_indices, d_out, scale_value, query_
     if sparse_mode not in (0, 3):
         raise ValueError("sparse_mode must be 0 or 3")
     B, S1, N1, D = query.shape
-    S2, K = key.shape[1], sparse_indices.shape[-1]
     if host_out is None:
         host_out = host_outputs(query, key, query_rope, key_rope)
     h_out, h_dq, h_dk, h_dv, h_dqr, h_dkr = host_out
@@ -87,8 +90,11 @@ def sfa_fwd_bwd_from_host(query, key, sparse_indices, d_out, scale_value, query_
     compute.wait_stream(h2d)
     used_by(compute, k_d, kr_d)
     act_q = S1 if actual_seq_length_query is None else int(actual_seq_length_query)
-    pairs = _row_pairs(S1, act_q, K, sparse_mode, S2)
-    bounds = [shard_rows(pairs, chunks, c) for c in range(chunks)]
+    chunks = default_chunks(S1) if chunks is None else int(chunks)
+    if chunks < 1:
+        raise ValueError("chunks must be >= 1")
+    rows = np.ones(S1, dtype=np.int64)      # equal rows: the copies bound the step
+    bounds = [shard_rows(rows, chunks, c) for c in range(chunks)]
     for b in range(B):
         kb, krb = k_d[b:b + 1], kr_d[b:b + 1]
         accs = None

@@ -60,6 +60,20 @@ def _worker(rank, world, port, case, out_q):
 
 
 @pytest.mark.timeout(300)
+def test_stream_chunks_cover_rows_equally():
+    """Host-streamed fwd+bwd: chunks of equal rows (the copies bound the step), 8 to 16."""
+    from dsa_triton_ascend_b200.streaming import default_chunks
+    assert default_chunks(8192) == 16 and default_chunks(1024) == 8 and default_chunks(64) == 8
+    assert default_chunks(6144) == 12 and default_chunks(1 << 20) == 16
+    for S1, n in [(8192, 32), (1000, 8), (5, 8)]:
+        ones = np.ones(S1, dtype=np.int64)
+        b = [shard_rows(ones, n, c) for c in range(n)]
+        assert b[0][0] == 0 and b[-1][1] == S1
+        assert all(b[c][1] == b[c + 1][0] for c in range(n - 1))
+        sizes = [r1 - r0 for r0, r1 in b]
+        assert max(sizes) - min(sizes) <= 1
+
+
 def test_two_rank_fwd_bwd_matches_single_rank():
     case = (1, 12, 64, 4, 128, 16, 1, 3, "fp32", 5)
     ctx = mp.get_context("spawn")
