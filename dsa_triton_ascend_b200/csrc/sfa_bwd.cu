@@ -74,7 +74,10 @@ struct Args {
   int* err;
 };
 
+// bar.sync is the aligned form: the whole warp must arrive converged, so converge it first
+// (a lane that left a wait early, e.g. after a timeout, rejoins here)
 __device__ __forceinline__ void named_bar(int id, int n) {
+  __syncwarp();
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 

@@ -66,7 +66,10 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// bar.sync is the aligned form: the whole warp must arrive converged, so converge it first
+// (a lane that left a wait early, e.g. after a timeout, rejoins here)
 __device__ __forceinline__ void named_bar_sync(int id, int n) {
+  __syncwarp();
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
