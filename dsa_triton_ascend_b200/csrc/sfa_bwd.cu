@@ -141,16 +141,17 @@ struct Maps1 {
 struct __align__(16) Bars1 {
   uint64_t q_full, full[kStages1], empty[kStages1], tfull[2], tfree[2];
   uint32_t tmem_slot;
-  float mxl[128];   // softmax_max * log2(e) per head (+inf for padded heads)
-  float inv[128];   // 1 / softmax_sum (0 for padded heads)
-  float dlt[128];   // rowsum(dO * O)
+  // per head: softmax_max * log2(e) (+inf for padded heads), 1 / softmax_sum (0 for padded
+  // heads), rowsum(dO * O), unused -- one 16-byte broadcast load per head
+  float4 hc[128];
 };
 
-constexpr int kGatherWarp1 = 6;
-constexpr int kGatherWarps1 = 8;   // a thread issues one gather4 every ~100 cycles and the
-                                   // lanes of a warp take turns: 4 gathers per warp
+constexpr int kElemWarps1 = 8;     // two per TMEM lane quadrant, 64 heads each
+constexpr int kGatherWarp1 = 2 + kElemWarps1;
+constexpr int kGatherWarps1 = 6;   // a thread issues one gather4 every ~100 cycles and the
+                                   // lanes of a warp take turns: at most 6 gathers per warp
 constexpr int kThreads1 = 32 * (kGatherWarp1 + kGatherWarps1);   // 0: Q/dO TMA, 1: MMA,
-                                                                 // 2-5: elementwise, 6-13: keys
+                                                                 // 2-9: elementwise, 10-15: keys
 
 template <int D, typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads1, 1)
@@ -177,14 +178,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads1, 1)
   for (int h = threadIdx.x; h < 128; h += kThreads1) {
     if (h < a.N1 && ntiles > 0) {
       const size_t hidx = (size_t)row * a.N1 + h;
-      bars.mxl[h] = __ldg(a.smax + hidx) * 1.4426950408889634f;
       const float sm = __ldg(a.ssum + hidx);
-      bars.inv[h] = 1.f / (sm > 0.f ? sm : 1.f);
-      bars.dlt[h] = __ldg(a.delta + hidx);
+      bars.hc[h] = make_float4(__ldg(a.smax + hidx) * 1.4426950408889634f, 1.f / (sm > 0.f ? sm : 1.f),
+                               __ldg(a.delta + hidx), 0.f);
     } else {   // padded heads: exp2(s - inf) = 0, so P = dS = 0
-      bars.mxl[h] = INFINITY;
-      bars.inv[h] = 0.f;
-      bars.dlt[h] = 0.f;
+      bars.hc[h] = make_float4(INFINITY, 0.f, 0.f, 0.f);
     }
   }
   if (threadIdx.x == 0) {
@@ -228,24 +226,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads1, 1)
     }
   } else if (warp >= kGatherWarp1) {
     // ---- the CTA's 128 keys of each tile, chunk by chunk (TMA gather4, 2-SM form):
-    // warp w gathers keys [16w, 16w+16), lanes 0-3 four rows each ----
+    // key group g (keys 4g..4g+3) on gather warp g % W, lane g / W ----
     const int w = warp - kGatherWarp1;
+    const int g = w + kGatherWarps1 * lane;
+    const bool issuer = g < kKeys1 / 4;
     const int filler = nvalid > 0 ? __ldg(rows) : 0;
     int r4[4] = {0, 0, 0, 0};
     for (int j = 0; j < nsteps && !failed; ++j) {
       const int t = j / C::kChunks, c = j % C::kChunks, s = j % kStages1;
       if (c == 0) {
-        const int e = 2 * kKeys1 * t + kKeys1 * (int)cta + 16 * w + (lane & 15);
-        const int my_row = e < nvalid ? __ldg(rows + e) : filler;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) r4[q] = __shfl_sync(0xffffffffu, my_row, 4 * (lane & 3) + q);
+        for (int q = 0; q < 4; ++q) {
+          const int e = 2 * kKeys1 * t + kKeys1 * (int)cta + 4 * g + q;
+          r4[q] = issuer && e < nvalid ? __ldg(rows + e) : filler;
+        }
       }
       mbar_wait(smem_u32(&bars.empty[s]), ((j / kStages1) & 1) ^ 1, a.err, &failed);
       if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
       const uint32_t full = smem_u32(&bars.full[s]);
       if (cta == 0 && w == 0 && lane == 0) mbar_arrive_expect_tx(full, 2 * C::kStage);
-      if (lane < 4)
-        tma_gather4_pair(sX + s * C::kStage + (16 * w + 4 * lane) * 128,
+      if (issuer)
+        tma_gather4_pair(sX + s * C::kStage + g * 512,
                          c < C::kNope ? &maps.k : &maps.kr, mapa_shared(full, 0),
                          c < C::kNope ? 64 * c : 0, r4[0], r4[1], r4[2], r4[3]);
       __syncwarp();
@@ -288,8 +289,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads1, 1)
     }
     __syncwarp();
   } else {
-    // ---- elementwise: thread = key (TMEM lane), 128 heads in the columns ----
+    // ---- elementwise: thread = key (TMEM lane); warps 2-5 heads 0-63, warps 6-9 64-127 ----
     const int qd = warp & 3;
+    const int hbase = 64 * ((warp - 2) >> 2);
     const int kk = 32 * qd + lane;
     const uint32_t lane_addr = (uint32_t)(32 * qd) << 16;
     const float c2 = a.scale * 1.4426950408889634f;
@@ -305,38 +307,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads1, 1)
       uint4* ds_row = reinterpret_cast<uint4*>(static_cast<T*>(a.ds) + ((size_t)row * a.kp + e) * kHeadsPad);
       uint4* p_row = reinterpret_cast<uint4*>(static_cast<T*>(a.pp) + ((size_t)row * a.kp + e) * kHeadsPad);
 #pragma unroll 1
-      for (int h0 = 0; h0 < 128; h0 += 32) {
-        uint32_t sr[32], pr[32];
+      for (int h0 = hbase; h0 < hbase + 64; h0 += 16) {
+        uint32_t sr[16], pr[16];
         if (!wfail) {
-          tmem_ld32(tmem + lane_addr + 256 * b + h0, sr);
-          tmem_ld32(tmem + lane_addr + 256 * b + 128 + h0, pr);
+          tmem_ld16(tmem + lane_addr + 256 * b + h0, sr);
+          tmem_ld16(tmem + lane_addr + 256 * b + 128 + h0, pr);
           tmem_ld_wait();
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) sr[i] = pr[i] = 0u;
+          for (int i = 0; i < 16; ++i) sr[i] = pr[i] = 0u;
         }
-        uint32_t pk_p[16], pk_s[16];
+        uint32_t pk_p[8], pk_s[8];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
+        for (int i = 0; i < 8; ++i) {
           float p[2], g[2];
 #pragma unroll
           for (int x = 0; x < 2; ++x) {
-            const int h = h0 + 2 * i + x;
-            const float pe = valid ? ex2(fmaf(__uint_as_float(sr[2 * i + x]), c2, -bars.mxl[h])) * bars.inv[h] : 0.f;
+            const float4 hc = bars.hc[h0 + 2 * i + x];
+            const float pe = valid ? ex2(fmaf(__uint_as_float(sr[2 * i + x]), c2, -hc.x)) * hc.y : 0.f;
             p[x] = pe;
-            g[x] = valid ? pe * (__uint_as_float(pr[2 * i + x]) - bars.dlt[h]) * a.scale : 0.f;
+            g[x] = valid ? pe * (__uint_as_float(pr[2 * i + x]) - hc.z) * a.scale : 0.f;
           }
           pk_p[i] = ElemTraits<T>::pack2(p[0], p[1]);
           pk_s[i] = ElemTraits<T>::pack2(g[0], g[1]);
         }
-#pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          ds_row[h0 / 8 + v] = make_uint4(pk_s[4 * v], pk_s[4 * v + 1], pk_s[4 * v + 2], pk_s[4 * v + 3]);
-          p_row[h0 / 8 + v] = make_uint4(pk_p[4 * v], pk_p[4 * v + 1], pk_p[4 * v + 2], pk_p[4 * v + 3]);
-        }
+        // 16 heads of one key = one 32-byte sector (rows are 256 B, the scratch 256 B aligned)
+        st_global_v8(ds_row + h0 / 8, pk_s);
+        st_global_v8(p_row + h0 / 8, pk_p);
       }
       tc_fence_before();
-      named_bar(1, 128);
+      named_bar(1, 32 * kElemWarps1);
       if (warp == 2 && lane == 0) mbar_arrive_cluster(b ? lead_f1 : lead_f0);
     }
   }
@@ -1051,7 +1051,7 @@ extern "C" int dsa_sfa_bwd(const DsaSfaBwdParams* p, void* stream_) {
       !p->dk_acc || !p->dkr_acc || !p->dv_acc)
     return DSA_ERR_INVALID_ARG;
   if (!p->block_table && !p->k_row_base) return DSA_ERR_INVALID_ARG;
-  if (!p->workspace ||
+  if (!p->workspace || (reinterpret_cast<uintptr_t>(p->workspace) & 255u) != 0 ||
       p->workspace_bytes < dsa_sfa_bwd_workspace_size(p->num_rows, p->topk, p->sparse_block_size))
     return DSA_ERR_INVALID_ARG;
   if (p->num_rows == 0) return DSA_OK;

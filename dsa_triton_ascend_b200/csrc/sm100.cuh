@@ -142,6 +142,13 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity, i
   }
 }
 
+// 32-byte global store (sm_100): one whole sector per thread. p must be 32-byte aligned.
+__device__ __forceinline__ void st_global_v8(void* p, const uint32_t (&v)[8]) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(v[0]),
+               "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // cluster helpers
 // ---------------------------------------------------------------------------

@@ -161,7 +161,8 @@ typedef struct DsaSfaBwdParams {
   float* dkr_acc;
   float* dv_acc;
   int* error_flag;
-  void* workspace;               /* dsa_sfa_bwd_workspace_size() bytes, caller-owned */
+  void* workspace;               /* dsa_sfa_bwd_workspace_size() bytes, caller-owned,
+                                    256-byte aligned (DSA_ERR_INVALID_ARG otherwise) */
   int64_t workspace_bytes;
   int64_t num_rows;
   int64_t batch;

@@ -58,3 +58,28 @@ def test_null_params_rejected_without_gpu_work(lib):
         f.restype = ctypes.c_int
         f.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
         assert f(None, None) == 1   # DSA_ERR_INVALID_ARG
+
+
+def test_bwd_rejects_misaligned_workspace_without_gpu_work(lib):
+    """The backward's scratch takes 32-byte stores: a workspace not 256-byte aligned is an
+    argument error, reported before any CUDA call (the pointers below are never touched)."""
+    from dsa_triton_ascend_b200._lib import SfaBwdParams
+    p = SfaBwdParams()
+    fake = 1 << 20
+    for name, _ in SfaBwdParams._fields_:
+        if name in ("block_table", "dk", "dkr", "dv", "error_flag", "workspace"):
+            continue
+        if name in ("q", "q_rope", "key", "key_rope", "d_out", "out", "softmax_max", "softmax_sum",
+                    "sparse_indices", "act_q", "act_k", "q_row_base", "k_row_base", "dq", "dqr",
+                    "dk_acc", "dkr_acc", "dv_acc"):
+            setattr(p, name, fake)
+    p.num_rows, p.batch, p.n1, p.d, p.topk, p.sparse_block_size, p.kv_rows = 4, 1, 16, 512, 64, 1, 64
+    f = lib.dsa_sfa_bwd_workspace_size
+    f.restype = ctypes.c_int64
+    f.argtypes = [ctypes.c_int64] * 3
+    p.workspace_bytes = f(4, 64, 1)
+    p.workspace = fake + 16            # 16-byte aligned, not 256
+    g = lib.dsa_sfa_bwd
+    g.restype = ctypes.c_int
+    g.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+    assert g(ctypes.addressof(p), None) == 1   # DSA_ERR_INVALID_ARG
