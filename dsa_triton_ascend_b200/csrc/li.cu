@@ -406,7 +406,7 @@ __device__ __forceinline__ void bitonic_desc(unsigned long long* sel) {
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kTopkThreads) li_topk_kernel(const TopkArgs a) {
+__global__ void __launch_bounds__(kTopkThreads, 2) li_topk_kernel(const TopkArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint32_t* keys = reinterpret_cast<uint32_t*>(smem_raw);                       // s2_row
   unsigned long long* sel = reinterpret_cast<unsigned long long*>(smem_raw + ((a.s2_row * 4 + 15) / 16) * 16);
@@ -446,14 +446,37 @@ __global__ void __launch_bounds__(kTopkThreads) li_topk_kernel(const TopkArgs a)
         if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255], 1);
       }
       __syncthreads();
-      if (threadIdx.x == 0) {
-        int above = 0, d = 255;
-        for (; d > 0; --d) {
-          if (above + hist[d] >= remaining) break;
-          above += hist[d];
+      if (threadIdx.x < 32) {
+        // digit of the `remaining`-th largest key: lane l sums digits 255-8l .. 248-8l, a
+        // warp prefix sum over the lanes (highest digits first) finds the lane, then the digit
+        const int lane = threadIdx.x;
+        int c[8], sum = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          c[j] = hist[255 - 8 * lane - j];
+          sum += c[j];
         }
-        s_digit = d;
-        s_above = above;
+        int incl = sum;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const int v = __shfl_up_sync(0xffffffffu, incl, off);
+          if (lane >= off) incl += v;
+        }
+        const bool mine = incl - sum < remaining && remaining <= incl;
+        const unsigned found = __ballot_sync(0xffffffffu, mine);   // every lane, before branching
+        if (mine) {
+          int above = incl - sum, d = 255 - 8 * lane - 7;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            if (above + c[j] >= remaining) { d = 255 - 8 * lane - j; break; }
+            above += c[j];
+          }
+          s_digit = d;
+          s_above = above;
+        } else if (found == 0u && lane == 31) {
+          s_digit = 0;                 // not reached: `remaining` never exceeds the count
+          s_above = incl - c[7];
+        }
       }
       __syncthreads();
       prefix |= (uint32_t)s_digit << shift;
@@ -469,9 +492,11 @@ __global__ void __launch_bounds__(kTopkThreads) li_topk_kernel(const TopkArgs a)
       const uint32_t k = i < lim ? keys[i] : 0u;
       const int is_gt = (i < lim && k > thr) ? 1 : 0;
       const int is_eq = (i < lim && k == thr) ? 1 : 0;
-      int tot_gt, tot_eq;
-      const int pg = block_scan(is_gt, warp_sums, &tot_gt);
-      const int pe = block_scan(is_eq, warp_sums, &tot_eq);
+      // one scan for both counts (each at most kTopkThreads, so 16 bits apiece)
+      int tot;
+      const int pge = block_scan(is_gt | (is_eq << 16), warp_sums, &tot);
+      const int pg = pge & 0xffff, pe = pge >> 16;
+      const int tot_gt = tot & 0xffff, tot_eq = tot >> 16;
       const unsigned long long comp = ((unsigned long long)k << 32) | (uint32_t)(~(uint32_t)i);
       if (is_gt) sel[gt_base + pg] = comp;
       if (is_eq && eq_base + pe < remaining) sel[(K - remaining) + eq_base + pe] = comp;
