@@ -27,6 +27,21 @@ def _cached(key, make):
     return t
 
 
+def _i32_from_host(vals, device) -> torch.Tensor:
+    """Host integers -> int32 device tensor without synchronising host and device.
+
+    ``torch.tensor(list, device=cuda)`` copies from pageable memory and waits for the
+    stream; a decode step would then pay a full host/device round trip per call. Values
+    are cached per device (the tensors are never written), and a miss is copied from
+    pinned memory asynchronously on the current stream."""
+    key = ("i32", tuple(vals), str(device))
+    t = _const_cache.get(key)
+    if t is None:
+        h = torch.tensor(list(vals), dtype=torch.int32).pin_memory()
+        t = _cached(key, lambda: h.to(device, non_blocking=True))
+    return t
+
+
 def lens_tensor(lens, batch: int, default: int, device) -> torch.Tensor:
     """None -> [default]*batch; list/tuple/int -> int32 tensor; tensor -> int32 on device."""
     if lens is None or isinstance(lens, int):
@@ -36,7 +51,7 @@ def lens_tensor(lens, batch: int, default: int, device) -> torch.Tensor:
     if isinstance(lens, (list, tuple)):
         if len(lens) != batch:
             raise ValueError(f"expected {batch} sequence lengths, got {len(lens)}")
-        return torch.tensor([int(x) for x in lens], dtype=torch.int32, device=device)
+        return _i32_from_host([int(x) for x in lens], device)
     t = torch.as_tensor(lens)
     if t.numel() != batch:
         raise ValueError(f"expected {batch} sequence lengths, got {t.numel()}")
@@ -48,7 +63,7 @@ def cumulative(lens, device) -> torch.Tensor:
     if lens is None:
         raise ValueError("TND layout requires cumulative actual sequence lengths")
     if isinstance(lens, (list, tuple)):
-        return torch.tensor([int(x) for x in lens], dtype=torch.int32, device=device)
+        return _i32_from_host([int(x) for x in lens], device)
     return torch.as_tensor(lens).reshape(-1).to(device=device, dtype=torch.int32)
 
 

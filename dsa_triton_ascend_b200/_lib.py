@@ -110,6 +110,8 @@ def lib() -> ctypes.CDLL:
                 l.dsa_sfa_fwd.restype = ctypes.c_int
                 l.dsa_sfa_fwd_workspace_size.argtypes = [_i64, _i64, _i64]
                 l.dsa_sfa_fwd_workspace_size.restype = _i64
+                l.dsa_sfa_fwd_fast_workspace_size.argtypes = [_i64] * 5
+                l.dsa_sfa_fwd_fast_workspace_size.restype = _i64
                 l.dsa_sfa_fwd_noalloc.argtypes = [ctypes.POINTER(SfaFwdParams), _p]
                 l.dsa_sfa_fwd_noalloc.restype = ctypes.c_int
                 l.dsa_sfa_bwd.argtypes = [ctypes.POINTER(SfaBwdParams), _p]

@@ -109,6 +109,12 @@ struct Args {
   const int32_t* ws_count;  // [num_rows] number of valid keys per query row
   int num_rows, B, N1, topk, block, kv_rows, page, max_blocks, s2_cap, sparse_mode;
   float scale;
+  // key splits per query row (1: the kernel writes out / softmax_max / softmax_sum itself;
+  // > 1: CTA pair p = row * splits + split handles tiles [split * T / splits, ...) of its
+  // row and writes a normalised fp32 partial O and {m_ref, m_run, l} for the combine kernel)
+  int splits;
+  float* part_o;    // [num_rows * splits][N1][D]
+  float4* part_s;   // [num_rows * splits][N1]
 };
 
 // Barrier protocol (t = tile, b = t & 1 selects the X stage, H slot, S and P buffer):
@@ -151,15 +157,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     return;
   }
   const uint32_t cta = cluster_ctarank();
-  const int row = blockIdx.x >> 1;
+  const int pair = blockIdx.x >> 1;
+  const int row = pair / a.splits;
+  const int split = pair - row * a.splits;
   const RowInfo ri = row_info(a, row);
   // Valid keys of this row, compacted by sfa_prep_kernel (identical in both CTAs).
   // A CTA that finds an earlier error recorded skips its row, so one protocol failure
   // does not turn into a slow cascade of timeouts over the whole grid.
   const bool abort = a.err != nullptr && *reinterpret_cast<volatile int*>(a.err) != 0;
-  const int nvalid = (ri.active && !abort) ? __ldg(a.ws_count + row) : 0;
-  const int ntiles = (nvalid + kTile - 1) / kTile;
-  const int32_t* rows = a.ws_rows + (size_t)row * a.topk * a.block;
+  const int nvalid_row = (ri.active && !abort) ? __ldg(a.ws_count + row) : 0;
+  const int ntiles_row = (nvalid_row + kTile - 1) / kTile;
+  // this pair's tiles [t0, t1) of the row (all of them unless the row is split)
+  const int t0 = (int)((int64_t)split * ntiles_row / a.splits);
+  const int t1 = (int)((int64_t)(split + 1) * ntiles_row / a.splits);
+  const int ntiles = t1 - t0;
+  const int nvalid = ntiles > 0 ? min(nvalid_row - kTile * t0, kTile * ntiles) : 0;
+  const int32_t* rows = a.ws_rows + (size_t)row * a.topk * a.block + (size_t)kTile * t0;
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(&bars.q_full), 1);
@@ -429,7 +442,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = 0u;
         }
-        if (head < a.N1) {
+        if (head < a.N1 && a.splits > 1) {
+          // split row: normalised fp32 partial for the combine kernel
+          float4* dst = reinterpret_cast<float4*>(a.part_o + ((size_t)pair * a.N1 + head) * D + dbase + cc);
+#pragma unroll
+          for (int v = 0; v < 8; ++v)
+            dst[v] = make_float4(__uint_as_float(o[4 * v + 0]) * inv, __uint_as_float(o[4 * v + 1]) * inv,
+                                 __uint_as_float(o[4 * v + 2]) * inv, __uint_as_float(o[4 * v + 3]) * inv);
+        } else if (head < a.N1) {
           uint4* dst = reinterpret_cast<uint4*>(orow + dbase + cc);
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
@@ -443,7 +463,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
       }
     }
-    if (head < a.N1 && half == 0 && a.smax != nullptr) {
+    if (head < a.N1 && half == 0 && a.splits > 1) {
+      const bool any = ntiles > 0 && l_tot > 0.f;
+      a.part_s[(size_t)pair * a.N1 + head] =
+          make_float4(any ? m_ref : -INFINITY, any ? m_run : -INFINITY, any ? l_tot : 0.f, 0.f);
+    } else if (head < a.N1 && half == 0 && a.smax != nullptr) {
       const bool any = ntiles > 0;
       a.smax[(size_t)row * a.N1 + head] = any ? m_run * a.scale : 0.f;
       a.ssum[(size_t)row * a.N1 + head] = any ? l_tot * ex2((m_ref - m_run) * c2) : 0.f;
@@ -455,6 +479,88 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   __syncthreads();
   cluster_sync();
   if (warp == 1) tmem_dealloc<2>(tmem, C::kTmemCols);
+}
+
+// Merge the key splits of each (row, head): weights w_s = l_s 2^((m_ref_s - M) c2) with
+// M = the largest m_ref, O = sum_s w_s O_s / sum_s w_s (O_s normalised by l_s), and the
+// statistics of the whole row: max = the largest m_run, sum = sum_s l_s 2^((m_ref_s - max) c2).
+// One warp per (row, head); lane l owns columns 4l + 128i.
+template <int D, typename T>
+__global__ void __launch_bounds__(256) sfa_fwd_combine_kernel(const float* __restrict__ part_o,
+                                                              const float4* __restrict__ part_s,
+                                                              T* __restrict__ out, float* smax,
+                                                              float* ssum, int num_rows, int n1,
+                                                              int splits, float scale) {
+  const int gw = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+  if (gw >= num_rows * n1) return;
+  const int row = gw / n1, h = gw - row * n1;
+  const float c2 = scale * 1.4426950408889634f;
+  float mref = -INFINITY, mrun = -INFINITY;
+  for (int sp = 0; sp < splits; ++sp) {
+    const float4 st = __ldg(part_s + ((size_t)row * splits + sp) * n1 + h);
+    if (st.z > 0.f) {
+      mref = fmaxf(mref, st.x);
+      mrun = fmaxf(mrun, st.y);
+    }
+  }
+  constexpr int kV = D / 128;
+  float4 acc[kV];
+#pragma unroll
+  for (int i = 0; i < kV; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  float wsum = 0.f, lsum = 0.f;
+  for (int sp = 0; sp < splits; ++sp) {
+    const size_t ps = ((size_t)row * splits + sp) * n1 + h;
+    const float4 st = __ldg(part_s + ps);
+    if (!(st.z > 0.f)) continue;
+    const float w = st.z * ex2((st.x - mref) * c2);
+    wsum += w;
+    lsum += st.z * ex2((st.x - mrun) * c2);
+    const float4* o = reinterpret_cast<const float4*>(part_o + ps * D);
+#pragma unroll
+    for (int i = 0; i < kV; ++i) {
+      const float4 v = __ldg(o + lane + 32 * i);
+      acc[i].x += w * v.x;
+      acc[i].y += w * v.y;
+      acc[i].z += w * v.z;
+      acc[i].w += w * v.w;
+    }
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  T* orow = out + ((size_t)row * n1 + h) * D;
+#pragma unroll
+  for (int i = 0; i < kV; ++i) {
+    uint2 pk;
+    pk.x = ElemTraits<T>::pack2(acc[i].x * inv, acc[i].y * inv);
+    pk.y = ElemTraits<T>::pack2(acc[i].z * inv, acc[i].w * inv);
+    *reinterpret_cast<uint2*>(orow + 4 * (lane + 32 * i)) = pk;
+  }
+  if (lane == 0 && smax != nullptr) {
+    const bool any = wsum > 0.f;
+    smax[(size_t)row * n1 + h] = any ? mrun * scale : 0.f;
+    ssum[(size_t)row * n1 + h] = any ? lsum : 0.f;
+  }
+}
+
+// Few query rows (decode) leave most SMs idle with one CTA pair per row; such rows are
+// split into key ranges so that up to kSplitPairs pairs (one CTA per SM on 148 SMs) run at
+// once, each with at least 4 tiles, when the workspace holds the partial results.
+constexpr int kSplitPairs = 74;
+
+inline int fwd_splits(int64_t num_rows, int64_t nent) {
+  if (num_rows <= 0 || num_rows >= kSplitPairs) return 1;
+  const int64_t ntiles = (nent + kTile - 1) / kTile;
+  int64_t sp = kSplitPairs / num_rows;
+  const int64_t cap = ntiles / 4 > 1 ? ntiles / 4 : 1;
+  if (sp > cap) sp = cap;
+  return sp > 1 ? (int)sp : 1;
+}
+
+inline int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
+
+// workspace layout: compaction (key rows, counts), then the split partials when split
+inline int64_t compaction_bytes(int64_t num_rows, int64_t nent) { return 4 * (num_rows * nent + num_rows); }
+inline int64_t partial_bytes(int64_t num_rows, int splits, int64_t n1, int64_t d) {
+  return splits > 1 ? num_rows * splits * n1 * (d + 4) * 4 : 0;
 }
 
 template <int D>
@@ -498,13 +604,28 @@ int launch(const DsaSfaFwdParams* p, cudaStream_t stream) {
   a.scale = p->scale;
   a.ws_rows = static_cast<const int32_t*>(p->workspace);
   a.ws_count = static_cast<const int32_t*>(p->workspace) + (size_t)p->num_rows * p->topk * p->sparse_block_size;
+  const int64_t nent = p->topk * p->sparse_block_size;
+  int splits = fwd_splits(p->num_rows, nent);
+  const int64_t part_off = align256(compaction_bytes(p->num_rows, nent));
+  if (splits > 1 && p->workspace_bytes < part_off + partial_bytes(p->num_rows, splits, p->n1, D))
+    splits = 1;   // the caller's workspace has no room for the partials: one pair per row
+  a.splits = splits;
+  a.part_o = splits > 1 ? reinterpret_cast<float*>(static_cast<char*>(p->workspace) + part_off) : nullptr;
+  a.part_s = splits > 1 ? reinterpret_cast<float4*>(a.part_o + (size_t)p->num_rows * splits * p->n1 * D)
+                        : nullptr;
   launch_prep(a, const_cast<int32_t*>(a.ws_rows), const_cast<int32_t*>(a.ws_count), p->num_rows,
               stream);
   auto kern = sfa_fwd_kernel<D, T>;
   constexpr int kSmem = smem_bytes<D>();
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
     return DSA_ERR_CUDA;
-  kern<<<dim3(2 * (unsigned)p->num_rows), dim3(kThreads), kSmem, stream>>>(maps, a);
+  kern<<<dim3(2 * (unsigned)(p->num_rows * splits)), dim3(kThreads), kSmem, stream>>>(maps, a);
+  if (splits > 1) {
+    const int64_t warps = p->num_rows * p->n1;
+    sfa_fwd_combine_kernel<D, T><<<dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, stream>>>(
+        a.part_o, a.part_s, static_cast<T*>(p->out), p->softmax_max, p->softmax_sum,
+        (int)p->num_rows, (int)p->n1, splits, p->scale);
+  }
   return cudaGetLastError() == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
 }
 
@@ -540,7 +661,17 @@ extern "C" int dsa_sfa_fwd(const DsaSfaFwdParams* p, void* stream_) {
 
 extern "C" int64_t dsa_sfa_fwd_workspace_size(int64_t num_rows, int64_t topk, int64_t sparse_block_size) {
   if (num_rows < 0 || topk < 0 || sparse_block_size < 1) return -1;
-  return 4 * (num_rows * topk * sparse_block_size + num_rows);
+  return dsa::sfa_fwd::compaction_bytes(num_rows, topk * sparse_block_size);
+}
+
+extern "C" int64_t dsa_sfa_fwd_fast_workspace_size(int64_t num_rows, int64_t n1, int64_t d, int64_t topk,
+                                                   int64_t sparse_block_size) {
+  using namespace dsa::sfa_fwd;
+  if (num_rows < 0 || n1 < 1 || d < 1 || topk < 0 || sparse_block_size < 1) return -1;
+  const int64_t nent = topk * sparse_block_size;
+  const int splits = fwd_splits(num_rows, nent);
+  if (splits <= 1) return compaction_bytes(num_rows, nent);
+  return align256(compaction_bytes(num_rows, nent)) + partial_bytes(num_rows, splits, n1, d);
 }
 
 // ---------------------------------------------------------------------------------------

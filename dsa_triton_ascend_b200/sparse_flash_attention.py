@@ -159,7 +159,8 @@ def sparse_flash_attention_triton(
         smax = alloc((B, 1, S1, N1), dtype=torch.float32, device=dev)
     ssum = alloc(smax.shape, dtype=torch.float32, device=dev)
 
-    ws_bytes = lib().dsa_sfa_fwd_workspace_size(num_rows, topk, int(sparse_block_size))
+    # room for the split partials too: few-row calls (decode) then spread over more SMs
+    ws_bytes = lib().dsa_sfa_fwd_fast_workspace_size(num_rows, N1, D, topk, int(sparse_block_size))
     ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=dev)
 
     p = SfaFwdParams()

@@ -99,6 +99,16 @@ int dsa_sfa_fwd(const DsaSfaFwdParams* params, void* stream);
  * Returns -1 for invalid sizes. */
 int64_t dsa_sfa_fwd_workspace_size(int64_t num_rows, int64_t topk, int64_t sparse_block_size);
 
+/* Workspace with which dsa_sfa_fwd may split the keys of few-row calls (fewer query rows
+ * than CTA pairs the GPU runs at once, e.g. decode) over several CTA pairs per row and
+ * merge their fp32 partial results in a second kernel: dsa_sfa_fwd_workspace_size() plus
+ * room for the partials (num_rows * splits * n1 * (d + 4) floats) when it would split,
+ * else exactly dsa_sfa_fwd_workspace_size().  dsa_sfa_fwd accepts any workspace of at
+ * least dsa_sfa_fwd_workspace_size() bytes and splits only when the partials fit.
+ * Returns -1 for invalid sizes. */
+int64_t dsa_sfa_fwd_fast_workspace_size(int64_t num_rows, int64_t n1, int64_t d, int64_t topk,
+                                        int64_t sparse_block_size);
+
 /*
  * Sparse flash attention forward that allocates nothing.  No counterpart in the
  * reference: it exists for callers that cannot allocate device memory when they run

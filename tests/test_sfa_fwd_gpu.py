@@ -123,6 +123,47 @@ def test_fwd_tnd_layout():
     _stats_close(host(mx), rm_t, host(sm), rs_t, "tnd")
 
 
+def test_fwd_split_rows_match_oracle():
+    """Few query rows with many keys: each row's keys are split over several CTA pairs whose
+    fp32 partials are merged by a second kernel. Batch 1 sees at most 100 keys (most of its
+    splits are empty) and its last row is past actual_seq_lengths_query (all splits empty)."""
+    act_q, act_k = [3, 2], [4096, 100]
+    c = I.sfa_case(2, 3, 4096, 128, 512, 2048, 1, 3, "bf16", seed=31, act_q=act_q, act_k=act_k)
+    out, mx, sm = _run(c, "bf16", 3, act_q=act_q, act_k=act_k)
+    ref, rm, rs = sfa.sfa_fwd(c["q"], c["k"], c["qr"], c["kr"], c["si"], c["scale"], act_q=act_q,
+                              act_k=act_k, sparse_mode=3, rounding="kernel")
+    assert_close(out, ref, what="split out")
+    _stats_close(mx, rm, sm, rs, "split")
+    assert np.all(out[1, 2] == 0) and np.all(mx[1, 0, 2] == 0) and np.all(sm[1, 0, 2] == 0)
+
+
+def test_fwd_paged_decode_split():
+    """Decode-shaped PA_BSND call (one query token per sequence, 2048 keys each): split."""
+    from dsa_triton_ascend_b200 import sparse_flash_attention_triton, check_device_errors
+    rng = np.random.default_rng(23)
+    B, N1, D, page, nblk, maxb = 3, 128, 512, 128, 80, 24
+    kv_len = [3000, 2048, 2500]
+    cache = I.randn(rng, (nblk, page, 1, D), "bf16")
+    cache_r = I.randn(rng, (nblk, page, 1, 64), "bf16")
+    bt = rng.permutation(nblk)[:B * maxb].reshape(B, maxb).astype(np.int32)
+    q = I.randn(rng, (B, 1, N1, D), "bf16")
+    qr = I.randn(rng, (B, 1, N1, 64), "bf16")
+    si = np.stack([np.sort(rng.permutation(kv_len[b])[:2048]) for b in range(B)]).astype(np.int32)
+    si = si.reshape(B, 1, 1, 2048)
+    scale = 1 / np.sqrt(576)
+    out, mx, sm = sparse_flash_attention_triton(
+        cuda(q), cuda(cache), cuda(cache), icuda(si), scale, block_table=icuda(bt),
+        actual_seq_lengths_kv=kv_len, query_rope=cuda(qr), key_rope=cuda(cache_r),
+        layout_kv="PA_BSND", sparse_mode=0, return_softmax_lse=True, block_size=page)
+    check_device_errors()
+    k_dense = sfa.pa_to_bsnd(cache, bt, maxb * page)
+    kr_dense = sfa.pa_to_bsnd(cache_r, bt, maxb * page)
+    ref, rm, rs = sfa.sfa_fwd(q, k_dense, qr, kr_dense, si, scale, act_k=kv_len, sparse_mode=0,
+                              rounding="kernel")
+    assert_close(host(out), ref, what="pa split out")
+    _stats_close(host(mx), rm, host(sm), rs, "pa split")
+
+
 def test_fwd_paged_kv():
     """PA_BSND: cache blocks addressed through block_table inside the kernel."""
     from dsa_triton_ascend_b200 import sparse_flash_attention_triton, check_device_errors
