@@ -43,6 +43,13 @@ PROFILE_PAIRS = 524288
 BWD_DRAM_BYTES_PER_PAIR = (94.85 + 215.33 + 146.08 + 20.42 + 396.22 + 26.15) * 1e6 / PROFILE_PAIRS
 BWD_DRAM_BYTES_PER_ROW = 2 * N1 * D * 2
 FWD_DRAM_BYTES_PER_PAIR = (49.38 + 2.23) * 1e6 / PROFILE_PAIRS
+# DRAM traffic of one call of each secondary workload at the size bench.py runs, from one ncu
+# capture of the library's kernels (profiles/secondary_workloads_traffic.md)
+WORKLOAD_DRAM_BYTES = {
+    "li": (138.45 + 39.17 + 67.69 + 47.88) * 1e6,            # score + top-k
+    "decode": (0.33 + 84.43 + 0.10 + 16.92) * 1e6,           # prep + forward + combine
+    "sli": (1284.81 + 58.37 + 260.75 + 109.38 + 4.20) * 1e6,  # teacher + index + cast
+}
 
 
 def load_peaks():
@@ -465,7 +472,8 @@ def run_other(args, rank, world, local):
                          else flops / (ms * 1e-3) / 1e12,
                          "peak": hbm_peak if bound == "hbm" else tf_peak,
                          "unit": "GB/s" if bound == "hbm" else "TFLOP/s",
-                         "frac": max(t_b, t_f) / (ms * 1e-3), "traffic": None,
+                         "frac": max(t_b, t_f) / (ms * 1e-3),
+                         "traffic": WORKLOAD_DRAM_BYTES[args.workload],
                          "peak_source": peak_kind}}
     if rank == 0:
         print(json.dumps(line), flush=True)
