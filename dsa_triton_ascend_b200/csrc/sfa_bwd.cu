@@ -842,12 +842,18 @@ __global__ void __launch_bounds__(kThreads3, 1)
       const bool lanes_ok = !rope || q < 2;   // rope: 64 output columns
       float* gcol = acc + col0 + mblk * 128 + 32 * q + lane - (lane & 1);
       const int32_t* rows = a.ws_rows + (size_t)x.row * a.topk * a.block;
+      // accumulator rows of the share's keys of tile t (-1: no key)
+      auto load_rows = [&](int t, int (&r)[2]) {
+        const int k0 = t * kKeyTile3 + key0;
+        r[0] = k0 + lane < x.nvalid ? __ldg(rows + k0 + lane) : -1;
+        r[1] = nk == 64 && k0 + 32 + lane < x.nvalid ? __ldg(rows + k0 + 32 + lane) : -1;
+      };
+      int kr[2];
+      load_rows(0, kr);
       for (int t = 0; t < x.ntiles; ++t) {
         const int tb = nt & 1;
-        const int k0 = t * kKeyTile3 + key0;
-        int kr[2];
-        kr[0] = k0 + lane < x.nvalid ? __ldg(rows + k0 + lane) : -1;
-        kr[1] = nk == 64 && k0 + 32 + lane < x.nvalid ? __ldg(rows + k0 + 32 + lane) : -1;
+        int kn[2] = {-1, -1};
+        if (t + 1 < x.ntiles) load_rows(t + 1, kn);   // in flight while this tile drains
         mbar_wait(smem_u32(&bars.t_full[tb]), (nt >> 1) & 1, a.err, &failed);
         if (__any_sync(0xffffffffu, failed)) break;
         tc_fence_after();
@@ -858,6 +864,8 @@ __global__ void __launch_bounds__(kThreads3, 1)
         else
           dkv_drain<32>(taddr, t_empty, lanes_ok, gcol, ld,
                         *reinterpret_cast<const int(*)[1]>(&kr[0]), lane);
+        kr[0] = kn[0];
+        kr[1] = kn[1];
         ++nt;
       }
       if (failed) break;
