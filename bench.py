@@ -298,6 +298,8 @@ def main():
     # Inputs in pinned host memory; the public streaming entry point copies them in, runs
     # the forward and backward in row chunks and copies every result out, with the copies
     # of one chunk overlapping the kernels of the next.
+    cpus_all = os.sched_getaffinity(0)
+    bound = dsa.bind_host_to_device(dev)   # pinned buffers on the GPU's NUMA node
     host_in = [x.cpu().pin_memory() for x in (q, qr, k, kr, si, dout)]
     h2d = sum(x.numel() * x.element_size() for x in host_in)
     hq, hqr, hk, hkr, hsi, hdo = host_in
@@ -328,6 +330,7 @@ def main():
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_ms = float(te.item()) / e_steps
     e2e_value = flops_total / (e2e_ms * 1e-3) / 1e12
+    os.sched_setaffinity(0, cpus_all)      # the CPU baseline below uses every host thread
 
     hbm_peak, tf_peak, peak_kind = load_peaks()
     # roofline of the dominant call on this rank's share (fwd or bwd, whichever is longer):
@@ -378,7 +381,8 @@ def main():
             "bwd_tflops": total_pairs * BWD_FLOP_PER_PAIR / (bwd_ms * 1e-3) / 1e12 if world == 1 else None,
             "fwd_roofline_frac": fwd_roof_frac,
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
-                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                    "host_numa_bound": bool(bound)},
             "gpu_launches": args.steps * (2 + 8),   # per step: prep + fwd; prep, delta, 3 bwd kernels, 3 casts
             "roofline": roof,
             "cpu_baseline": cpu,

@@ -26,7 +26,7 @@ from .sparse_flash_attention_grad import (  # noqa: F401
     sparse_flash_attention_grad_partial,
     sparse_flash_attention_grad_triton,
 )
-from .streaming import host_outputs, sfa_fwd_bwd_from_host  # noqa: F401
+from .streaming import bind_host_to_device, host_outputs, sfa_fwd_bwd_from_host  # noqa: F401
 from .autograd import (  # noqa: F401
     IndexerKLLossFunction,
     SparseAttentionWithIndexer,

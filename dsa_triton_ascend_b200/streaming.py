@@ -33,6 +33,42 @@ from .sparse_flash_attention import sparse_flash_attention_triton
 from .sparse_flash_attention_grad import sparse_flash_attention_grad_partial
 
 
+def _parse_cpulist(text: str):
+    cpus = set()
+    for part in text.strip().split(","):
+        if not part:
+            continue
+        if "-" in part:
+            lo, hi = part.split("-")
+            cpus.update(range(int(lo), int(hi) + 1))
+        else:
+            cpus.add(int(part))
+    return cpus
+
+
+def bind_host_to_device(device=None) -> bool:
+    """Run this process on the CPUs next to ``device``'s PCIe root (Linux sysfs).
+
+    Pinned host buffers are placed on the NUMA node of the thread that first touches them,
+    and every host<->device copy crosses from that node to the GPU; a rank whose buffers sit
+    on the far socket pays the inter-socket link on every byte. Call this before allocating
+    the pinned buffers of :func:`sfa_fwd_bwd_from_host` (one process per GPU). Returns False
+    (and changes nothing) where the topology is not visible."""
+    import os
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    try:
+        prop = torch.cuda.get_device_properties(dev)
+        bus = "%04x:%02x:%02x.0" % (prop.pci_domain_id, prop.pci_bus_id, prop.pci_device_id)
+        with open(f"/sys/bus/pci/devices/{bus}/local_cpulist") as f:
+            cpus = _parse_cpulist(f.read()) & set(os.sched_getaffinity(0))
+        if not cpus:
+            return False
+        os.sched_setaffinity(0, cpus)
+        return True
+    except (OSError, ValueError, AttributeError):
+        return False
+
+
 def default_chunks(S1: int) -> int:
     """Chunks of about 512 rows, at least 8 and at most 16."""
     return max(8, min(16, S1 // 512))
