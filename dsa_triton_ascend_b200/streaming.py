@@ -55,8 +55,8 @@ def bind_host_to_device(device=None) -> bool:
     the pinned buffers of :func:`sfa_fwd_bwd_from_host` (one process per GPU). Returns False
     (and changes nothing) where the topology is not visible."""
     import os
-    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     try:
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         prop = torch.cuda.get_device_properties(dev)
         bus = "%04x:%02x:%02x.0" % (prop.pci_domain_id, prop.pci_bus_id, prop.pci_device_id)
         with open(f"/sys/bus/pci/devices/{bus}/local_cpulist") as f:
@@ -65,7 +65,7 @@ def bind_host_to_device(device=None) -> bool:
             return False
         os.sched_setaffinity(0, cpus)
         return True
-    except (OSError, ValueError, AttributeError):
+    except (OSError, ValueError, AttributeError, RuntimeError, AssertionError):
         return False
 
 

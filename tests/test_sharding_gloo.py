@@ -96,3 +96,14 @@ def test_two_rank_fwd_bwd_matches_single_rank():
     np.testing.assert_allclose(dq, rdq, rtol=1e-5, atol=1e-6)
     for g, r in zip(grads, (rdk, rdv, rdkr)):
         np.testing.assert_allclose(g, r, rtol=1e-4, atol=1e-5)
+
+
+def test_cpulist_parsing_and_binding_without_gpu():
+    from dsa_triton_ascend_b200.streaming import _parse_cpulist, bind_host_to_device
+    assert _parse_cpulist("0-3,8,10-11\n") == {0, 1, 2, 3, 8, 10, 11}
+    assert _parse_cpulist("") == set()
+    if not torch.cuda.is_available():
+        before = os.sched_getaffinity(0)
+        assert bind_host_to_device() is False
+        assert os.sched_getaffinity(0) == before
+
