@@ -24,9 +24,11 @@
 // the second half.  Valid indices are compacted by sfa_prep_kernel, so causal rows
 // with fewer than topK visible keys only pay for their valid keys.
 //
-// Warp roles (352 threads): warps 0 and 6 copy X -> H (warp 0 first loads Q); warp 1
+// Warp roles (512 threads): warps 0 and 6 copy X -> H (warp 0 first loads Q); warp 1
 // issues UMMA (pair leader) and owns TMEM; warps 2-5 run the online softmax, the lazy O
-// rescale and the epilogue; warps 7-10 gather the QK^T keys with TMA gather4.
+// rescale and the epilogue; warps 7-15 gather the QK^T keys with TMA gather4, one 64-dim
+// chunk each.  Rows with few keys per SM (decode) are split into key ranges whose fp32
+// partials sfa_fwd_combine_kernel merges.
 
 #include <cuda_runtime.h>
 #include <stdint.h>

@@ -16,7 +16,8 @@
 //   teacher : CTA pair per row.  2-SM UMMA with M = 256 keys (128 per CTA) and N = 128
 //             query heads (Q split 64/64 across the pair), so each thread of the epilogue
 //             owns one key and all 128 head scores of it: p[k] is a per-thread sum.
-//             Keys stream through a ring of 64-dim chunks (cp.async gathers).
+//             Keys stream through a ring of 64-dim chunks (TMA gather4, 2-SM form, issued
+//             by 8 warps).
 //   index   : one CTA per row.  Pass A: I = KI QI^T (UMMA, keys as M) -> softmax, dI, loss.
 //             Pass B: recompute ReLU(KI QI^T), form C in shared memory, then dQI^T += KI^T C
 //             and dKI_tile = C QI on tcgen05; dKI rows are scatter-added in fp32 with
