@@ -475,13 +475,20 @@ __global__ void __launch_bounds__(kIThreads, 1)
     const uint32_t lane_addr = (uint32_t)(32 * qd) << 16;
     float* stage = reinterpret_cast<float*>(smem_raw + C::kOffStage) + (warp - kIDrain0) * 32 * 33;
     float* acc_out = a.dki_acc;
+    // accumulator row of this thread's key in tile t (-1: none); the next tile's is loaded
+    // while the current tile drains
+    auto key_row = [&](int t) {
+      const int my_key = kIKeys * t + 32 * qd + lane;
+      return my_key < n ? key_row_of(a, b, row, my_key) : -1;
+    };
+    int next_row = ntiles > 0 ? key_row(0) : -1;
     for (int t = 0; t < ntiles; ++t) {
       const int db = t & 1;
+      const int my_row = next_row;
+      if (t + 1 < ntiles) next_row = key_row(t + 1);
       mbar_wait(smem_u32(&bars.dfull[db]), (t >> 1) & 1, a.err, &failed);
       const bool dfail = __any_sync(0xffffffffu, failed);
       tc_fence_after();
-      const int my_key = kIKeys * t + 32 * qd + lane;
-      const int my_row = my_key < n ? key_row_of(a, b, row, my_key) : -1;
       if (!dfail) {
         for (int c0 = 64 * half; c0 < 64 * half + 64; c0 += 32) {
           uint32_t r[32];
