@@ -83,3 +83,20 @@ def test_bwd_rejects_misaligned_workspace_without_gpu_work(lib):
     g.restype = ctypes.c_int
     g.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
     assert g(ctypes.addressof(p), None) == 1   # DSA_ERR_INVALID_ARG
+
+
+def test_fast_forward_workspace_only_grows_for_split_calls(lib):
+    """dsa_sfa_fwd_fast_workspace_size adds room for key-split partials only for calls with
+    fewer rows than the 74 CTA pairs a B200 runs at once and enough tiles to split."""
+    base = lib.dsa_sfa_fwd_workspace_size
+    base.restype, base.argtypes = ctypes.c_int64, [ctypes.c_int64] * 3
+    fast = lib.dsa_sfa_fwd_fast_workspace_size
+    fast.restype, fast.argtypes = ctypes.c_int64, [ctypes.c_int64] * 5
+    # decode: 32 rows, top-2048 -> 2 splits of 16 tiles
+    assert fast(32, 128, 512, 2048, 1) >= base(32, 2048, 1) + 32 * 2 * 128 * (512 + 4) * 4
+    # one row: as many splits as 4-tile pieces allow (32 tiles -> 8)
+    assert fast(1, 128, 512, 2048, 1) >= base(1, 2048, 1) + 8 * 128 * (512 + 4) * 4
+    # prefill (many rows) and short rows (fewer than 8 tiles): no split, the minimum
+    assert fast(8192, 128, 512, 2048, 1) == base(8192, 2048, 1)
+    assert fast(16, 128, 512, 256, 1) == base(16, 256, 1)
+    assert fast(-1, 128, 512, 2048, 1) == -1 and fast(4, 0, 512, 2048, 1) == -1
