@@ -377,6 +377,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         m_ref = mnew;
       }
       const float off = m_ref * c2;
+      l_part *= factor;   // earlier tiles' sum onto the new reference (factor 1 unless rescaling)
       uint32_t pk[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
@@ -390,7 +391,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (__any_sync(0xffffffffu, rescale)) {
         if (t >= 1)
           mbar_wait(smem_u32(&bars.pv_done[s ^ 1]), (uint32_t)((t - 1) >> 1) & 1u, a.err, &failed);
-        l_part *= factor;
         if (!__any_sync(0xffffffffu, failed)) {
           tc_fence_after();
           for (int cc = 0; cc < D / 2; cc += 16) {

@@ -137,6 +137,41 @@ def test_fwd_split_rows_match_oracle():
     assert np.all(out[1, 2] == 0) and np.all(mx[1, 0, 2] == 0) and np.all(sm[1, 0, 2] == 0)
 
 
+@pytest.mark.parametrize("S1,N1", [(80, 16), (4, 128)], ids=["one_pair_per_row", "split_rows"])
+def test_fwd_running_max_rescale(S1, N1):
+    """Later key tiles score far above the first ones (the rope part of keys past position
+    600 scaled by 20, ids sorted ascending), so the running max grows by more than the
+    lazy-rescale threshold and O and the row sum move onto a new exponent reference mid-row.
+    80 rows run one CTA pair per row; 4 rows are split over several pairs whose partials are
+    merged.
+
+    The softmax is then so peaked that bf16 rounding of the unnormalised probabilities
+    (relative error <= 2^-8 each, whatever exponent reference they are taken against)
+    dominates the output error, so the output is checked against an exact float64 softmax
+    with the bound that rounding allows: |O - O_exact| <= 2^-7 (sum_i p_i |v_i| / l +
+    |O_exact|) + 1e-3 (P rounding, the bf16 output, a factor 2 of margin). The statistics
+    are fp32 quantities and keep the oracle's tolerance."""
+    c = I.sfa_case(1, S1, 2048, N1, 512, 1024, 1, 0, "bf16", seed=41)
+    c["kr"][:, 600:] = I.cast(c["kr"][:, 600:] * 20.0, "bf16")
+    out, mx, sm = _run(c, "bf16", 0)
+    _, rm, rs = sfa.sfa_fwd(c["q"], c["k"], c["qr"], c["kr"], c["si"], c["scale"], sparse_mode=0,
+                            rounding="kernel")
+    _stats_close(mx, rm, sm, rs, "rescale")
+    for s1 in range(S1):
+        pos = c["si"][0, s1, 0]
+        pos = pos[pos >= 0]
+        kk = np.concatenate([c["k"][0, pos, 0], c["kr"][0, pos, 0]], 1).astype(np.float64)
+        qf = np.concatenate([c["q"][0, s1], c["qr"][0, s1]], 1).astype(np.float64)
+        sc = qf @ kk.T * c["scale"]
+        p = np.exp(sc - sc.max(1, keepdims=True))
+        l = p.sum(1, keepdims=True)
+        v = kk[:, :512]
+        exact, mag = (p @ v) / l, (p @ np.abs(v)) / l
+        err = np.abs(out[0, s1].astype(np.float64) - exact)
+        bound = 2.0 ** -7 * (mag + np.abs(exact)) + 1e-3
+        assert np.all(err <= bound), f"row {s1}: worst excess {float((err - bound).max()):.3g}"
+
+
 def test_fwd_paged_decode_split():
     """Decode-shaped PA_BSND call (one query token per sequence, 2048 keys each): split."""
     from dsa_triton_ascend_b200 import sparse_flash_attention_triton, check_device_errors
