@@ -9,14 +9,20 @@ Drop-in for the operators of 18851871668/dsa_triton_ascend, on CUDA torch tensor
   :class:`SparseLightningIndexerGradKLLossTriton`
 
 plus :func:`sfa_fwd_bwd_from_host` (forward + backward of host-resident inputs, with the
-copies overlapped with the kernels) and the autograd functions of :mod:`.autograd`.
+copies overlapped with the kernels), :func:`lightning_indexer_paged` (the indexer over a
+paged key cache, which the reference's indexer rejects) and the autograd functions of
+:mod:`.autograd`.
 """
 from ._lib import check_device_errors, lib as _load_library  # noqa: F401
 from .sparse_flash_attention import (  # noqa: F401
     SparseFlashAttentionTriton,
     sparse_flash_attention_triton,
 )
-from .lightning_indexer import LightningIndexerTriton, lightning_indexer_triton  # noqa: F401
+from .lightning_indexer import (  # noqa: F401
+    LightningIndexerTriton,
+    lightning_indexer_paged,
+    lightning_indexer_triton,
+)
 from .sparse_lightning_indexer_grad_kl_loss import (  # noqa: F401
     SparseLightningIndexerGradKLLossTriton,
     sparse_lightning_indexer_grad_kl_loss_triton,

@@ -73,6 +73,7 @@ class LiParams(ctypes.Structure):
         ("kv_rows", _i64), ("sparse_count", _i64), ("s2_row", _i64), ("s2_cap", _i64),
         ("q_len_max", _i64), ("q_len_dense", _i64),
         ("sparse_mode", ctypes.c_int32), ("dtype", ctypes.c_int32), ("weights_dtype", ctypes.c_int32),
+        ("block_table", _p), ("page_size", _i64), ("max_blocks", _i64),
     ]
 
 

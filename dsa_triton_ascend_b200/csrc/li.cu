@@ -43,6 +43,11 @@ struct Args {
   int* err;
   int B, N1, N2, G, D, Tq, N, nblk, q_rows_max, s2_row, s2_cap, sparse_mode, w_dtype;
   int q_len_dense;          // >0: BSND query, every batch has this many rows
+  // paged keys (block_table != NULL): position s2 of batch b is pool row
+  // block_table[b][s2 / page] * page + s2 % page; a tile of 128 keys is fetched as boxes of
+  // box_rows rows (box_rows = min(page, 128), so a box never crosses a block)
+  const int32_t* block_table;
+  int page, max_blocks, box_rows;
 };
 
 __device__ __forceinline__ float load_w(const void* w, int dtype, size_t i) {
@@ -104,7 +109,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nrows_b = a.q_len_dense > 0 ? a.q_len_dense : aq;
   if (s1_0 >= nrows_b) return;   // uniform
   const int qbase = __ldg(a.q_row_base + b);
-  const int kbase = __ldg(a.k_row_base + b);
+  const int kbase = a.block_table == nullptr ? __ldg(a.k_row_base + b) : 0;
   const int N = a.N, G = a.G, Tq = a.Tq;
 
   // ---- per token: visible limit and query row; block key range ----
@@ -175,9 +180,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(smem_u32(&bars.empty[s]), ((t / C::kStages) & 1) ^ 1, a.err, &failed)) break;
         const uint32_t fb = smem_u32(&bars.full[s]);
         mbar_arrive_expect_tx(fb, C::kStageBytes);
-        for (int c = 0; c < C::kChunks; ++c)
-          tma_load_3d(sK + s * C::kStageBytes + c * kKeys * 128, &kmap, fb, 64 * c, n2,
-                      kbase + kKeys * t);
+        if (a.block_table == nullptr) {
+          for (int c = 0; c < C::kChunks; ++c)
+            tma_load_3d(sK + s * C::kStageBytes + c * kKeys * 128, &kmap, fb, 64 * c, n2,
+                        kbase + kKeys * t);
+        } else {
+          for (int r0 = 0; r0 < kKeys; r0 += a.box_rows) {
+            const int tok = kKeys * t + r0;
+            const int pidx = tok / a.page;
+            // no block: a box that lies wholly before the pool, which the TMA unit fills
+            // with zeros (those positions are past the row's visible keys anyway)
+            int prow = -a.box_rows;
+            if (pidx < a.max_blocks) {
+              const int blk = __ldg(a.block_table + (size_t)b * a.max_blocks + pidx);
+              if (blk >= 0) prow = blk * a.page + tok % a.page;
+            }
+            for (int c = 0; c < C::kChunks; ++c)
+              tma_load_3d(sK + s * C::kStageBytes + c * kKeys * 128 + r0 * 128, &kmap, fb, 64 * c,
+                          n2, prow);
+          }
+        }
       }
     }
     __syncwarp();
@@ -309,6 +331,7 @@ struct TopkArgs {
   void* out_val;            // [q_rows][N2][K] query dtype, or NULL
   int* err;
   int B, N2, K, KP, s2_row, s2_cap, sparse_mode, q_rows, q_len_dense, val_dtype;
+  int keys_in_gmem;         // 1: rows too long for shared memory are read from `scores` per pass
 };
 
 // Block-wide exclusive scan of one int per thread (kTopkThreads threads); returns the
@@ -408,8 +431,10 @@ __device__ __forceinline__ void bitonic_desc(unsigned long long* sel) {
 template <typename T>
 __global__ void __launch_bounds__(kTopkThreads, 2) li_topk_kernel(const TopkArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
+  const bool gmem = a.keys_in_gmem != 0;
   uint32_t* keys = reinterpret_cast<uint32_t*>(smem_raw);                       // s2_row
-  unsigned long long* sel = reinterpret_cast<unsigned long long*>(smem_raw + ((a.s2_row * 4 + 15) / 16) * 16);
+  unsigned long long* sel = reinterpret_cast<unsigned long long*>(
+      smem_raw + (gmem ? 0 : ((a.s2_row * 4 + 15) / 16) * 16));
   __shared__ int hist[256];
   __shared__ int warp_sums[32];
   __shared__ int s_digit, s_above;
@@ -426,13 +451,17 @@ __global__ void __launch_bounds__(kTopkThreads, 2) li_topk_kernel(const TopkArgs
   if (a.q_len_dense <= 0 && s1 >= aq) lim = 0;
   lim = min(lim, a.s2_row);
   const float* src = a.scores + ((size_t)row * a.N2 + n2) * a.s2_row;
-  for (int i = threadIdx.x; i < lim; i += kTopkThreads) keys[i] = order_key(src[i]);
+  if (!gmem)
+    for (int i = threadIdx.x; i < lim; i += kTopkThreads) keys[i] = order_key(src[i]);
   __syncthreads();
+  // order-preserving key of score i: from shared memory, or from the score row (L2) when
+  // the row does not fit
+  auto key_at = [&](int i) -> uint32_t { return gmem ? order_key(__ldg(src + i)) : keys[i]; };
   const int K = a.K;
   int nsel;
   if (lim <= K) {
     for (int i = threadIdx.x; i < lim; i += kTopkThreads)
-      sel[i] = ((unsigned long long)keys[i] << 32) | (uint32_t)(~(uint32_t)i);
+      sel[i] = ((unsigned long long)key_at(i) << 32) | (uint32_t)(~(uint32_t)i);
     nsel = lim;
   } else {
     // radix select: after the 4 passes `prefix` is the key of the K-th largest element
@@ -442,7 +471,7 @@ __global__ void __launch_bounds__(kTopkThreads, 2) li_topk_kernel(const TopkArgs
       for (int i = threadIdx.x; i < 256; i += kTopkThreads) hist[i] = 0;
       __syncthreads();
       for (int i = threadIdx.x; i < lim; i += kTopkThreads) {
-        const uint32_t k = keys[i];
+        const uint32_t k = key_at(i);
         if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255], 1);
       }
       __syncthreads();
@@ -489,7 +518,7 @@ __global__ void __launch_bounds__(kTopkThreads, 2) li_topk_kernel(const TopkArgs
     int gt_base = 0, eq_base = 0;
     for (int base = 0; base < lim; base += kTopkThreads) {
       const int i = base + threadIdx.x;
-      const uint32_t k = i < lim ? keys[i] : 0u;
+      const uint32_t k = i < lim ? key_at(i) : 0u;
       const int is_gt = (i < lim && k > thr) ? 1 : 0;
       const int is_eq = (i < lim && k == thr) ? 1 : 0;
       // one scan for both counts (each at most kTopkThreads, so 16 bits apiece)
@@ -569,9 +598,10 @@ int launch(const DsaLiParams* p, cudaStream_t stream) {
   if (Tq < 1) return DSA_ERR_INVALID_ARG;
   const int N = ((Tq * G + 15) / 16) * 16;
   CUtensorMap kmap;
-  // key viewed as {D, N2, kv_rows}; box {64, 1, 128}
+  const int box_rows = p->block_table ? (int)(p->page_size < kKeys ? p->page_size : kKeys) : kKeys;
+  // key viewed as {D, N2, kv_rows}; box {64, 1, box_rows}
   if (!make_tmap_3d_16b(&kmap, p->key, bf16, p->d, p->n2, p->kv_rows, (uint64_t)p->d * 2,
-                        (uint64_t)p->n2 * p->d * 2, 64, 1, kKeys))
+                        (uint64_t)p->n2 * p->d * 2, 64, 1, box_rows))
     return DSA_ERR_TMA_DESCRIPTOR;
   Args a;
   a.q = p->query;
@@ -596,6 +626,10 @@ int launch(const DsaLiParams* p, cudaStream_t stream) {
   a.sparse_mode = p->sparse_mode;
   a.w_dtype = p->weights_dtype;
   a.q_len_dense = (int)p->q_len_dense;
+  a.block_table = p->block_table;
+  a.page = (int)p->page_size;
+  a.max_blocks = (int)p->max_blocks;
+  a.box_rows = box_rows;
   int rc;
   if (N == 256 && G == 64) rc = launch_score<DP, T, 64>(kmap, a, p->batch, p->n2, stream);
   else if (N == 256 && G == 32) rc = launch_score<DP, T, 32>(kmap, a, p->batch, p->n2, stream);
@@ -622,8 +656,11 @@ int launch(const DsaLiParams* p, cudaStream_t stream) {
   t.sparse_mode = p->sparse_mode;
   t.q_rows = (int)p->q_rows;
   t.q_len_dense = (int)p->q_len_dense;
-  const int tsmem = ((t.s2_row * 4 + 15) / 16) * 16 + kp * 8;
-  if (tsmem > 200 * 1024) return DSA_ERR_INVALID_ARG;
+  // the row's keys stay in shared memory when they fit; longer rows (decode-length key
+  // caches) are read from the score matrix in each pass
+  const int64_t tsmem_row = ((int64_t)t.s2_row * 4 + 15) / 16 * 16 + (int64_t)kp * 8;
+  t.keys_in_gmem = tsmem_row > 200 * 1024 ? 1 : 0;
+  const int tsmem = t.keys_in_gmem ? kp * 8 : (int)tsmem_row;
   if (cudaFuncSetAttribute(li_topk_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, tsmem) !=
       cudaSuccess)
     return DSA_ERR_CUDA;
@@ -643,7 +680,12 @@ extern "C" int dsa_li_score_topk(const DsaLiParams* p, void* stream_) {
   using namespace dsa::li;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   if (!p || !p->query || !p->key || !p->weights || !p->act_q || !p->act_k || !p->q_row_base ||
-      !p->k_row_base || !p->out_indices || !p->workspace)
+      (!p->k_row_base && !p->block_table) || !p->out_indices || !p->workspace)
+    return DSA_ERR_INVALID_ARG;
+  if (p->block_table &&
+      (p->max_blocks < 1 || p->page_size < 8 ||
+       (p->page_size % kKeys != 0 && kKeys % p->page_size != 0) ||
+       p->max_blocks * p->page_size > (int64_t)1 << 30 || p->kv_rows > (int64_t)1 << 30))
     return DSA_ERR_INVALID_ARG;
   if (p->n1 < 1 || p->n2 < 1 || p->n1 % p->n2 != 0 || p->n1 / p->n2 > 256 || p->d < 16 ||
       p->d > 256 || p->d % 8 != 0 || p->sparse_count < 1 || p->sparse_count > 4096 ||

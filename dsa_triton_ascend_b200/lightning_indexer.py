@@ -110,6 +110,96 @@ def lightning_indexer_triton(
     return indices, values
 
 
+def lightning_indexer_paged(
+    query: torch.Tensor,
+    key_cache: torch.Tensor,
+    weights: torch.Tensor,
+    block_table: torch.Tensor,
+    actual_seq_lengths_query=None,
+    actual_seq_lengths_key=None,
+    layout_query="BSND",
+    sparse_count=2048,
+    sparse_mode=3,
+    return_value=False,
+):
+    """Lightning indexer over a paged key cache (the decode-time indexer).
+
+    No counterpart in the reference, whose indexer rejects ``block_table``
+    (lightning_indexer_triton.py:497-498); the scores, masks, tie order and outputs are those
+    of ``lightning_indexer_triton``.  ``key_cache`` is a block pool [num_blocks, page_size,
+    N2, D]; ``block_table`` [B, max_blocks] int32 maps position s2 of batch b to block
+    ``block_table[b, s2 // page_size]``, row ``s2 % page_size``.  ``actual_seq_lengths_key``
+    gives each batch's key length (default: max_blocks * page_size, which is also the length
+    of a score row).  ``query`` is BSND [B, S1, N1, D] or TND [T1, N1, D] with cumulative
+    ``actual_seq_lengths_query``.  page_size is a multiple of 128, or divides 128 and is at
+    least 8.  Rows longer than about 50k keys are selected from the score matrix in global
+    memory instead of shared memory.
+    """
+    if sparse_mode not in (0, 3):
+        raise ValueError("Only sparse_mode 0 (full) / 3 (rightDownCausal) supported")
+    H.require_cuda(query, key_cache, weights, block_table)
+    if key_cache.dim() != 4:
+        raise ValueError("key_cache must be [num_blocks, page_size, N2, D]")
+    if block_table.dim() != 2 or block_table.dtype != torch.int32:
+        raise ValueError("block_table must be an int32 [B, max_blocks] tensor")
+    nblocks, page, N2, Dk = key_cache.shape
+    if page < 8 or (page % 128 != 0 and 128 % page != 0):
+        raise ValueError(f"page_size ({page}) must be a multiple of 128 or divide 128 (>= 8)")
+    dev = query.device
+    B, max_blocks = block_table.shape
+    s2 = max_blocks * page
+    if layout_query == "TND":
+        cum_q = H.cumulative(actual_seq_lengths_query, dev)
+        if cum_q.numel() != B:
+            raise ValueError("actual_seq_lengths_query must have one entry per block_table row")
+        q_base, act_q = H.tnd_offsets(cum_q)
+        T1, N1, D = query.shape
+        q_rows, q_len_dense = T1, 0
+        q_len_max = int(act_q.max().item()) if B > 0 else 0
+        out_shape = (T1, N2, int(sparse_count))
+    else:
+        Bq, S1, N1, D = query.shape
+        if Bq != B:
+            raise ValueError("query batch and block_table rows differ")
+        q_rows, q_len_max, q_len_dense = B * S1, S1, S1
+        q_base = H.row_bases(B, S1, dev)
+        act_q = H.lens_tensor(actual_seq_lengths_query, B, S1, dev)
+        out_shape = (B, S1, N2, int(sparse_count))
+    act_k = H.lens_tensor(actual_seq_lengths_key, B, s2, dev)
+    if N1 % N2 != 0:
+        raise ValueError(f"N1({N1}) must be divisible by N2({N2})")
+    if Dk != D or key_cache.dtype != query.dtype:
+        raise ValueError("query and key_cache must share dtype and head dim")
+    K = int(sparse_count)
+    if K > s2:
+        raise ValueError(f"sparse_count ({K}) exceeds the block table's capacity ({s2})")
+    q = query.contiguous()
+    k = key_cache.contiguous()
+    w = weights.contiguous()
+    bt = block_table.contiguous()
+    indices = torch.empty(out_shape, dtype=torch.int32, device=dev)
+    values = (torch.empty(out_shape, dtype=query.dtype, device=dev) if return_value
+              else torch.zeros(out_shape, dtype=query.dtype, device=dev))
+    ws_bytes = lib().dsa_li_workspace_size(q_rows, N2, s2)
+    ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=dev)
+    p = LiParams()
+    p.query, p.key, p.weights = ptr(q), ptr(k), ptr(w)
+    p.act_q, p.act_k, p.q_row_base, p.k_row_base = ptr(act_q), ptr(act_k), ptr(q_base), 0
+    p.out_indices = ptr(indices)
+    p.out_values = ptr(values) if return_value else 0
+    p.error_flag = ptr(error_flag(dev))
+    p.workspace, p.workspace_bytes = ptr(ws), ws_bytes
+    p.q_rows, p.batch, p.n1, p.n2, p.d, p.kv_rows = q_rows, B, N1, N2, D, nblocks * page
+    p.sparse_count, p.s2_row, p.s2_cap = K, s2, s2
+    p.q_len_max, p.q_len_dense = q_len_max, q_len_dense
+    p.sparse_mode = int(sparse_mode)
+    p.dtype = H.dtype_code(query)
+    p.weights_dtype = _weights_code(w)
+    p.block_table, p.page_size, p.max_blocks = ptr(bt), page, max_blocks
+    check(lib().dsa_li_score_topk(p, stream_ptr(dev)), "dsa_li_score_topk")
+    return indices, values
+
+
 class LightningIndexerTriton(torch.nn.Module):
     """Module wrapper (reference cell: lightning_indexer_triton.py:416-459)."""
 

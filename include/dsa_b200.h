@@ -218,6 +218,12 @@ int64_t dsa_sfa_bwd_workspace_size(int64_t num_rows, int64_t topk, int64_t spars
  * (rows s1 >= act_q exist but see nothing); a TND caller passes q_len_dense = 0 (a batch has
  * act_q rows).  q_len_max = largest row count of a batch.  s2_row = length of a score row
  * (>= sparse_count).  Workspace: dsa_li_workspace_size() bytes (the fp32 score matrix).
+ * Paged keys (no counterpart in the reference, whose indexer rejects block_table at
+ * lightning_indexer_triton.py:497-498): with block_table != NULL, key is a block pool
+ * [kv_rows = blocks * page_size][n2][d] and key position s2 of batch b is pool row
+ * block_table[b * max_blocks + s2 / page_size] * page_size + s2 % page_size (k_row_base is
+ * not read).  page_size is a multiple of 128 or divides 128 and is at least 8.  Blocks past
+ * a row's visible keys are never read for its scores; a negative id reads zeros.
  */
 typedef struct DsaLiParams {
   const void* query;
@@ -246,6 +252,9 @@ typedef struct DsaLiParams {
   int32_t sparse_mode;
   int32_t dtype;
   int32_t weights_dtype;
+  const int32_t* block_table;   /* NULL: dense keys at k_row_base; else [batch][max_blocks] */
+  int64_t page_size;
+  int64_t max_blocks;
 } DsaLiParams;
 
 int dsa_li_score_topk(const DsaLiParams* params, void* stream);
