@@ -90,6 +90,19 @@ class SliParams(ctypes.Structure):
     ]
 
 
+class DenseIndexerParams(ctypes.Structure):
+    _fields_ = [
+        ("query", _p), ("key", _p), ("query_rope", _p), ("key_rope", _p), ("query_index", _p),
+        ("key_index", _p), ("weights", _p), ("softmax_max", _p), ("softmax_sum", _p),
+        ("index_max", _p), ("index_sum", _p), ("act_q", _p), ("act_k", _p),
+        ("d_query_index", _p), ("d_key_index", _p), ("d_weights", _p), ("loss", _p),
+        ("workspace", _p), ("workspace_bytes", _i64),
+        ("batch", _i64), ("s1", _i64), ("s2", _i64), ("n1", _i64), ("n2", _i64), ("d", _i64),
+        ("d_rope", _i64), ("n_index", _i64), ("d_index", _i64),
+        ("scale", ctypes.c_float), ("dtype", ctypes.c_int32), ("weights_dtype", ctypes.c_int32),
+    ]
+
+
 _lock = threading.Lock()
 _lib = None
 _err_bufs: dict = {}
@@ -129,6 +142,11 @@ def lib() -> ctypes.CDLL:
                 l.dsa_sli_grad.restype = ctypes.c_int
                 l.dsa_sli_workspace_size.argtypes = [_i64, _i64, _i64]
                 l.dsa_sli_workspace_size.restype = _i64
+                for fn in (l.dsa_dense_indexer_softmax_lse, l.dsa_dense_indexer_grad_kl_loss):
+                    fn.argtypes = [ctypes.POINTER(DenseIndexerParams), _p]
+                    fn.restype = ctypes.c_int
+                l.dsa_dense_indexer_workspace_size.argtypes = [_i64] * 4
+                l.dsa_dense_indexer_workspace_size.restype = _i64
                 _lib = l
     return _lib
 

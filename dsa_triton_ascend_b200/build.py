@@ -14,7 +14,7 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libdsa_b200.so")
-SOURCES = ["capi.cu", "sfa_fwd.cu", "sfa_bwd.cu", "li.cu", "sli.cu"]
+SOURCES = ["capi.cu", "sfa_fwd.cu", "sfa_bwd.cu", "li.cu", "sli.cu", "dense.cu"]
 FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17", "-lineinfo",
          "-Xcompiler", "-fPIC", "-shared", "--expt-relaxed-constexpr"]
 

@@ -310,6 +310,60 @@ typedef struct DsaSliParams {
 int dsa_sli_grad(const DsaSliParams* params, void* stream);
 int64_t dsa_sli_workspace_size(int64_t batch, int64_t s1, int64_t topk);
 
+/*
+ * Dense lightning-indexer KL loss: the indexer loss over every visible key of a query row
+ * (BSND, sparse_mode 3).  Replaces the reference's dense path: `_dense_index_stats_core` and
+ * `_dense_loss_backward_core` / `_dense_loss_backward_with_index_core` with their kernels
+ * (dense_loss_backward_triton.py:129-397, :410-646).
+ *   query [batch*s1][n1][d], key [batch*s2][n2][d], query_rope / key_rope [..][64] or NULL
+ *   (d_rope 0 / 64), query_index [batch*s1][n_index][d_index], key_index [batch*s2][d_index],
+ *   weights [batch*s1][n_index] (query dtype or fp32), softmax_max / softmax_sum
+ *   [batch][n2][s1][n1/n2] fp32 (statistics of the full attention), act_q / act_k [batch].
+ * dsa_dense_indexer_softmax_lse writes index_max / index_sum [batch*s1] (max of the index
+ * scores over the visible keys and the sum of exp(score - max); -inf / 0 for a row without
+ * visible keys).  dsa_dense_indexer_grad_kl_loss reads them and writes d_query_index
+ * (query_index dtype), d_weights (weights dtype), loss [1] fp32 (sum over rows, zeroed by the
+ * call) and, if d_key_index != NULL, the key_index gradient in its dtype.  n_index <= 128,
+ * d_index <= 512 (multiples of 8).  Workspace: dsa_dense_indexer_workspace_size() bytes.
+ */
+typedef struct DsaDenseIndexerParams {
+  const void* query;
+  const void* key;
+  const void* query_rope;
+  const void* key_rope;
+  const void* query_index;
+  const void* key_index;
+  const void* weights;
+  const float* softmax_max;
+  const float* softmax_sum;
+  float* index_max;
+  float* index_sum;
+  const int32_t* act_q;
+  const int32_t* act_k;
+  void* d_query_index;
+  void* d_key_index;
+  void* d_weights;
+  float* loss;
+  void* workspace;
+  int64_t workspace_bytes;
+  int64_t batch;
+  int64_t s1;
+  int64_t s2;
+  int64_t n1;
+  int64_t n2;
+  int64_t d;
+  int64_t d_rope;
+  int64_t n_index;
+  int64_t d_index;
+  float scale;
+  int32_t dtype;
+  int32_t weights_dtype;
+} DsaDenseIndexerParams;
+
+int dsa_dense_indexer_softmax_lse(const DsaDenseIndexerParams* params, void* stream);
+int dsa_dense_indexer_grad_kl_loss(const DsaDenseIndexerParams* params, void* stream);
+int64_t dsa_dense_indexer_workspace_size(int64_t batch, int64_t s1, int64_t s2, int64_t d_index);
+
 #ifdef __cplusplus
 }
 #endif

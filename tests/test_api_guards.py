@@ -81,3 +81,43 @@ def test_modules_forward_to_functions():
         m(*sfa_args(), query_rope=t(1, 2, 8, 64), key_rope=t(1, 16, 1, 64))
     assert dsa.LightningIndexerTriton().sparse_mode == 3
     assert dsa.SparseFlashAttentionGradTriton().sparse_mode == 3
+
+
+def _dense_args(**over):
+    B, S1, S2, N1, N2, D, Ni, Di = 1, 2, 64, 32, 32, 128, 32, 128
+    a = dict(query=t(B, S1, N1, D, dtype=torch.float16), key=t(B, S2, N2, D, dtype=torch.float16),
+             query_index=t(B, S1, Ni, Di, dtype=torch.float16),
+             key_index=t(B, S2, 1, Di, dtype=torch.float16), weights=t(B, S1, Ni, dtype=torch.float16),
+             softmax_max=t(B, N2, S1, N1 // N2, dtype=torch.float32),
+             softmax_sum=t(B, N2, S1, N1 // N2, dtype=torch.float32))
+    a.update(over)
+    return a
+
+
+@pytest.mark.parametrize("over,exc,msg", [
+    (dict(layout="TND"), ValueError, "BSND"),
+    (dict(sparse_mode=0), ValueError, "sparse_mode"),
+    (dict(query_index=t(1, 2, 48, 128, dtype=torch.float16),
+          weights=t(1, 2, 48, dtype=torch.float16)), ValueError, "Nidx1"),
+    (dict(key=t(1, 64, 32, 128, dtype=torch.bfloat16)), TypeError, "share dtype"),
+    (dict(softmax_max=t(1, 32, 2, 1, dtype=torch.float16)), TypeError, "float32"),
+    (dict(softmax_sum=t(1, 1, 2, 32, dtype=torch.float32)), ValueError, "softmax_max"),
+    (dict(query_rope=t(1, 2, 32, 64, dtype=torch.float16)), ValueError, "both"),
+    (dict(softmax_max_index=t(1, 1, 2, dtype=torch.float32)), ValueError, "both"),
+])
+def test_dense_loss_guards(over, exc, msg):
+    """dense_loss_backward_triton.py:649-749, :785-791"""
+    a = _dense_args(**{k: v for k, v in over.items() if k not in ("layout", "sparse_mode")})
+    kw = {k: v for k, v in over.items() if k in ("layout", "sparse_mode")}
+    with pytest.raises(exc, match=msg):
+        dsa.dense_loss_backward_triton(**a, **kw)
+
+
+def test_dense_lse_guards():
+    qi, ki, w = t(1, 2, 32, 128), t(1, 64, 1, 128), t(1, 2, 32)
+    with pytest.raises(ValueError, match="key_index"):
+        dsa.dense_lightning_indexer_softmax_lse_triton(qi, t(1, 64, 2, 128), w)
+    with pytest.raises(ValueError, match="D_idx"):
+        dsa.dense_lightning_indexer_softmax_lse_triton(t(1, 2, 32, 64), t(1, 64, 1, 64), w)
+    with pytest.raises(ValueError, match="CUDA"):
+        dsa.dense_lightning_indexer_softmax_lse_triton(qi, ki, w)
