@@ -10,7 +10,8 @@ Drop-in for the operators of 18851871668/dsa_triton_ascend, on CUDA torch tensor
 
 plus :func:`sfa_fwd_bwd_from_host` (forward + backward of host-resident inputs, with the
 copies overlapped with the kernels), :func:`lightning_indexer_paged` (the indexer over a
-paged key cache, which the reference's indexer rejects), the dense indexer KL loss of
+paged key cache, which the reference's indexer rejects), :func:`lightning_indexer_fp8` (the
+FP8 indexer), the dense indexer KL loss of
 :mod:`.dense_indexer_loss` (``dense_loss_backward_triton`` and its softmax-LSE helper) and
 the autograd functions of :mod:`.autograd`.
 """
@@ -21,6 +22,7 @@ from .sparse_flash_attention import (  # noqa: F401
 )
 from .lightning_indexer import (  # noqa: F401
     LightningIndexerTriton,
+    lightning_indexer_fp8,
     lightning_indexer_paged,
     lightning_indexer_triton,
 )

@@ -23,6 +23,7 @@ SFA_FWD_NOALLOC_SCRATCH_BYTES = 16 << 20   # DSA_SFA_FWD_NOALLOC_SCRATCH_BYTES
 DSA_DTYPE_BF16 = 0
 DSA_DTYPE_FP16 = 1
 DSA_DTYPE_FP32 = 2
+DSA_DTYPE_FP8_E4M3 = 3
 
 _ERR_TEXT = {
     DSA_ERR_INVALID_ARG: "invalid argument",
@@ -73,7 +74,7 @@ class LiParams(ctypes.Structure):
         ("kv_rows", _i64), ("sparse_count", _i64), ("s2_row", _i64), ("s2_cap", _i64),
         ("q_len_max", _i64), ("q_len_dense", _i64),
         ("sparse_mode", ctypes.c_int32), ("dtype", ctypes.c_int32), ("weights_dtype", ctypes.c_int32),
-        ("block_table", _p), ("page_size", _i64), ("max_blocks", _i64),
+        ("block_table", _p), ("page_size", _i64), ("max_blocks", _i64), ("key_scale", _p),
     ]
 
 

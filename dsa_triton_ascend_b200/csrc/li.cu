@@ -18,16 +18,55 @@
 // score over the visible prefix, ordered compaction (ties at the threshold taken in
 // ascending index order), then a bitonic sort by (score desc, index asc).  -inf slots
 // get index -1 (:353-355).  Values are returned in the query dtype (:541-542).
+//
+// FP8 indexer (no counterpart in the reference): e4m3 query and key with a positive fp32
+// scale per key row, score = key_scale * sum_g ReLU(q_g . k) * w_g (a query scale is folded
+// into the weights by the caller).  The same kernel with tcgen05.mma kind::f8f6f4 (fp32
+// accumulation): a 128-byte smem row holds 128 fp8 elements and one MMA takes 32 of them,
+// so the shared-memory layout and descriptors are those of the 16-bit path; values come
+// back in fp32.
 
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <type_traits>
 
 #include "dsa_b200.h"
 #include "sm100.cuh"
 #include "tma_host.h"
 
 namespace dsa {
+
+// fp8 (e4m3) query / key elements for the FP8 indexer, and fp32 output values
+template <>
+struct ElemTraits<__nv_fp8_e4m3> {
+  static constexpr bool kIsBf16 = false;
+  __device__ static __forceinline__ float to_f(__nv_fp8_e4m3 x) { return float(x); }
+  __device__ static __forceinline__ __nv_fp8_e4m3 from_f(float x) { return __nv_fp8_e4m3(x); }
+};
+template <>
+struct ElemTraits<float> {
+  static constexpr bool kIsBf16 = false;
+  __device__ static __forceinline__ float to_f(float x) { return x; }
+  __device__ static __forceinline__ float from_f(float x) { return x; }
+};
+
 namespace li {
+
+template <typename T>
+constexpr bool kIsFp8 = std::is_same<T, __nv_fp8_e4m3>::value;
+
+// tcgen05 MMA of e4m3 operands with fp32 accumulation (kind::f8f6f4; the instruction
+// descriptor's A / B format code 0 is E4M3, so idesc_f16(.., false, ..) encodes it)
+__device__ __forceinline__ void umma_e4m3(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 
 constexpr int kKeys = 128;          // keys per tile (UMMA M)
 constexpr int kThreads = 192;       // 0: TMA, 1: MMA + TMEM, 2-5: epilogue
@@ -48,6 +87,7 @@ struct Args {
   // box_rows rows (box_rows = min(page, 128), so a box never crosses a block)
   const int32_t* block_table;
   int page, max_blocks, box_rows;
+  const float* kscale;      // fp8 keys: per (key row, n2) scale, laid out like the key rows
 };
 
 __device__ __forceinline__ float load_w(const void* w, int dtype, size_t i) {
@@ -124,24 +164,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ---- Q block (N rows x DP, zero padded) and weights into smem ----
   const T* q = static_cast<const T*>(a.q);
   uint8_t* gQ = smem_raw + C::kOffQ;
-  for (int i = threadIdx.x; i < N * (DP / 8); i += kThreads) {
-    const int r = i / (DP / 8), piece = i % (DP / 8);
+  // 16-byte pieces: 8 elements of 16 bits or 16 of fp8; a 128-byte chunk holds kEpc elements
+  constexpr int kEP = 16 / (int)sizeof(T);
+  constexpr int kPieces = C::kChunks * 8;
+  constexpr int kEpc = 128 / (int)sizeof(T);
+  for (int i = threadIdx.x; i < N * kPieces; i += kThreads) {
+    const int r = i / kPieces, piece = i % kPieces;
     const int tq = r / G, g = r % G;
-    const int d0 = piece * 8;
+    const int d0 = piece * kEP;
     uint4 v = make_uint4(0, 0, 0, 0);
     const int s1 = s1_0 + tq;
     if (tq < Tq && s1 < nrows_b && d0 < a.D) {
       const T* src = q + ((size_t)(qbase + s1) * a.N1 + n2 * G + g) * a.D + d0;
-      if (d0 + 8 <= a.D) {
+      if (d0 + kEP <= a.D) {
         v = *reinterpret_cast<const uint4*>(src);
       } else {
-        T tmp[8];
-        for (int e = 0; e < 8; ++e) tmp[e] = d0 + e < a.D ? src[e] : ElemTraits<T>::from_f(0.f);
+        T tmp[kEP];
+        for (int e = 0; e < kEP; ++e) tmp[e] = d0 + e < a.D ? src[e] : ElemTraits<T>::from_f(0.f);
         v = *reinterpret_cast<const uint4*>(tmp);
       }
     }
-    const int c = d0 / 64, ch16 = (d0 % 64) / 8;
-    *reinterpret_cast<uint4*>(gQ + c * N * 128 + sw128_offset(r, ch16)) = v;
+    *reinterpret_cast<uint4*>(gQ + (piece / 8) * N * 128 + sw128_offset(r, piece % 8)) = v;
   }
   for (int r = threadIdx.x; r < N; r += kThreads) {
     const int tq = r / G, g = r % G, s1 = s1_0 + tq;
@@ -182,7 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(fb, C::kStageBytes);
         if (a.block_table == nullptr) {
           for (int c = 0; c < C::kChunks; ++c)
-            tma_load_3d(sK + s * C::kStageBytes + c * kKeys * 128, &kmap, fb, 64 * c, n2,
+            tma_load_3d(sK + s * C::kStageBytes + c * kKeys * 128, &kmap, fb, kEpc * c, n2,
                         kbase + kKeys * t);
         } else {
           for (int r0 = 0; r0 < kKeys; r0 += a.box_rows) {
@@ -196,7 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (blk >= 0) prow = blk * a.page + tok % a.page;
             }
             for (int c = 0; c < C::kChunks; ++c)
-              tma_load_3d(sK + s * C::kStageBytes + c * kKeys * 128 + r0 * 128, &kmap, fb, 64 * c,
+              tma_load_3d(sK + s * C::kStageBytes + c * kKeys * 128 + r0 * 128, &kmap, fb, kEpc * c,
                           n2, prow);
           }
         }
@@ -218,9 +261,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < C::kChunks; ++c)
 #pragma unroll
-          for (int u = 0; u < 4; ++u)
-            umma_f16<1>(tmem + 256 * buf, dk + (uint64_t)((c * kKeys * 128 + u * 32) >> 4),
-                        dq + (uint64_t)((c * N * 128 + u * 32) >> 4), id, (c | u) != 0);
+          for (int u = 0; u < 4; ++u) {   // 32 bytes of K per MMA (16 bf16 / fp16, 32 fp8)
+            const uint64_t ka = dk + (uint64_t)((c * kKeys * 128 + u * 32) >> 4);
+            const uint64_t qb = dq + (uint64_t)((c * N * 128 + u * 32) >> 4);
+            if constexpr (kIsFp8<T>) umma_e4m3(tmem + 256 * buf, ka, qb, id, (c | u) != 0);
+            else umma_f16<1>(tmem + 256 * buf, ka, qb, id, (c | u) != 0);
+          }
         umma_commit(smem_u32(&bars.empty[s]));
         umma_commit(smem_u32(&bars.tfull[buf]));
       }
@@ -236,11 +282,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool wfail = __any_sync(0xffffffffu, failed);
       tc_fence_after();
       const int key = kKeys * t + 32 * qd + lane;
+      // fp8 keys carry a positive per-key scale: key_scale * sum_g w_g ReLU(q_g . k)
+      float ks = 1.f;
+      if (a.kscale != nullptr && key < kmax) {
+        int krow = -1;
+        if (a.block_table == nullptr) {
+          krow = kbase + key;
+        } else if (key / a.page < a.max_blocks) {
+          const int blk = __ldg(a.block_table + (size_t)b * a.max_blocks + key / a.page);
+          if (blk >= 0) krow = blk * a.page + key % a.page;
+        }
+        ks = krow >= 0 ? __ldg(a.kscale + (size_t)krow * a.N2 + n2) : 0.f;
+      }
       auto emit = [&](int tq, float v) {
         const int lim = bars.lim[tq];
         if (lim >= 0 && key < a.s2_row) {
           float* dst = a.scores + ((size_t)bars.qrow[tq] * a.N2 + n2) * a.s2_row + key;
-          *dst = key < lim ? v : -INFINITY;
+          *dst = key < lim ? v * ks : -INFINITY;
         }
       };
       if constexpr (GF > 0) {
@@ -599,10 +657,14 @@ int launch(const DsaLiParams* p, cudaStream_t stream) {
   const int N = ((Tq * G + 15) / 16) * 16;
   CUtensorMap kmap;
   const int box_rows = p->block_table ? (int)(p->page_size < kKeys ? p->page_size : kKeys) : kKeys;
-  // key viewed as {D, N2, kv_rows}; box {64, 1, box_rows}
-  if (!make_tmap_3d_16b(&kmap, p->key, bf16, p->d, p->n2, p->kv_rows, (uint64_t)p->d * 2,
-                        (uint64_t)p->n2 * p->d * 2, 64, 1, box_rows))
-    return DSA_ERR_TMA_DESCRIPTOR;
+  // key viewed as {D, N2, kv_rows}; box {one 128-byte chunk, 1, box_rows}
+  const uint64_t esz = sizeof(T);
+  const bool mapped =
+      kIsFp8<T> ? make_tmap_3d_8b(&kmap, p->key, p->d, p->n2, p->kv_rows, (uint64_t)p->d,
+                                  (uint64_t)p->n2 * p->d, 128, 1, box_rows)
+                : make_tmap_3d_16b(&kmap, p->key, bf16, p->d, p->n2, p->kv_rows, p->d * esz,
+                                   (uint64_t)p->n2 * p->d * esz, 64, 1, box_rows);
+  if (!mapped) return DSA_ERR_TMA_DESCRIPTOR;
   Args a;
   a.q = p->query;
   a.w = p->weights;
@@ -630,6 +692,7 @@ int launch(const DsaLiParams* p, cudaStream_t stream) {
   a.page = (int)p->page_size;
   a.max_blocks = (int)p->max_blocks;
   a.box_rows = box_rows;
+  a.kscale = kIsFp8<T> ? p->key_scale : nullptr;
   int rc;
   if (N == 256 && G == 64) rc = launch_score<DP, T, 64>(kmap, a, p->batch, p->n2, stream);
   else if (N == 256 && G == 32) rc = launch_score<DP, T, 32>(kmap, a, p->batch, p->n2, stream);
@@ -661,10 +724,12 @@ int launch(const DsaLiParams* p, cudaStream_t stream) {
   const int64_t tsmem_row = ((int64_t)t.s2_row * 4 + 15) / 16 * 16 + (int64_t)kp * 8;
   t.keys_in_gmem = tsmem_row > 200 * 1024 ? 1 : 0;
   const int tsmem = t.keys_in_gmem ? kp * 8 : (int)tsmem_row;
-  if (cudaFuncSetAttribute(li_topk_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, tsmem) !=
+  // values in the query dtype; fp32 for fp8 queries
+  using VT = std::conditional_t<kIsFp8<T>, float, T>;
+  if (cudaFuncSetAttribute(li_topk_kernel<VT>, cudaFuncAttributeMaxDynamicSharedMemorySize, tsmem) !=
       cudaSuccess)
     return DSA_ERR_CUDA;
-  li_topk_kernel<T><<<dim3((unsigned)p->q_rows, (unsigned)p->n2), dim3(kTopkThreads), tsmem, stream>>>(t);
+  li_topk_kernel<VT><<<dim3((unsigned)p->q_rows, (unsigned)p->n2), dim3(kTopkThreads), tsmem, stream>>>(t);
   return cudaGetLastError() == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
 }
 
@@ -688,7 +753,8 @@ extern "C" int dsa_li_score_topk(const DsaLiParams* p, void* stream_) {
        p->max_blocks * p->page_size > (int64_t)1 << 30 || p->kv_rows > (int64_t)1 << 30))
     return DSA_ERR_INVALID_ARG;
   if (p->n1 < 1 || p->n2 < 1 || p->n1 % p->n2 != 0 || p->n1 / p->n2 > 256 || p->d < 16 ||
-      p->d > 256 || p->d % 8 != 0 || p->sparse_count < 1 || p->sparse_count > 4096 ||
+      p->d > 256 || p->d % (p->dtype == DSA_DTYPE_FP8_E4M3 ? 128 : 8) != 0 ||
+      (p->dtype == DSA_DTYPE_FP8_E4M3 && !p->key_scale) || p->sparse_count < 1 || p->sparse_count > 4096 ||
       p->sparse_count > p->s2_row || p->batch < 1 || p->kv_rows < 1)
     return DSA_ERR_INVALID_ARG;
   if (p->workspace_bytes < dsa_li_workspace_size(p->q_rows, p->n2, p->s2_row))
@@ -704,6 +770,10 @@ extern "C" int dsa_li_score_topk(const DsaLiParams* p, void* stream_) {
     if (dp == 64) return launch<64, __half>(p, stream);
     if (dp == 128) return launch<128, __half>(p, stream);
     return launch<256, __half>(p, stream);
+  }
+  if (p->dtype == DSA_DTYPE_FP8_E4M3) {   // 128 fp8 elements per 128-byte chunk
+    if (p->d <= 128) return launch<64, __nv_fp8_e4m3>(p, stream);
+    return launch<128, __nv_fp8_e4m3>(p, stream);
   }
   return DSA_ERR_INVALID_ARG;
 }

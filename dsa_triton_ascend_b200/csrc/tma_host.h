@@ -67,4 +67,20 @@ inline bool make_tmap_3d_16b(CUtensorMap* map, const void* base, bool is_bf16, u
   return r == CUDA_SUCCESS;
 }
 
+// 8-bit elements (fp8): the same 3-D tiled map with 1-byte elements
+inline bool make_tmap_3d_8b(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1,
+                            uint64_t d2, uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1,
+                            uint32_t b2) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (!fn) return false;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {s1, s2};
+  cuuint32_t box[3] = {b0, b1, b2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 }  // namespace dsa

@@ -12,7 +12,7 @@ from __future__ import annotations
 import torch
 
 from . import _host as H
-from ._lib import LiParams, DSA_DTYPE_FP32, check, error_flag, lib, ptr, stream_ptr
+from ._lib import LiParams, DSA_DTYPE_FP32, DSA_DTYPE_FP8_E4M3, check, error_flag, lib, ptr, stream_ptr
 
 INT64_MAX = H.INT64_MAX
 
@@ -196,6 +196,95 @@ def lightning_indexer_paged(
     p.dtype = H.dtype_code(query)
     p.weights_dtype = _weights_code(w)
     p.block_table, p.page_size, p.max_blocks = ptr(bt), page, max_blocks
+    check(lib().dsa_li_score_topk(p, stream_ptr(dev)), "dsa_li_score_topk")
+    return indices, values
+
+
+def lightning_indexer_fp8(
+    query: torch.Tensor,
+    key: torch.Tensor,
+    key_scale: torch.Tensor,
+    weights: torch.Tensor,
+    actual_seq_lengths_query=None,
+    actual_seq_lengths_key=None,
+    block_table=None,
+    sparse_count=2048,
+    sparse_mode=3,
+    return_value=False,
+):
+    """FP8 lightning indexer: e4m3 query and key with a per-key scale.
+
+    No counterpart in the reference (its indexer is bf16 / fp16); DeepSeek-V3.2 runs the
+    indexer in FP8.  score[s2] = key_scale[s2] * sum_g ReLU(q_g . k_s2) * w_g, with any
+    per-query scale folded into ``weights`` by the caller; masks, top-k and tie order are
+    those of ``lightning_indexer_triton``.  ``query`` [B, S1, N1, D] and ``key`` are
+    ``torch.float8_e4m3fn`` (D 128 or 256); ``key`` is [B, S2, N2, D] with
+    ``key_scale`` [B, S2, N2], or, with ``block_table`` [B, max_blocks] int32, a block pool
+    [num_blocks, page_size, N2, D] with ``key_scale`` [num_blocks, page_size, N2] (paging as
+    in ``lightning_indexer_paged``).  ``key_scale`` is fp32 and positive.  Returns (indices
+    int32 [B, S1, N2, sparse_count], values fp32; zeros unless ``return_value``).
+    """
+    if sparse_mode not in (0, 3):
+        raise ValueError("Only sparse_mode 0 (full) / 3 (rightDownCausal) supported")
+    H.require_cuda(query, key, key_scale, weights, block_table)
+    if query.dtype != torch.float8_e4m3fn or key.dtype != torch.float8_e4m3fn:
+        raise ValueError("query and key must be torch.float8_e4m3fn")
+    if key_scale.dtype != torch.float32 or tuple(key_scale.shape) != tuple(key.shape[:3]):
+        raise ValueError("key_scale must be float32 with the key's shape without D")
+    if query.dim() != 4 or key.dim() != 4:
+        raise ValueError("query and key must be 4-D")
+    B, S1, N1, D = query.shape
+    dev = query.device
+    if block_table is None:
+        if key.shape[0] != B:
+            raise ValueError("key batch differs from query batch")
+        S2, N2 = key.shape[1], key.shape[2]
+        kv_rows, page, max_blocks, bt = B * S2, 0, 0, None
+        k_base = H.row_bases(B, S2, dev)
+    else:
+        if block_table.dim() != 2 or block_table.dtype != torch.int32 or block_table.shape[0] != B:
+            raise ValueError("block_table must be an int32 [B, max_blocks] tensor")
+        nblocks, page, N2 = key.shape[0], key.shape[1], key.shape[2]
+        if page < 8 or (page % 128 != 0 and 128 % page != 0):
+            raise ValueError(f"page_size ({page}) must be a multiple of 128 or divide 128 (>= 8)")
+        max_blocks = block_table.shape[1]
+        S2, kv_rows = max_blocks * page, nblocks * page
+        bt = block_table.contiguous()
+        k_base = None
+    if key.shape[3] != D or D not in (128, 256):
+        raise ValueError("query and key must share a head dim of 128 or 256")
+    if N1 % N2 != 0:
+        raise ValueError(f"N1({N1}) must be divisible by N2({N2})")
+    K = int(sparse_count)
+    if K > S2:
+        raise ValueError(f"sparse_count ({K}) exceeds the key length ({S2})")
+    q_base = H.row_bases(B, S1, dev)
+    act_q = H.lens_tensor(actual_seq_lengths_query, B, S1, dev)
+    act_k = H.lens_tensor(actual_seq_lengths_key, B, S2, dev)
+    q, k, ks, w = query.contiguous(), key.contiguous(), key_scale.contiguous(), weights.contiguous()
+    out_shape = (B, S1, N2, K)
+    indices = torch.empty(out_shape, dtype=torch.int32, device=dev)
+    values = (torch.empty(out_shape, dtype=torch.float32, device=dev) if return_value
+              else torch.zeros(out_shape, dtype=torch.float32, device=dev))
+    ws_bytes = lib().dsa_li_workspace_size(B * S1, N2, S2)
+    ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=dev)
+    p = LiParams()
+    p.query, p.key, p.weights = ptr(q), ptr(k), ptr(w)
+    p.act_q, p.act_k, p.q_row_base = ptr(act_q), ptr(act_k), ptr(q_base)
+    p.k_row_base = ptr(k_base) if k_base is not None else 0
+    p.out_indices = ptr(indices)
+    p.out_values = ptr(values) if return_value else 0
+    p.error_flag = ptr(error_flag(dev))
+    p.workspace, p.workspace_bytes = ptr(ws), ws_bytes
+    p.q_rows, p.batch, p.n1, p.n2, p.d, p.kv_rows = B * S1, B, N1, N2, D, kv_rows
+    p.sparse_count, p.s2_row, p.s2_cap = K, S2, S2
+    p.q_len_max, p.q_len_dense = S1, S1
+    p.sparse_mode = int(sparse_mode)
+    p.dtype = DSA_DTYPE_FP8_E4M3
+    p.weights_dtype = _weights_code(w)
+    p.block_table = ptr(bt) if bt is not None else 0
+    p.page_size, p.max_blocks = page, max_blocks
+    p.key_scale = ptr(ks)
     check(lib().dsa_li_score_topk(p, stream_ptr(dev)), "dsa_li_score_topk")
     return indices, values
 

@@ -32,6 +32,7 @@ extern "C" {
 #define DSA_DTYPE_BF16 0
 #define DSA_DTYPE_FP16 1
 #define DSA_DTYPE_FP32 2
+#define DSA_DTYPE_FP8_E4M3 3      /* lightning indexer only (dsa_li_score_topk) */
 
 /* Library version, (major << 16) | minor. */
 int dsa_version(void);
@@ -224,6 +225,10 @@ int64_t dsa_sfa_bwd_workspace_size(int64_t num_rows, int64_t topk, int64_t spars
  * block_table[b * max_blocks + s2 / page_size] * page_size + s2 % page_size (k_row_base is
  * not read).  page_size is a multiple of 128 or divides 128 and is at least 8.  Blocks past
  * a row's visible keys are never read for its scores; a negative id reads zeros.
+ * FP8 indexer (no counterpart in the reference): dtype DSA_DTYPE_FP8_E4M3 takes e4m3 query
+ * and key (d 128 or 256) and key_scale [kv_rows][n2] (positive fp32, laid out
+ * like the key rows, paged or not); score = key_scale * sum_g ReLU(q_g . k) * w_g, and
+ * out_values are fp32.
  */
 typedef struct DsaLiParams {
   const void* query;
@@ -255,6 +260,7 @@ typedef struct DsaLiParams {
   const int32_t* block_table;   /* NULL: dense keys at k_row_base; else [batch][max_blocks] */
   int64_t page_size;
   int64_t max_blocks;
+  const float* key_scale;       /* dtype DSA_DTYPE_FP8_E4M3 only: [kv_rows][n2] fp32 > 0 */
 } DsaLiParams;
 
 int dsa_li_score_topk(const DsaLiParams* params, void* stream);
