@@ -183,9 +183,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="sfa", choices=["sfa", "li", "decode", "sli"],
+    ap.add_argument("--workload", default="sfa", choices=["sfa", "li", "li_fp8", "decode", "sli"],
                     help="sfa: config 4 forward+backward (the headline); li: config 2 indexer; "
-                         "decode: config 3 paged forward; sli: config 5 indexer KL-loss grad")
+                         "li_fp8: config 2 geometry through the FP8 indexer (e4m3 query / key, "
+                         "per-key scales); decode: config 3 paged forward; sli: config 5 "
+                         "indexer KL-loss grad")
     ap.add_argument("--rows", type=int, default=0,
                     help="profiling aid: time only the last ROWS query rows of config 4 "
                          "(each sees the full 2048 keys); 0 = the whole workload")
@@ -431,6 +433,20 @@ def run_other(args, rank, world, local):
         pairs = B * S * (S + 1) // 2
         flops, nbytes = pairs * N1_ * 2 * Dh, q.numel() * 2 + k.numel() * 2 + w.numel() * 4 + 2 * B * S * K * 4
         metric, unit, wl = "LI score+top-k TFLOP/s", "TFLOP/s", "BASELINE config 2 (B=2, S1=S2=4096, N1=64, D=128, top-2048, mode 3)"
+    elif args.workload == "li_fp8":
+        B, S, N1_, Dh, K = 2, 4096, 64, 128, 2048
+        f8 = torch.float8_e4m3fn
+        q = torch.randn(B, S, N1_, Dh, generator=g, device=dev).to(f8)
+        k = torch.randn(B, S, 1, Dh, generator=g, device=dev).to(f8)
+        ks = torch.rand(B, S, 1, generator=g, device=dev) + 0.5
+        w = torch.randn(B, S, N1_, generator=g, device=dev) / _m.sqrt(N1_)
+        fn = lambda: dsa.lightning_indexer_fp8(q, k, ks, w, sparse_count=K, sparse_mode=3,
+                                               return_value=True)
+        pairs = B * S * (S + 1) // 2
+        flops = pairs * N1_ * 2 * Dh
+        nbytes = q.numel() + k.numel() + ks.numel() * 4 + w.numel() * 4 + 2 * B * S * K * 4
+        metric, unit, wl = ("LI FP8 score+top-k TFLOP/s", "TFLOP/s",
+                            "config 2 geometry, FP8 indexer (B=2, S1=S2=4096, N1=64, D=128, top-2048, mode 3)")
     elif args.workload == "decode":
         B, N1_, page, nblk, maxb, K = 32, 128, 128, 16384, 512, 2048
         lens = torch.randint(8192, 65537, (B,), generator=g, device=dev)
@@ -485,14 +501,15 @@ def run_other(args, rank, world, local):
     bound = "hbm" if t_b >= t_f else "tensor"
     line = {"metric": metric, "value": flops / (ms * 1e-3) / 1e12 * world, "unit": unit,
             "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "e4m3" if args.workload == "li_fp8" else "bf16",
             "data": "synthetic", "config": {"workload": wl, "timing": timing},
             "roofline": {"bound": bound, "achieved": (nbytes / (ms * 1e-3) / 1e9) if bound == "hbm"
                          else flops / (ms * 1e-3) / 1e12,
                          "peak": hbm_peak if bound == "hbm" else tf_peak,
                          "unit": "GB/s" if bound == "hbm" else "TFLOP/s",
                          "frac": max(t_b, t_f) / (ms * 1e-3),
-                         "traffic": WORKLOAD_DRAM_BYTES[args.workload],
+                         "traffic": WORKLOAD_DRAM_BYTES.get(args.workload),
                          "peak_source": peak_kind}}
     if rank == 0:
         print(json.dumps(line), flush=True)
