@@ -441,24 +441,22 @@ __device__ __forceinline__ void bitonic_desc(unsigned long long* sel) {
         __syncthreads();
 #pragma unroll
         for (int e = 0; e < E; ++e) {
-          const int p = E * t + e, q = p ^ stride;
-          const unsigned long long y = sel[q];
-          const bool desc = (p & size) == 0;
-          const bool lo = p < q;
-          const unsigned long long mx = v[e] > y ? v[e] : y, mn = v[e] > y ? y : v[e];
-          v[e] = (desc == lo) ? mx : mn;
+          // keep the larger of the pair when this slot is the descending block's low end or
+          // the ascending block's high end: one comparison and one select per element
+          const int p = E * t + e;
+          const unsigned long long y = sel[p ^ stride];
+          const bool keep_max = ((p & size) == 0) == ((p & stride) == 0);
+          v[e] = ((v[e] > y) == keep_max) ? v[e] : y;
         }
         __syncthreads();
       } else {
         const int lx = stride / E;   // partner lane distance
 #pragma unroll
         for (int e = 0; e < E; ++e) {
-          const int p = E * t + e, q = p ^ stride;
+          const int p = E * t + e;
           const unsigned long long y = __shfl_xor_sync(0xffffffffu, v[e], lx);
-          const bool desc = (p & size) == 0;
-          const bool lo = p < q;
-          const unsigned long long mx = v[e] > y ? v[e] : y, mn = v[e] > y ? y : v[e];
-          v[e] = (desc == lo) ? mx : mn;
+          const bool keep_max = ((p & size) == 0) == ((p & stride) == 0);
+          v[e] = ((v[e] > y) == keep_max) ? v[e] : y;
         }
       }
     }
