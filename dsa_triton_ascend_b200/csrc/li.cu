@@ -439,23 +439,21 @@ __device__ __forceinline__ void bitonic_desc(unsigned long long* sel) {
 #pragma unroll
         for (int e = 0; e < E; ++e) sel[E * t + e] = v[e];
         __syncthreads();
+        // keep the larger of the pair when this slot is the descending block's low end or
+        // the ascending block's high end; stride >= E, so that is the same for all E elements
+        const bool keep_max = (((E * t) & size) == 0) == (((E * t) & stride) == 0);
 #pragma unroll
         for (int e = 0; e < E; ++e) {
-          // keep the larger of the pair when this slot is the descending block's low end or
-          // the ascending block's high end: one comparison and one select per element
-          const int p = E * t + e;
-          const unsigned long long y = sel[p ^ stride];
-          const bool keep_max = ((p & size) == 0) == ((p & stride) == 0);
+          const unsigned long long y = sel[(E * t + e) ^ stride];
           v[e] = ((v[e] > y) == keep_max) ? v[e] : y;
         }
         __syncthreads();
       } else {
         const int lx = stride / E;   // partner lane distance
+        const bool keep_max = (((E * t) & size) == 0) == (((E * t) & stride) == 0);
 #pragma unroll
         for (int e = 0; e < E; ++e) {
-          const int p = E * t + e;
           const unsigned long long y = __shfl_xor_sync(0xffffffffu, v[e], lx);
-          const bool keep_max = ((p & size) == 0) == ((p & stride) == 0);
           v[e] = ((v[e] > y) == keep_max) ? v[e] : y;
         }
       }
@@ -468,10 +466,10 @@ __device__ __forceinline__ void bitonic_desc(unsigned long long* sel) {
         for (int e = 0; e < E; ++e) {
           const int f = e ^ st;
           if (f > e) {
-            const int p = E * t + e;
-            const bool desc = (p & size) == 0;
+            // direction of element e's block: from the thread when size >= E, else from e
+            const bool desc = size >= E ? ((E * t) & size) == 0 : (e & size) == 0;
             const unsigned long long x = v[e], y = v[f];
-            const bool swap = desc ? (x < y) : (x > y);
+            const bool swap = (x < y) == desc;   // keys are distinct (the index is part of them)
             v[e] = swap ? y : x;
             v[f] = swap ? x : y;
           }
