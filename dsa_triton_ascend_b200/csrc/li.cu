@@ -562,29 +562,36 @@ __global__ void __launch_bounds__(kTopkThreads, 2) li_topk_kernel(const TopkArgs
         }
       }
       __syncthreads();
+      // s_digit / s_above are rewritten only after the next pass's two barriers, and every
+      // thread has read them by then
       prefix |= (uint32_t)s_digit << shift;
       mask |= 255u << shift;
       remaining -= s_above;
-      __syncthreads();
     }
     const uint32_t thr = prefix;
-    // ordered compaction: all keys > thr, and the first `remaining` keys == thr by index
-    int gt_base = 0, eq_base = 0;
-    for (int base = 0; base < lim; base += kTopkThreads) {
-      const int i = base + threadIdx.x;
-      const uint32_t k = i < lim ? key_at(i) : 0u;
-      const int is_gt = (i < lim && k > thr) ? 1 : 0;
-      const int is_eq = (i < lim && k == thr) ? 1 : 0;
-      // one scan for both counts (each at most kTopkThreads, so 16 bits apiece)
-      int tot;
-      const int pge = block_scan(is_gt | (is_eq << 16), warp_sums, &tot);
-      const int pg = pge & 0xffff, pe = pge >> 16;
-      const int tot_gt = tot & 0xffff, tot_eq = tot >> 16;
+    // ordered compaction: all keys > thr, and the first `remaining` keys == thr by index.
+    // Each thread takes a contiguous range, so one block scan orders both classes; the
+    // counts are packed as gt | eq << 13 (gt < K <= 4096, eq <= lim <= 2^17, so the block total stays below 2^31).
+    const int per = (lim + kTopkThreads - 1) / kTopkThreads;
+    const int i0 = min((int)threadIdx.x * per, lim), i1 = min(i0 + per, lim);
+    int ngt = 0, neq = 0;
+    for (int i = i0; i < i1; ++i) {
+      const uint32_t k = key_at(i);
+      ngt += k > thr;
+      neq += k == thr;
+    }
+    int tot;
+    const int pge = block_scan(ngt | (neq << 13), warp_sums, &tot);
+    int gpos = pge & 0x1fff, epos = pge >> 13;
+    for (int i = i0; i < i1; ++i) {
+      const uint32_t k = key_at(i);
       const unsigned long long comp = ((unsigned long long)k << 32) | (uint32_t)(~(uint32_t)i);
-      if (is_gt) sel[gt_base + pg] = comp;
-      if (is_eq && eq_base + pe < remaining) sel[(K - remaining) + eq_base + pe] = comp;
-      gt_base += tot_gt;
-      eq_base += tot_eq;
+      if (k > thr) {
+        sel[gpos++] = comp;
+      } else if (k == thr) {
+        if (epos < remaining) sel[(K - remaining) + epos] = comp;
+        ++epos;
+      }
     }
     nsel = K;
   }
@@ -751,7 +758,7 @@ extern "C" int dsa_li_score_topk(const DsaLiParams* p, void* stream_) {
   if (p->n1 < 1 || p->n2 < 1 || p->n1 % p->n2 != 0 || p->n1 / p->n2 > 256 || p->d < 16 ||
       p->d > 256 || p->d % (p->dtype == DSA_DTYPE_FP8_E4M3 ? 128 : 8) != 0 ||
       (p->dtype == DSA_DTYPE_FP8_E4M3 && !p->key_scale) || p->sparse_count < 1 || p->sparse_count > 4096 ||
-      p->sparse_count > p->s2_row || p->batch < 1 || p->kv_rows < 1)
+      p->sparse_count > p->s2_row || p->s2_row > (1 << 17) || p->batch < 1 || p->kv_rows < 1)
     return DSA_ERR_INVALID_ARG;
   if (p->workspace_bytes < dsa_li_workspace_size(p->q_rows, p->n2, p->s2_row))
     return DSA_ERR_INVALID_ARG;

@@ -218,7 +218,7 @@ int64_t dsa_sfa_bwd_workspace_size(int64_t num_rows, int64_t topk, int64_t spars
  * Query rows: q_row_base[b] is batch b's first row; a BSND caller passes q_len_dense = S1
  * (rows s1 >= act_q exist but see nothing); a TND caller passes q_len_dense = 0 (a batch has
  * act_q rows).  q_len_max = largest row count of a batch.  s2_row = length of a score row
- * (>= sparse_count).  Workspace: dsa_li_workspace_size() bytes (the fp32 score matrix).
+ * (>= sparse_count, <= 131072).  Workspace: dsa_li_workspace_size() bytes (the fp32 score matrix).
  * Paged keys (no counterpart in the reference, whose indexer rejects block_table at
  * lightning_indexer_triton.py:497-498): with block_table != NULL, key is a block pool
  * [kv_rows = blocks * page_size][n2][d] and key position s2 of batch b is pool row
