@@ -137,7 +137,6 @@ def lightning_indexer_paged(
     """
     if sparse_mode not in (0, 3):
         raise ValueError("Only sparse_mode 0 (full) / 3 (rightDownCausal) supported")
-    H.require_cuda(query, key_cache, weights, block_table)
     if key_cache.dim() != 4:
         raise ValueError("key_cache must be [num_blocks, page_size, N2, D]")
     if block_table.dim() != 2 or block_table.dtype != torch.int32:
@@ -145,6 +144,7 @@ def lightning_indexer_paged(
     nblocks, page, N2, Dk = key_cache.shape
     if page < 8 or (page % 128 != 0 and 128 % page != 0):
         raise ValueError(f"page_size ({page}) must be a multiple of 128 or divide 128 (>= 8)")
+    H.require_cuda(query, key_cache, weights, block_table)
     dev = query.device
     B, max_blocks = block_table.shape
     s2 = max_blocks * page
@@ -226,13 +226,13 @@ def lightning_indexer_fp8(
     """
     if sparse_mode not in (0, 3):
         raise ValueError("Only sparse_mode 0 (full) / 3 (rightDownCausal) supported")
-    H.require_cuda(query, key, key_scale, weights, block_table)
     if query.dtype != torch.float8_e4m3fn or key.dtype != torch.float8_e4m3fn:
         raise ValueError("query and key must be torch.float8_e4m3fn")
     if key_scale.dtype != torch.float32 or tuple(key_scale.shape) != tuple(key.shape[:3]):
         raise ValueError("key_scale must be float32 with the key's shape without D")
     if query.dim() != 4 or key.dim() != 4:
         raise ValueError("query and key must be 4-D")
+    H.require_cuda(query, key, key_scale, weights, block_table)
     B, S1, N1, D = query.shape
     dev = query.device
     if block_table is None:

@@ -121,3 +121,31 @@ def test_dense_lse_guards():
         dsa.dense_lightning_indexer_softmax_lse_triton(t(1, 2, 32, 64), t(1, 64, 1, 64), w)
     with pytest.raises(ValueError, match="CUDA"):
         dsa.dense_lightning_indexer_softmax_lse_triton(qi, ki, w)
+
+
+def test_paged_indexer_guards():
+    """lightning_indexer_paged: no counterpart in the reference; its own argument checks."""
+    q, w = t(1, 2, 8, 128), t(1, 2, 8, dtype=torch.float32)
+    bt = t(1, 4, dtype=torch.int32)
+    with pytest.raises(ValueError, match="key_cache"):
+        dsa.lightning_indexer_paged(q, t(64, 1, 128), w, bt)
+    with pytest.raises(ValueError, match="block_table"):
+        dsa.lightning_indexer_paged(q, t(4, 64, 1, 128), w, t(1, 4, dtype=torch.int64))
+    with pytest.raises(ValueError, match="page_size"):
+        dsa.lightning_indexer_paged(q, t(4, 96, 1, 128), w, bt)
+    with pytest.raises(ValueError, match="sparse_mode"):
+        dsa.lightning_indexer_paged(q, t(4, 64, 1, 128), w, bt, sparse_mode=1)
+    with pytest.raises(ValueError, match="CUDA"):
+        dsa.lightning_indexer_paged(q, t(4, 64, 1, 128), w, bt)
+
+
+def test_fp8_indexer_guards():
+    f8 = torch.float8_e4m3fn
+    q, k = t(1, 2, 8, 128, dtype=f8), t(1, 64, 1, 128, dtype=f8)
+    ks, w = t(1, 64, 1, dtype=torch.float32), t(1, 2, 8, dtype=torch.float32)
+    with pytest.raises(ValueError, match="float8_e4m3fn"):
+        dsa.lightning_indexer_fp8(t(1, 2, 8, 128), k, ks, w)
+    with pytest.raises(ValueError, match="key_scale"):
+        dsa.lightning_indexer_fp8(q, k, t(1, 64, dtype=torch.float32), w)
+    with pytest.raises(ValueError, match="CUDA"):
+        dsa.lightning_indexer_fp8(q, k, ks, w)
