@@ -15,6 +15,12 @@ from . import _host as H
 from ._lib import LiParams, DSA_DTYPE_FP32, DSA_DTYPE_FP8_E4M3, check, error_flag, lib, ptr, stream_ptr
 
 INT64_MAX = H.INT64_MAX
+MAX_SCORE_ROW = 1 << 17   # keys in one score row (the top-k kernel's packed counts)
+
+
+def _check_row_length(s2):
+    if s2 > MAX_SCORE_ROW:
+        raise ValueError(f"key length {s2} exceeds the {MAX_SCORE_ROW} keys a score row may hold")
 
 
 def _weights_code(w: torch.Tensor) -> int:
@@ -79,6 +85,7 @@ def lightning_indexer_triton(
         raise ValueError(f"N1({N1}) must be divisible by N2({N2})")
     if key.shape[-1] != D or key.dtype != query.dtype:
         raise ValueError("query and key must share dtype and head dim")
+    _check_row_length(s2)
     k_eff = min(int(sparse_count), s2)
     if k_eff != int(sparse_count):
         # the reference reshapes min(k, S2) results into sparse_count columns and fails
@@ -144,6 +151,7 @@ def lightning_indexer_paged(
     nblocks, page, N2, Dk = key_cache.shape
     if page < 8 or (page % 128 != 0 and 128 % page != 0):
         raise ValueError(f"page_size ({page}) must be a multiple of 128 or divide 128 (>= 8)")
+    _check_row_length(block_table.shape[1] * page)
     H.require_cuda(query, key_cache, weights, block_table)
     dev = query.device
     B, max_blocks = block_table.shape
@@ -232,6 +240,7 @@ def lightning_indexer_fp8(
         raise ValueError("key_scale must be float32 with the key's shape without D")
     if query.dim() != 4 or key.dim() != 4:
         raise ValueError("query and key must be 4-D")
+    _check_row_length(key.shape[1] if block_table is None else block_table.shape[1] * key.shape[1])
     H.require_cuda(query, key, key_scale, weights, block_table)
     B, S1, N1, D = query.shape
     dev = query.device

@@ -149,3 +149,14 @@ def test_fp8_indexer_guards():
         dsa.lightning_indexer_fp8(q, k, t(1, 64, dtype=torch.float32), w)
     with pytest.raises(ValueError, match="CUDA"):
         dsa.lightning_indexer_fp8(q, k, ks, w)
+
+
+def test_indexer_score_row_cap():
+    """Score rows hold at most 131,072 keys (the top-k kernel packs its counts)."""
+    q, w = t(1, 2, 8, 128), t(1, 2, 8, dtype=torch.float32)
+    with pytest.raises(ValueError, match="score row"):
+        dsa.lightning_indexer_paged(q, t(4, 128, 1, 128), w, t(1, 1025, dtype=torch.int32))
+    f8 = torch.float8_e4m3fn
+    with pytest.raises(ValueError, match="score row"):
+        dsa.lightning_indexer_fp8(t(1, 2, 8, 128, dtype=f8), t(1, 131073, 1, 128, dtype=f8),
+                                  t(1, 131073, 1, dtype=torch.float32), w)
