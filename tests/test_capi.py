@@ -100,3 +100,47 @@ def test_fast_forward_workspace_only_grows_for_split_calls(lib):
     assert fast(8192, 128, 512, 2048, 1) == base(8192, 2048, 1)
     assert fast(16, 128, 512, 256, 1) == base(16, 256, 1)
     assert fast(-1, 128, 512, 2048, 1) == -1 and fast(4, 0, 512, 2048, 1) == -1
+
+
+def test_dense_indexer_and_fp8_li_reject_bad_arguments_without_gpu_work(lib):
+    """The dense indexer loss entry points and the FP8 / paged indexer validate their
+    arguments on the host (the fake pointers below are never touched)."""
+    from dsa_triton_ascend_b200._lib import DenseIndexerParams, LiParams
+    for fn in ("dsa_dense_indexer_softmax_lse", "dsa_dense_indexer_grad_kl_loss"):
+        f = getattr(lib, fn)
+        f.restype = ctypes.c_int
+        f.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+        assert f(None, None) == 1
+    ws = lib.dsa_dense_indexer_workspace_size
+    ws.restype = ctypes.c_int64
+    ws.argtypes = [ctypes.c_int64] * 4
+    assert ws(1, 4, 100, 128) == (4 * 100 * 4 + 255) // 256 * 256 + 100 * 128 * 4
+    assert ws(-1, 4, 100, 128) == -1
+    fake = 1 << 20
+    d = DenseIndexerParams()
+    for name in ("query_index", "key_index", "weights", "act_q", "act_k", "index_max", "index_sum"):
+        setattr(d, name, fake)
+    d.batch, d.s1, d.s2, d.n_index, d.d_index = 1, 4, 64, 256, 128   # n_index > 128
+    f = lib.dsa_dense_indexer_softmax_lse
+    f.argtypes = [ctypes.POINTER(DenseIndexerParams), ctypes.c_void_p]
+    assert f(ctypes.byref(d), None) == 1
+    p = LiParams()
+    for name in ("query", "key", "weights", "act_q", "act_k", "q_row_base", "k_row_base",
+                 "out_indices", "workspace"):
+        setattr(p, name, fake)
+    p.q_rows, p.batch, p.n1, p.n2, p.d, p.kv_rows = 4, 1, 64, 1, 128, 256
+    p.sparse_count, p.s2_row, p.s2_cap, p.q_len_max, p.q_len_dense = 64, 256, 256, 4, 4
+    p.workspace_bytes = 1 << 20
+    p.dtype = 3                       # DSA_DTYPE_FP8_E4M3 without key_scale
+    g = lib.dsa_li_score_topk
+    g.restype = ctypes.c_int
+    g.argtypes = [ctypes.POINTER(LiParams), ctypes.c_void_p]
+    assert g(ctypes.byref(p), None) == 1
+    p.dtype, p.key_scale = 0, 0
+    p.s2_row = p.s2_cap = (1 << 17) + 1   # score rows are capped at 131,072 keys
+    p.workspace_bytes = 1 << 40           # (so that the cap, not the workspace, is what fails)
+    assert g(ctypes.byref(p), None) == 1
+    p.workspace_bytes = 1 << 20
+    p.s2_row = p.s2_cap = 256
+    p.block_table, p.page_size, p.max_blocks = fake, 96, 4   # page neither 128k nor 128/k
+    assert g(ctypes.byref(p), None) == 1
