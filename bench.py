@@ -33,8 +33,12 @@ N1, D, DR, TOPK = 128, 512, 64, 2048
 FWD_FLOP_PER_PAIR = N1 * (2 * (D + DR) + 2 * D)              # QK^T + P V
 BWD_FLOP_PER_PAIR = N1 * (3 * 2 * (D + DR) + 2 * 2 * D)        # S, dQ, dK (576) + dP, dV (512)
 GATHER_BYTES_PER_PAIR = (D + DR) * 2                           # one bf16 key row
-# backward: the key row gathered twice (scores, dQ) + the fp32 dK/dKr/dV scatter
-BWD_BYTES_PER_PAIR = 2 * GATHER_BYTES_PER_PAIR + 4 * (2 * D + DR)
+# backward, roofline bytes by the north-star definition (gathered bytes at HBM): the key row
+# gathered twice, for the scores (K1) and for dQ (K2)
+BWD_BYTES_PER_PAIR = 2 * GATHER_BYTES_PER_PAIR
+# backward: the fp32 dK / dKr / dV scatter-add of every pair, into accumulators that stay in
+# L2 (35.7 MB at config 4); reported beside the roofline, not in it
+BWD_SCATTER_BYTES_PER_PAIR = 4 * (2 * D + DR)
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per valid pair, from one
 # `ncu --set full` capture of the last 256 query rows of config 4 (524,288 pairs; command and
 # figures in profiles/sfa_kernels_config4_rows256_full.md), scaled to a launch by its pairs.
@@ -235,24 +239,28 @@ def main():
             q, k, k, si, scale, actual_seq_lengths_query=aq, query_rope=qr, key_rope=kr,
             sparse_mode=3, return_softmax_lse=True)
 
-    def bwd(out, mx, sm):
-        """Backward of this rank's rows; the fp32 key gradients are summed over ranks."""
+    def bwd(out, mx, sm, ev_r=None):
+        """Backward of this rank's rows; the fp32 key gradients are summed over ranks with
+        one NCCL all-reduce of their contiguous buffer (dk | dkr | dv)."""
         accs, finish = dsa.sparse_flash_attention_grad_partial(
             q, k, k, si, dout, out, mx, sm, scale, query_rope=qr, key_rope=kr,
             actual_seq_lengths_query=aq, sparse_mode=3)
         if world > 1:
-            for t in accs:
-                dist.all_reduce(t)
+            if ev_r is not None:
+                ev_r[0].record(stream)
+            dist.all_reduce(finish.key_grad_buffer)
+            if ev_r is not None:
+                ev_r[1].record(stream)
         return finish()
 
-    def step(ev_f=None, ev_b=None):
+    def step(ev_f=None, ev_b=None, ev_r=None):
         if ev_f is not None:
             ev_f[0].record(stream)
         out, mx, sm = fwd()
         if ev_f is not None:
             ev_f[1].record(stream)
             ev_b[0].record(stream)
-        grads = bwd(out, mx, sm)
+        grads = bwd(out, mx, sm, ev_r)
         if ev_b is not None:
             ev_b[1].record(stream)
         return out, grads
@@ -272,13 +280,14 @@ def main():
     mk = lambda: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
     ev_f = [mk() for _ in range(args.steps)]
     ev_b = [mk() for _ in range(args.steps)]
+    ev_r = [mk() for _ in range(args.steps)]
     barrier()
     torch.cuda.synchronize(dev)
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     start.record(stream)
     for i in range(args.steps):
-        step(ev_f[i], ev_b[i])
+        step(ev_f[i], ev_b[i], ev_r[i])
     end.record(stream)
     torch.cuda.synchronize(dev)
     barrier()
@@ -287,10 +296,21 @@ def main():
     ms_total = start.elapsed_time(end)
     fwd_ms = float(np.mean([a.elapsed_time(b) for a, b in ev_f]))
     bwd_ms = float(np.mean([a.elapsed_time(b) for a, b in ev_b]))
+    ar_ms = float(np.mean([a.elapsed_time(b) for a, b in ev_r])) if world > 1 else 0.0
     t = torch.tensor([ms_total], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_step = float(t.item()) / args.steps
+    # per-rank breakdown (rank 0 reports it): step, forward, backward (including the
+    # all-reduce) and all-reduce times, and the rank's share of the valid pairs
+    mine = torch.tensor([ms_total / args.steps, fwd_ms, bwd_ms, ar_ms, float(my_pairs)],
+                        device=dev, dtype=torch.float64)
+    if world > 1:
+        allr = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(allr, mine)
+        per_rank = [x.tolist() for x in allr]
+    else:
+        per_rank = [mine.tolist()]
 
     flops_total = total_pairs * (FWD_FLOP_PER_PAIR + BWD_FLOP_PER_PAIR)
     value = flops_total / (ms_step * 1e-3) / 1e12
@@ -336,9 +356,10 @@ def main():
 
     hbm_peak, tf_peak, peak_kind = load_peaks()
     # roofline of the dominant call on this rank's share (fwd or bwd, whichever is longer):
-    # time bound = max(algorithmic FLOPs / tensor peak, algorithmic bytes / HBM peak)
+    # time bound = max(algorithmic FLOPs / tensor peak, gathered bytes / HBM peak), the
+    # north-star definition; the backward's time excludes its all-reduce
     if bwd_ms >= fwd_ms:
-        kname, kms = "dsa_sfa_bwd", bwd_ms
+        kname, kms = "dsa_sfa_bwd", bwd_ms - ar_ms
         kflops, kbytes = my_pairs * BWD_FLOP_PER_PAIR, my_pairs * BWD_BYTES_PER_PAIR
         ktraffic = my_pairs * BWD_DRAM_BYTES_PER_PAIR + (r1 - r0) * BWD_DRAM_BYTES_PER_ROW
     else:
@@ -382,6 +403,13 @@ def main():
             "fwd_tflops": total_pairs * FWD_FLOP_PER_PAIR / (fwd_ms * 1e-3) / 1e12 if world == 1 else None,
             "bwd_tflops": total_pairs * BWD_FLOP_PER_PAIR / (bwd_ms * 1e-3) / 1e12 if world == 1 else None,
             "fwd_roofline_frac": fwd_roof_frac,
+            "bwd_scatter": {"bytes_per_pair": BWD_SCATTER_BYTES_PER_PAIR,
+                            "bytes_per_step": my_pairs * BWD_SCATTER_BYTES_PER_PAIR,
+                            "target": "fp32 key-gradient accumulators, L2-resident",
+                            "gbs_over_bwd": my_pairs * BWD_SCATTER_BYTES_PER_PAIR / ((bwd_ms - ar_ms) * 1e-3) / 1e9},
+            "ranks": [{"rank": i, "step_ms": r[0], "fwd_ms": r[1], "bwd_ms": r[2],
+                       "allreduce_ms": r[3], "pairs": int(r[4])} for i, r in enumerate(per_rank)],
+            "step_ms_max_min": [max(r[0] for r in per_rank), min(r[0] for r in per_rank)],
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                     "host_numa_bound": bool(bound)},

@@ -681,39 +681,83 @@ extern "C" int64_t dsa_sfa_fwd_fast_workspace_size(int64_t num_rows, int64_t n1,
 // they run attention (a serving runtime whose KV-cache pool took all free HBM at
 // start-up, or a plain C/C++ host with no allocator of its own that may not call
 // cudaMalloc on its hot path).  The only device memory dsa_sfa_fwd needs besides the
-// caller's inputs and outputs is the compaction workspace; here that workspace is the
-// file-scope array below, so the call allocates nothing.
+// caller's inputs and outputs is its workspace (the compaction, plus the key-split
+// partials of few-row calls); here that workspace is the file-scope array below, so the
+// call allocates nothing.
 //
 // The array lives in every GPU that loads this module, for as long as the process runs.
-// Its name is only a host-side handle: the device address is looked up per device with
-// cudaGetSymbolAddress, once, by the first call on that device (with the device
-// current), and cached.  That first call should therefore come before any stream
-// capture.  All calls on a device share the array and it keeps the last call's
-// contents; no entry has to start at zero, because sfa_prep_kernel writes the count of
-// every query row and the key rows below each count before sfa_fwd_kernel reads them.
+// Its name is only a host-side handle: the device address is looked up with
+// cudaGetSymbolAddress, with the device current, by the first call in each CUDA context
+// (a device's primary context, or a context a driver-API host made itself), and cached
+// under that context's unique id -- an address is valid only in the context it was looked
+// up in, and a context created later (after cudaDeviceReset, say) gets a new id and a new
+// lookup.  That first call should therefore come before any stream capture.  All calls in
+// a context share the array and it keeps the last call's contents.  It holds the
+// compaction workspace and, for calls with few query rows (decode), the fp32 key-split
+// partials when they fit (otherwise such calls run unsplit); no entry has to start at
+// zero, because sfa_prep_kernel writes the count of every query row and the key rows below
+// each count, and every split writes its whole partial, before anything reads them.
 // Calls that overlap on the GPU (different streams, no ordering) race on the array.
 
 static __device__ __align__(256) int32_t g_sfa_fwd_noalloc_scratch[DSA_SFA_FWD_NOALLOC_SCRATCH_BYTES / 4];
 
 namespace {
 
-constexpr int kNoAllocMaxDevices = 64;
-std::mutex g_noalloc_mu;
-void* g_noalloc_addr[kNoAllocMaxDevices] = {};
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
 
-// Device address of this device's scratch array (looked up on first use).
-int noalloc_scratch_address(void** addr) {
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess) return DSA_ERR_CUDA;
-  if (dev < 0 || dev >= kNoAllocMaxDevices) return DSA_ERR_INVALID_ARG;
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_addr[dev]) {
-    void* a = nullptr;
-    if (cudaGetSymbolAddress(&a, g_sfa_fwd_noalloc_scratch) != cudaSuccess || !a)
-      return DSA_ERR_CUDA;
-    g_noalloc_addr[dev] = a;
+struct NoAllocEntry {
+  unsigned long long ctx_id;
+  void* addr;
+};
+constexpr int kNoAllocEntries = 64;
+std::mutex g_noalloc_mu;
+NoAllocEntry g_noalloc[kNoAllocEntries] = {};
+int g_noalloc_next = 0;
+
+// Unique id of the calling thread's current CUDA context (false if there is none or the
+// driver does not provide the entry points).
+bool current_context_id(unsigned long long* id) {
+  static CtxGetCurrentFn get_cur = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_cur = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+    tried = true;
   }
-  *addr = g_noalloc_addr[dev];
+  CUcontext ctx = nullptr;
+  if (!get_cur || !get_id || get_cur(&ctx) != CUDA_SUCCESS || !ctx) return false;
+  return get_id(ctx, id) == CUDA_SUCCESS;
+}
+
+// Device address of the scratch array in the current context (looked up on first use in
+// that context; without a context id it is looked up on every call).
+int noalloc_scratch_address(void** addr) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  unsigned long long id = 0;
+  bool have_id = current_context_id(&id);
+  if (have_id)
+    for (const NoAllocEntry& e : g_noalloc)
+      if (e.addr && e.ctx_id == id) {
+        *addr = e.addr;
+        return DSA_OK;
+      }
+  void* a = nullptr;
+  if (cudaGetSymbolAddress(&a, g_sfa_fwd_noalloc_scratch) != cudaSuccess || !a) return DSA_ERR_CUDA;
+  if (!have_id) have_id = current_context_id(&id);   // the lookup made the primary context current
+  if (have_id) {
+    g_noalloc[g_noalloc_next] = NoAllocEntry{id, a};
+    g_noalloc_next = (g_noalloc_next + 1) % kNoAllocEntries;
+  }
+  *addr = a;
   return DSA_OK;
 }
 

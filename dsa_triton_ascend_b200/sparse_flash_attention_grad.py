@@ -92,10 +92,14 @@ def _sfa_grad(query, key, value, sparse_indices, d_out, out, softmax_max, softma
 
     dq = torch.empty_like(q)
     dqr = torch.empty_like(qr)
+    flat = None
     if accumulators is None:
-        dk_acc = torch.empty((kv_rows, D), dtype=torch.float32, device=dev)
-        dkr_acc = torch.empty((kv_rows, D_ROPE), dtype=torch.float32, device=dev)
-        dv_acc = torch.empty((kv_rows, D), dtype=torch.float32, device=dev)
+        # one contiguous fp32 buffer [dk | dkr | dv], so a multi-GPU caller can sum the key
+        # gradients of all ranks with a single all-reduce
+        flat = torch.empty(kv_rows * (2 * D + D_ROPE), dtype=torch.float32, device=dev)
+        dk_acc = flat[: kv_rows * D].view(kv_rows, D)
+        dkr_acc = flat[kv_rows * D: kv_rows * (D + D_ROPE)].view(kv_rows, D_ROPE)
+        dv_acc = flat[kv_rows * (D + D_ROPE):].view(kv_rows, D)
     else:
         dk_acc, dkr_acc, dv_acc = accumulators
         for t, n in ((dk_acc, D), (dkr_acc, D_ROPE), (dv_acc, D)):
@@ -133,6 +137,9 @@ def _sfa_grad(query, key, value, sparse_indices, d_out, out, softmax_max, softma
             check(lib().dsa_sfa_bwd_cast(p, stream_ptr(dev)), "dsa_sfa_bwd_cast")
             return dq, dk, dv, dqr, dkr
         finish.query_grads = (dq, dqr)   # ready before the cast (they need no reduction)
+        # the three accumulators as one contiguous fp32 tensor (None when the caller passed
+        # its own accumulators)
+        finish.key_grad_buffer = flat
         return (dk_acc, dkr_acc, dv_acc), finish
     return dq, dk, dv, dqr, dkr
 
@@ -175,7 +182,8 @@ def sparse_flash_attention_grad_partial(query, key, value, sparse_indices, d_out
     (query rows processed in several calls); without it they are fresh and zeroed.
     Returns ``((dk_acc, dkr_acc, dv_acc), finish)``: the fp32 key-gradient accumulators,
     which the caller may all-reduce in place, and ``finish()`` which casts them to the key
-    dtype and returns the usual 5-tuple.
+    dtype and returns the usual 5-tuple.  Fresh accumulators are views of one contiguous
+    buffer, ``finish.key_grad_buffer``, so one all-reduce of it sums all three.
     """
     args = dict(query_rope=None, key_rope=None, actual_seq_lengths_query=None,
                 actual_seq_lengths_kv=None, sparse_block_size=1, layout="BSND", sparse_mode=3,

@@ -118,18 +118,25 @@ int64_t dsa_sfa_fwd_fast_workspace_size(int64_t num_rows, int64_t n1, int64_t d,
  * pool) and may not call cudaMalloc on its hot path.
  *
  * Same parameters and results as dsa_sfa_fwd, except that `workspace` and
- * `workspace_bytes` are ignored: the compaction workspace is a fixed array of
+ * `workspace_bytes` are ignored: the workspace is a fixed array of
  * DSA_SFA_FWD_NOALLOC_SCRATCH_BYTES inside the library, which every GPU that loads
- * the library's forward module holds until the process exits.
+ * the library's forward module holds until the process exits.  It holds the
+ * compaction of the index rows and, for calls with few query rows (decode), the fp32
+ * partial results of the key splits, up to DSA_SFA_FWD_NOALLOC_SCRATCH_BYTES in all; a
+ * few-row call whose partials do not fit beside the compaction runs unsplit instead.
  *   - Calls whose dsa_sfa_fwd_workspace_size(num_rows, topk, sparse_block_size)
  *     exceeds DSA_SFA_FWD_NOALLOC_SCRATCH_BYTES return DSA_ERR_TOO_LARGE and launch
  *     nothing (split the query rows into several calls, or use dsa_sfa_fwd).
- *   - The first call on a device looks up that device's copy of the array (with the
- *     device current); make that first call before any stream capture begins.
- *   - Every call on a device shares the one array and it keeps the last call's
+ *   - The first call in a CUDA context looks up that context's copy of the array (with
+ *     the device current) and caches its address under the context's unique id; the
+ *     address is valid only in that context, so a new context (after cudaDeviceReset,
+ *     or one a driver-API host creates) gets its own lookup.  Make that first call
+ *     before any stream capture begins.
+ *   - Every call in a context shares the one array and it keeps the last call's
  *     contents.  Nothing in it has to start at zero (each call writes every entry it
  *     later reads), but calls that overlap on the GPU -- on different streams without
- *     ordering between them -- race on it and give wrong results.
+ *     ordering between them -- race on it (compaction and partials alike) and give
+ *     wrong results.
  * Calls no cudaMalloc, cudaFree or other allocating routine.
  */
 #define DSA_SFA_FWD_NOALLOC_SCRATCH_BYTES (16LL << 20)

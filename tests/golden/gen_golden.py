@@ -46,6 +46,7 @@ SFA_BWD_CASES = [
     ("bwd_multibatch_d512_bf16", 2, 8, 128, 16, 512, 64, 1, 3, "bf16", 13),
     ("bwd_blk2_d128_bf16", 1, 8, 128, 8, 128, 16, 2, 3, "bf16", 14),
     ("bwd_n1_64_d512_bf16", 1, 2, 128, 64, 512, 64, 1, 3, "bf16", 15),
+    ("bwd_blk4_d256_bf16", 1, 8, 256, 16, 256, 24, 4, 3, "bf16", 16),
 ]
 
 # (name, B, S1, S2, N1, D, Nidx1, Di, topK, pattern, seed)
@@ -54,6 +55,15 @@ SLI_CASES = [
     ("sli_continuous", 1, 4, 256, 16, 512, 8, 128, 64, "continuous", 22),
     ("sli_repeated", 1, 4, 256, 16, 512, 8, 128, 64, "repeated", 23),
     ("sli_n1_32_k128", 1, 3, 512, 32, 512, 16, 128, 128, "causal_random", 24),
+]
+
+# Lightning-indexer score pins: the SLI golden's stage-1 scores I_scores
+# (sli_grad_kl_loss_numpy.py:64-76) with index rows that list every visible key
+# ("causal_continuous", topK = S2), i.e. the indexer's score of every visible key.
+# (name, B, S1, S2, N1, D, Nidx1, Di, seed); the SLI inputs are generated in fp16.
+LI_SCORE_CASES = [
+    ("li_scores_n8_d128", 1, 4, 128, 16, 512, 8, 128, 31),
+    ("li_scores_n64_d128", 1, 3, 96, 16, 512, 64, 128, 32),
 ]
 
 CONFIG1_ROWS = list(range(0, 128, 8))
@@ -74,7 +84,10 @@ def np_dtype(golden_mod, dtype):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="reference project checkout")
+    ap.add_argument("--only", nargs="*", default=None,
+                    help="write only the fixtures with these names (default: all)")
     args = ap.parse_args()
+    want = (lambda n: True) if not args.only else (lambda n: n in args.only)
     sys.path.insert(0, os.path.abspath(args.reference))
     stub = types.ModuleType("mindspore")
     stub.GRAPH_MODE, stub.PYNATIVE_MODE = 0, 1
@@ -86,6 +99,8 @@ def main():
     import sli_grad_kl_loss_numpy as sli_g
 
     for name, B, S1, S2, N1, D, cnt, blk, mode, dt, seed in SFA_FWD_CASES:
+        if not want(name):
+            continue
         c = I.sfa_case(B, S1, S2, N1, D, cnt, blk, mode, dt, seed)
         out, mx, sm = fwd_g.sparse_flash_attention_golden_bsnd(
             c["q"], c["k"], c["k"], c["si"], c["qr"], c["kr"], c["scale"],
@@ -95,17 +110,20 @@ def main():
                             softmax_max=mx, softmax_sum=sm)
         print("wrote", name)
 
-    c = I.config1()
-    out, mx, sm = fwd_g.sparse_flash_attention_golden_bsnd(
-        c["q"], c["k"], c["k"], c["si"], c["qr"], c["kr"], c["scale"], [128], [2048],
-        sparse_block_size=1, sparse_mode=3, return_softmax_lse=True, dtype=fwd_g.BF16)
-    np.savez_compressed(os.path.join(HERE, "config1.npz"),
-                        rows=np.array(CONFIG1_ROWS, np.int32),
-                        out_rows=bits16(out[:, CONFIG1_ROWS], "bf16"),
-                        softmax_max=mx, softmax_sum=sm)
-    print("wrote config1")
+    if want("config1"):
+        c = I.config1()
+        out, mx, sm = fwd_g.sparse_flash_attention_golden_bsnd(
+            c["q"], c["k"], c["k"], c["si"], c["qr"], c["kr"], c["scale"], [128], [2048],
+            sparse_block_size=1, sparse_mode=3, return_softmax_lse=True, dtype=fwd_g.BF16)
+        np.savez_compressed(os.path.join(HERE, "config1.npz"),
+                            rows=np.array(CONFIG1_ROWS, np.int32),
+                            out_rows=bits16(out[:, CONFIG1_ROWS], "bf16"),
+                            softmax_max=mx, softmax_sum=sm)
+        print("wrote config1")
 
     for name, B, S1, S2, N1, D, cnt, blk, mode, dt, seed in SFA_BWD_CASES:
+        if not want(name):
+            continue
         c = I.sfa_case(B, S1, S2, N1, D, cnt, blk, mode, dt, seed)
         out, mx, sm = fwd_g.sparse_flash_attention_golden_bsnd(
             c["q"], c["k"], c["k"], c["si"], c["qr"], c["kr"], c["scale"],
@@ -122,6 +140,8 @@ def main():
         print("wrote", name)
 
     for name, B, S1, S2, N1, D, Nidx1, Di, topK, pat, seed in SLI_CASES:
+        if not want(name):
+            continue
         c = I.sli_case(B, S1, S2, N1, D, Nidx1, Di, topK, pat, "fp16", seed)
         mx, sm = sli_g._compute_sm_stats(c["q"], c["k"], c["qr"], c["kr"], c["scale"])
         r = sli_g.numpy_reference(c["q"], c["k"], c["qr"], c["kr"], c["qi"], c["ki"],
@@ -129,6 +149,16 @@ def main():
         np.savez_compressed(os.path.join(HERE, name + ".npz"), softmax_max=mx, softmax_sum=sm,
                             dQueryIndex=r["dQueryIndex"], dKeyIndex=r["dKeyIndex"],
                             dW=r["dW"], loss=r["loss"])
+        print("wrote", name)
+
+    for name, B, S1, S2, N1, D, Nidx1, Di, seed in LI_SCORE_CASES:
+        if not want(name):
+            continue
+        c = I.sli_case(B, S1, S2, N1, D, Nidx1, Di, S2, "causal_continuous", "fp16", seed)
+        mx, sm = sli_g._compute_sm_stats(c["q"], c["k"], c["qr"], c["kr"], c["scale"])
+        r = sli_g.numpy_reference(c["q"], c["k"], c["qr"], c["kr"], c["qi"], c["ki"],
+                                  c["w"], c["si"], mx, sm, c["scale"])
+        np.savez_compressed(os.path.join(HERE, name + ".npz"), I_scores=r["I_scores"])
         print("wrote", name)
 
 

@@ -118,3 +118,31 @@ def test_li_tnd_layout():
         scp[..., :lk[b]] = sc
         check_topk(idx[off:off + lq[b]].cpu().numpy(), host(val[off:off + lq[b]]), scp, 128,
                    what=f"tnd b{b}")
+
+
+def test_li_scores_match_reference_golden_stage1():
+    """Indexer scores of every visible key against the reference's own golden numbers.
+
+    The fixtures hold the SLI golden's stage-1 scores I = sum_g w_g ReLU(qi_g . ki)
+    (sli_grad_kl_loss_numpy.py:64-76) for index rows listing every visible key, i.e. the
+    indexer's score row.  The golden rounds each dot product to fp16 and the kernel keeps
+    it in fp32, and the returned values are in the query dtype (fp16 here), so the bound is
+    a few fp16 ulps of the largest term.
+    """
+    from golden_io import load
+    from gen_golden import LI_SCORE_CASES
+    for name, B, S1, S2, N1, D, Nidx1, Di, seed in LI_SCORE_CASES:
+        c = I.sli_case(B, S1, S2, N1, D, Nidx1, Di, S2, "causal_continuous", "fp16", seed)
+        g = load(name)["I_scores"]
+        c2 = dict(q=c["qi"], k=c["ki"], w=c["w"])
+        idx, val, _ = _run(c2, S2, 3, dt="fp16")
+        for s1 in range(S1):
+            vis = S2 - S1 + s1 + 1
+            got = np.full(S2, np.nan, np.float32)
+            ids = idx[0, s1, 0, :vis]
+            assert np.all(ids >= 0) and np.all(idx[0, s1, 0, vis:] == -1), f"{name} row {s1}"
+            got[ids] = val[0, s1, 0, :vis]
+            ref = g[0, s1, :vis]
+            bound = 4e-3 * np.abs(ref) + 2e-3 * np.abs(ref).max()
+            assert np.all(np.abs(got[:vis] - ref) <= bound), (
+                f"{name} row {s1}: max err {np.nanmax(np.abs(got[:vis] - ref)):.3g}")

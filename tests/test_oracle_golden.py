@@ -7,7 +7,7 @@ import numpy as np
 import pytest
 
 import inputs as I
-from gen_golden import SFA_FWD_CASES, SFA_BWD_CASES, SLI_CASES, CONFIG1_ROWS
+from gen_golden import SFA_FWD_CASES, SFA_BWD_CASES, SLI_CASES, CONFIG1_ROWS, LI_SCORE_CASES
 from golden_io import load, from_bits16
 from oracle import sfa, sli, li
 
@@ -110,3 +110,28 @@ def test_li_topk_ragged_and_short():
     np.testing.assert_array_equal(idx[0], [0, 2, 3, -1, -1])
     idx2, _ = li.li_topk(sc, 2)
     np.testing.assert_array_equal(idx2[0], [0, 2])
+
+
+@pytest.mark.parametrize("case", LI_SCORE_CASES, ids=[c[0] for c in LI_SCORE_CASES])
+def test_li_score_oracle_matches_sli_golden_stage1(case):
+    """The indexer's score arithmetic, pinned to the reference's own golden.
+
+    The SLI golden's stage 1 (sli_grad_kl_loss_numpy.py:64-76) computes
+    I = sum_g w_g ReLU(qi_g . ki) for the keys listed in each index row.  With rows that
+    list every visible key in order (causal_continuous, topK = S2) that is the indexer's
+    score of every visible key under sparse_mode 3 (lightning_indexer_triton.py:202-280).
+    The golden rounds its inputs and every dot product to fp16; so does the oracle here.
+    """
+    name, B, S1, S2, N1, D, Nidx1, Di, seed = case
+    c = I.sli_case(B, S1, S2, N1, D, Nidx1, Di, S2, "causal_continuous", "fp16", seed)
+    g = load(name)["I_scores"]                                   # [B, S1, topK = S2]
+    sc = li.li_score(c["qi"], c["ki"], c["w"], sparse_mode=3, emulate_fp16=True)
+    for s1 in range(S1):
+        vis = S2 - S1 + s1 + 1
+        assert np.all(np.isneginf(sc[0, s1, 0, vis:]))
+        # fp32 summation order differs (one fp16 ulp of a dot product at most)
+        _close(sc[0, s1, 0, :vis], g[0, s1, :vis], rtol=1e-4, atol=2e-3)
+    # the same scores without fp16 emulation stay within the fp16 rounding band
+    sc32 = li.li_score(c["qi"], c["ki"], c["w"], sparse_mode=3)
+    vis = S2 - S1 + 1
+    _close(sc32[0, 0, 0, :vis], g[0, 0, :vis], rtol=2e-2, atol=2e-2)

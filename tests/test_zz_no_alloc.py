@@ -42,7 +42,8 @@ def _case_params(c, B, S1, S2, N1, D, topk, mode, noalloc_ws=False):
     if noalloc_ws:
         p.workspace, p.workspace_bytes = 0, 0          # ignored by the no-alloc entry point
     else:
-        ws_bytes = _lib.lib().dsa_sfa_fwd_workspace_size(num_rows, topk, 1)
+        # the workspace with room for key-split partials, so few-row calls split here too
+        ws_bytes = _lib.lib().dsa_sfa_fwd_fast_workspace_size(num_rows, N1, D, topk, 1)
         t["ws"] = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
         p.workspace, p.workspace_bytes = _lib.ptr(t["ws"]), ws_bytes
     p.num_rows, p.batch, p.n1, p.d, p.topk = num_rows, B, N1, D, topk
@@ -54,12 +55,16 @@ def _case_params(c, B, S1, S2, N1, D, topk, mode, noalloc_ws=False):
     return p, t
 
 
-# (B, S1, S2, N1, D, topk, sparse_mode, seed): the second case has fewer query rows and a
-# smaller top-k than the first, so it runs over the first call's leftover scratch contents
-CASES = [(2, 48, 640, 16, 512, 512, 3, 11), (1, 20, 300, 64, 512, 96, 0, 12)]
+# (B, S1, S2, N1, D, topk, sparse_mode, seed): each case has fewer query rows than the one
+# before it, so it runs over the previous call's leftover scratch contents.  The last one is
+# decode-shaped (2 query rows of 2048 keys): both entry points split its keys over several
+# CTA pairs and put the fp32 partials in their workspace (the fixed array for the no-alloc
+# entry point).
+CASES = [(2, 48, 640, 16, 512, 512, 3, 11), (1, 20, 300, 64, 512, 96, 0, 12),
+         (1, 2, 4096, 128, 512, 2048, 0, 14)]
 
 
-def test_noalloc_matches_workspace_entry_point_twice_in_a_row():
+def test_noalloc_matches_workspace_entry_point_calls_in_a_row():
     from dsa_triton_ascend_b200 import _lib, check_device_errors
     L = _lib.lib()
     stream = torch.cuda.current_stream().cuda_stream
@@ -69,7 +74,12 @@ def test_noalloc_matches_workspace_entry_point_twice_in_a_row():
         cases.append(c)
         noalloc.append(_case_params(c, B, S1, S2, N1, D, K, mode, noalloc_ws=True))
         ref.append(_case_params(c, B, S1, S2, N1, D, K, mode))
-    # two no-alloc calls back to back on one stream, then the workspace entry point
+    # decode-shaped case: its partials fit in the fixed array beside the compaction, so the
+    # no-alloc call takes the same split path as the reference call
+    nr, n1, d, k = 2, 128, 512, 2048
+    assert L.dsa_sfa_fwd_fast_workspace_size(nr, n1, d, k, 1) > L.dsa_sfa_fwd_workspace_size(nr, k, 1)
+    assert L.dsa_sfa_fwd_fast_workspace_size(nr, n1, d, k, 1) <= _lib.SFA_FWD_NOALLOC_SCRATCH_BYTES
+    # no-alloc calls back to back on one stream, then the workspace entry point
     for p, _ in noalloc:
         assert L.dsa_sfa_fwd_noalloc(ctypes.byref(p), ctypes.c_void_p(stream)) == _lib.DSA_OK
     for p, _ in ref:
