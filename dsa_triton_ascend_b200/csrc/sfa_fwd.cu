@@ -134,11 +134,6 @@ struct __align__(16) Bars {
   float red_sum[4][32];
 };
 
-__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint4 v) {
-  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x),
-               "r"(v.y), "r"(v.z), "r"(v.w)
-               : "memory");
-}
 
 template <int D, typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
@@ -221,8 +216,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint32_t ph = (uint32_t)(t >> 1) & 1u;
       // QK^T(t) done (so X(t) landed in both CTAs) and PV(t-2) done (H slot b free in
       // both CTAs: one pair MMA)
-      mbar_wait(smem_u32(&bars.s_full[b]), ph, a.err, &failed);
-      mbar_wait(smem_u32(&bars.pv_done[b]), ph ^ 1u, a.err, &failed);
+      mbar_wait_spin(smem_u32(&bars.s_full[b]), ph, a.err, &failed);
+      mbar_wait_spin(smem_u32(&bars.pv_done[b]), ph ^ 1u, a.err, &failed);
       if (!failed) {
         const uint32_t xs = C::kOffX + b * C::kXBytes;
         const uint32_t hs = C::kOffH + b * C::kHBytes + cta * C::kHHalf;   // my tokens' half
@@ -265,7 +260,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int r4[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) r4[e] = __shfl_sync(0xffffffffu, my_row, 4 * (lane & 7) + e);
-      mbar_wait(smem_u32(&bars.x_empty[b]), ((uint32_t)(t >> 1) & 1u) ^ 1u, a.err, &failed);
+      mbar_wait_spin(smem_u32(&bars.x_empty[b]), ((uint32_t)(t >> 1) & 1u) ^ 1u, a.err, &failed);
       if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
       const uint32_t full = smem_u32(&bars.x_full[b]);
       if (cta == 0 && wq == 0 && lane == 0) mbar_arrive_expect_tx(full, 2 * C::kXBytes);
@@ -280,53 +275,59 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       __syncwarp();
     }
   } else if (warp == 1) {
-    // ======================= MMA issuer (pair leader) =======================
-    if (cta == 0 && ntiles > 0 && lane == 0) {
+    // ================ MMA issuer (pair leader): the whole warp runs the loop =================
+    // (waits included) and one elected lane issues each tcgen05 instruction; a single lane
+    // running the loop alone issues the MMAs much more slowly (5.9 against 7.8 ms at config 4)
+    if (cta == 0 && ntiles > 0) {
       const bool bf16 = ElemTraits<T>::kIsBf16;
       const uint32_t id_qk = idesc_f16(128, kTile, bf16, false, false);
       const uint32_t id_pv = idesc_f16(128, C::kNPV, bf16, false, true);
-      mbar_wait(smem_u32(&bars.q_full), 0, a.err, &failed);
-      // Descriptors are built once; each MMA only adds a compile-time byte offset
-      // (>> 4) to the start-address field, which cannot carry: shared addresses < 2^18.
+      mbar_wait_spin(smem_u32(&bars.q_full), 0, a.err, &failed);
       const uint64_t dq = smem_desc_sw128(sQ, 16, 1024);
       const uint64_t dx0 = smem_desc_sw128(sX, 16, 1024);
       const uint64_t dp0 = smem_desc_sw128(sP, 16, 1024);
       const uint64_t dh0 = smem_desc_sw128(sH, kChunkBytesH, 1024);
       auto issue_qk = [&](int t) {
         const int b = t & 1;
-        if (!mbar_wait(smem_u32(&bars.x_full[b]), (uint32_t)(t >> 1) & 1u, a.err, &failed, true))
-          return;
+        mbar_wait_spin(smem_u32(&bars.x_full[b]), (uint32_t)(t >> 1) & 1u, a.err, &failed, true);
+        if (__any_sync(0xffffffffu, failed)) { failed = true; return; }
         tc_fence_after();
         const uint32_t d = tmem + 32 * b;
         const uint64_t bx = dx0 + (uint64_t)((b * C::kXBytes) >> 4);
+        if (elect_one()) {
 #pragma unroll
-        for (int c = 0; c < C::kChunks; ++c)
+          for (int c = 0; c < C::kChunks; ++c)
 #pragma unroll
-          for (int u = 0; u < 4; ++u)
-            umma_f16<2>(d, dq + (uint64_t)((c * kHeads * 128 + u * 32) >> 4),
-                        bx + (uint64_t)((c * kChunkBytesX + u * 32) >> 4), id_qk, (c | u) != 0);
-        umma_commit_pair(smem_u32(&bars.s_full[b]), 3);
+            for (int u = 0; u < 4; ++u)
+              umma_f16<2>(d, dq + (uint64_t)((c * kHeads * 128 + u * 32) >> 4),
+                          bx + (uint64_t)((c * kChunkBytesX + u * 32) >> 4), id_qk, (c | u) != 0);
+          umma_commit_pair(smem_u32(&bars.s_full[b]), 3);
+        }
+        __syncwarp();
       };
       if (!failed) issue_qk(0);
       for (int t = 0; t < ntiles && !failed; ++t) {
         if (t + 1 < ntiles) issue_qk(t + 1);
         const int b = t & 1;
         const uint32_t par = (uint32_t)(t >> 1) & 1u;
-        mbar_wait(smem_u32(&bars.p_full[b]), par, a.err, &failed, true);
-        mbar_wait(smem_u32(&bars.h_full[b]), par, a.err, &failed, true);
-        if (failed) break;
+        mbar_wait_spin(smem_u32(&bars.p_full[b]), par, a.err, &failed, true);
+        mbar_wait_spin(smem_u32(&bars.h_full[b]), par, a.err, &failed, true);
+        if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
         tc_fence_after();
         const uint64_t dp = dp0 + (uint64_t)((b * C::kPBytes) >> 4);
         const uint64_t dh = dh0 + (uint64_t)((b * C::kHBytes) >> 4);
+        if (elect_one()) {
 #pragma unroll
-        for (int j = 0; j < C::kNumPV; ++j)
+          for (int j = 0; j < C::kNumPV; ++j)
 #pragma unroll
-          for (int k = 0; k < kTile / 16; ++k)
-            umma_f16<2>(tmem + C::kTmemO + j * (C::kNPV / 2), dp + (uint64_t)((k * 32) >> 4),
-                        dh + (uint64_t)(((k >> 1) * C::kHHalf + j * C::kCpj * kChunkBytesH +
-                                         (k & 1) * 2048) >> 4),
-                        id_pv, (t | k) != 0);
-        umma_commit_pair(smem_u32(&bars.pv_done[b]), 3);
+            for (int k = 0; k < kTile / 16; ++k)
+              umma_f16<2>(tmem + C::kTmemO + j * (C::kNPV / 2), dp + (uint64_t)((k * 32) >> 4),
+                          dh + (uint64_t)(((k >> 1) * C::kHHalf + j * C::kCpj * kChunkBytesH +
+                                           (k & 1) * 2048) >> 4),
+                          id_pv, (t | k) != 0);
+          umma_commit_pair(smem_u32(&bars.pv_done[b]), 3);
+        }
+        __syncwarp();
       }
     }
     __syncwarp();
@@ -345,7 +346,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int s = t & 1;
       const uint32_t par = (t >> 1) & 1;
       const int nv = min(kTile, nvalid - kTile * t) - kOwn * half;   // valid keys in my half
-      mbar_wait(smem_u32(&bars.s_full[s]), par, a.err, &failed);
+      mbar_wait_spin(smem_u32(&bars.s_full[s]), par, a.err, &failed);
       bool wfail = __any_sync(0xffffffffu, failed);                  // warp-uniform
       tc_fence_after();
       uint32_t r[32];
@@ -387,10 +388,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         pk[i] = ElemTraits<T>::pack2(p0, p1);
       }
       // P buffer s was last read by PV(t-2); O may be touched only once PV(t-1) is done.
-      if (t >= 2) mbar_wait(smem_u32(&bars.pv_done[s]), par ^ 1u, a.err, &failed);
+      if (t >= 2) mbar_wait_spin(smem_u32(&bars.pv_done[s]), par ^ 1u, a.err, &failed);
       if (__any_sync(0xffffffffu, rescale)) {
         if (t >= 1)
-          mbar_wait(smem_u32(&bars.pv_done[s ^ 1]), (uint32_t)((t - 1) >> 1) & 1u, a.err, &failed);
+          mbar_wait_spin(smem_u32(&bars.pv_done[s ^ 1]), (uint32_t)((t - 1) >> 1) & 1u, a.err, &failed);
         if (!__any_sync(0xffffffffu, failed)) {
           tc_fence_after();
           for (int cc = 0; cc < D / 2; cc += 16) {
@@ -424,7 +425,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     bars.red_sum[q][lane] = l_part;
     if (ntiles > 0) {
       const int tl = ntiles - 1;
-      mbar_wait(smem_u32(&bars.pv_done[tl & 1]), (uint32_t)(tl >> 1) & 1u, a.err, &failed);
+      mbar_wait_spin(smem_u32(&bars.pv_done[tl & 1]), (uint32_t)(tl >> 1) & 1u, a.err, &failed);
     }
     const bool read_o = ntiles > 0 && !__any_sync(0xffffffffu, failed);
     named_bar_sync(1, 128);

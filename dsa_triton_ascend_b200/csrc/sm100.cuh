@@ -105,7 +105,9 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
 }
 
 // Bounded wait.  Returns false (and records kErrTimeout) when the limit is hit.
-// `*failed` short-circuits later waits of the same thread once one has failed.
+// `*failed` short-circuits later waits of the same thread once one has failed.  (Reading
+// the global timer is slow; a thread that polls many barriers in parallel with others thus
+// backs off between polls, which keeps issue slots for the warps doing the work.)
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, bool* failed,
                                           bool cluster_scope = false) {
   if (*failed) return false;
@@ -123,6 +125,37 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
   }
 }
 
+// Slow path of mbar_wait_spin: poll against the wall-clock limit; false (error recorded)
+// on timeout.  It takes no pointer to the caller's `failed` flag, so that flag stays in a
+// register.
+static __device__ __noinline__ bool mbar_wait_timed(uint32_t bar, uint32_t parity, int* err,
+                                                    bool cluster_scope) {
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    for (int i = 0; i < 64; ++i)
+      if (cluster_scope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity))
+        return true;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      report_error(err, kErrTimeout);
+      return false;
+    }
+  }
+}
+
+// Bounded wait for a latency-critical thread (an MMA issuer waiting for operands that are
+// about to land): the first polls do not read the slow global timer, so the issuer reacts
+// as soon as the phase completes and the tensor pipe does not starve.
+__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, int* err,
+                                               bool* failed, bool cluster_scope = false) {
+  if (*failed) return false;
+#pragma unroll 1
+  for (int i = 0; i < 32; ++i)
+    if (cluster_scope ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
+  if (mbar_wait_timed(bar, parity, err, cluster_scope)) return true;
+  *failed = true;
+  return false;
+}
+
 // Bounded wait with a sleep between polls, for a role thread that waits long (a producer
 // for a free slot, an MMA issuer for a drained buffer): polling at full rate would take
 // issue slots from the warps that do the work on the same scheduler.
@@ -130,14 +163,20 @@ __device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity, i
                                                 bool* failed, uint32_t sleep_ns = 128) {
   if (*failed) return false;
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
-  while (true) {
+  uint64_t t0 = 0;
+#pragma unroll 1
+  for (uint32_t i = 0;; ++i) {
     __nanosleep(sleep_ns);
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer() - t0 > kWaitLimitNs) {
-      report_error(err, kErrTimeout);
-      *failed = true;
-      return false;
+    if ((i & 15u) == 15u) {   // the global timer is slow to read: check it now and then
+      const uint64_t now = globaltimer();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > kWaitLimitNs) {
+        report_error(err, kErrTimeout);
+        *failed = true;
+        return false;
+      }
     }
   }
 }
@@ -178,6 +217,30 @@ __device__ __forceinline__ void cluster_sync() {
 
 __device__ __forceinline__ void st_cluster_f32(uint32_t cluster_addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_cluster_s32(uint32_t cluster_addr, int v) {
+  asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_cluster_v4(uint32_t cluster_addr, uint4 v) {
+  asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "r"(v.x),
+               "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// Named barrier over `n` threads that also ORs a predicate across them (bar.red.or).  The
+// aligned form: converge the warp first.
+__device__ __forceinline__ bool named_bar_or(int id, int n, bool v) {
+  __syncwarp();
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, %2, %3, p;\n"
+      " selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
 }
 
 // ---------------------------------------------------------------------------
@@ -342,6 +405,17 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint6
         : "memory");
 }
 
+// A operand from tensor memory (`a_tmem`: M rows = TMEM lanes, K elements packed two per
+// 32-bit column, K-major), B from shared memory; single-CTA form.
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive once on an own-CTA barrier when all prior tcgen05 ops of this thread finish.
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
@@ -352,6 +426,16 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
 __device__ __forceinline__ void umma_commit_pair(uint32_t bar, uint16_t mask) {
   asm volatile(
       "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(bar),
+      "h"(mask)
+      : "memory");
+}
+
+// Single-CTA MMAs, completion signalled on the barrier at the same offset in every CTA of
+// `mask` (e.g. the issuing CTA and a consumer CTA of the cluster).
+__device__ __forceinline__ void umma_commit_mc(uint32_t bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
       " [%0], %1;" ::"r"(bar),
       "h"(mask)
       : "memory");
