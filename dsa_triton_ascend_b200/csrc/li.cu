@@ -247,28 +247,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
-    if (lane == 0) {
+    // The whole warp runs the loop (waits included); one elected lane issues each tcgen05
+    // instruction (a lone lane issues MMAs much more slowly).
+    {
       const bool bf16 = ElemTraits<T>::kIsBf16;
       const uint32_t id = idesc_f16(128, N, bf16, false, false);
       const uint64_t dq = smem_desc_sw128(sQ, 16, 1024);
       for (int t = 0; t < ntiles && !failed; ++t) {
         const int s = t % C::kStages, buf = t & 1;
-        if (t >= 2) mbar_wait(smem_u32(&bars.tfree[buf]), ((t >> 1) - 1) & 1, a.err, &failed);
-        mbar_wait(smem_u32(&bars.full[s]), (t / C::kStages) & 1, a.err, &failed);
-        if (failed) break;
+        if (t >= 2) mbar_wait_spin(smem_u32(&bars.tfree[buf]), ((t >> 1) - 1) & 1, a.err, &failed);
+        mbar_wait_spin(smem_u32(&bars.full[s]), (t / C::kStages) & 1, a.err, &failed);
+        if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
         tc_fence_after();
         const uint64_t dk = smem_desc_sw128(sK + s * C::kStageBytes, 16, 1024);
+        if (elect_one()) {
 #pragma unroll
-        for (int c = 0; c < C::kChunks; ++c)
+          for (int c = 0; c < C::kChunks; ++c)
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {   // 32 bytes of K per MMA (16 bf16 / fp16, 32 fp8)
-            const uint64_t ka = dk + (uint64_t)((c * kKeys * 128 + u * 32) >> 4);
-            const uint64_t qb = dq + (uint64_t)((c * N * 128 + u * 32) >> 4);
-            if constexpr (kIsFp8<T>) umma_e4m3(tmem + 256 * buf, ka, qb, id, (c | u) != 0);
-            else umma_f16<1>(tmem + 256 * buf, ka, qb, id, (c | u) != 0);
-          }
-        umma_commit(smem_u32(&bars.empty[s]));
-        umma_commit(smem_u32(&bars.tfull[buf]));
+            for (int u = 0; u < 4; ++u) {   // 32 bytes of K per MMA (16 bf16 / fp16, 32 fp8)
+              const uint64_t ka = dk + (uint64_t)((c * kKeys * 128 + u * 32) >> 4);
+              const uint64_t qb = dq + (uint64_t)((c * N * 128 + u * 32) >> 4);
+              if constexpr (kIsFp8<T>) umma_e4m3(tmem + 256 * buf, ka, qb, id, (c | u) != 0);
+              else umma_f16<1>(tmem + 256 * buf, ka, qb, id, (c | u) != 0);
+            }
+          umma_commit(smem_u32(&bars.empty[s]));
+          umma_commit(smem_u32(&bars.tfull[buf]));
+        }
+        __syncwarp();
       }
     }
     __syncwarp();

@@ -253,38 +253,44 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads1, 1)
     }
   } else if (warp == 1) {
     // ---- UMMA issue (pair leader): S^T and dP^T, M = 256 keys, N = 128 heads ----
-    if (cta == 0 && ntiles > 0 && lane == 0) {
+    // The whole warp runs the loop (waits included); one elected lane issues each tcgen05
+    // instruction (a lone lane issues MMAs much more slowly).
+    if (cta == 0 && ntiles > 0) {
       const bool bf16 = ElemTraits<T>::kIsBf16;
       const uint32_t id = idesc_f16(256, 128, bf16, false, false);
       const uint64_t dq = smem_desc_sw128(sQ, 16, 1024);
       const uint64_t dd = smem_desc_sw128(sO, 16, 1024);
       const uint64_t dx0 = smem_desc_sw128(sX, 16, 1024);
-      mbar_wait(smem_u32(&bars.q_full), 0, a.err, &failed);
+      mbar_wait_spin(smem_u32(&bars.q_full), 0, a.err, &failed);
       for (int t = 0; t < ntiles && !failed; ++t) {
         const int b = t & 1;
         if (t >= 2)
-          mbar_wait(smem_u32(&bars.tfree[b]), (uint32_t)((t >> 1) - 1) & 1u, a.err, &failed, true);
+          mbar_wait_spin(smem_u32(&bars.tfree[b]), (uint32_t)((t >> 1) - 1) & 1u, a.err, &failed, true);
         const uint32_t d_s = tmem + 256 * b, d_p = tmem + 256 * b + 128;
-        for (int c = 0; c < C::kChunks && !failed; ++c) {
+        for (int c = 0; c < C::kChunks; ++c) {
           const int j = t * C::kChunks + c, s = j % kStages1;
-          if (!mbar_wait(smem_u32(&bars.full[s]), (uint32_t)(j / kStages1) & 1u, a.err, &failed, true))
-            break;
+          mbar_wait_spin(smem_u32(&bars.full[s]), (uint32_t)(j / kStages1) & 1u, a.err, &failed, true);
+          if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
           tc_fence_after();
           const uint64_t bx = dx0 + (uint64_t)((s * C::kStage) >> 4);
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            umma_f16<2>(d_s, bx + (uint64_t)((u * 32) >> 4),
-                        dq + (uint64_t)((c * kHeads * 128 + u * 32) >> 4), id, (c | u) != 0);
-          if (c < C::kNope) {
+          if (elect_one()) {
 #pragma unroll
             for (int u = 0; u < 4; ++u)
-              umma_f16<2>(d_p, bx + (uint64_t)((u * 32) >> 4),
-                          dd + (uint64_t)((c * kHeads * 128 + u * 32) >> 4), id, (c | u) != 0);
+              umma_f16<2>(d_s, bx + (uint64_t)((u * 32) >> 4),
+                          dq + (uint64_t)((c * kHeads * 128 + u * 32) >> 4), id, (c | u) != 0);
+            if (c < C::kNope) {
+#pragma unroll
+              for (int u = 0; u < 4; ++u)
+                umma_f16<2>(d_p, bx + (uint64_t)((u * 32) >> 4),
+                            dd + (uint64_t)((c * kHeads * 128 + u * 32) >> 4), id, (c | u) != 0);
+            }
+            umma_commit_pair(smem_u32(&bars.empty[s]), 3);
           }
-          umma_commit_pair(smem_u32(&bars.empty[s]), 3);
+          __syncwarp();
         }
         if (failed) break;
-        umma_commit_pair(smem_u32(&bars.tfull[b]), 3);
+        if (elect_one()) umma_commit_pair(smem_u32(&bars.tfull[b]), 3);
+        __syncwarp();
       }
     }
     __syncwarp();
@@ -477,7 +483,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
       __syncwarp();
     }
   } else if (warp == 1) {
-    if (cta == 0 && ntiles > 0 && lane == 0) {
+    // (whole warp runs the loop, one elected lane issues; see K1)
+    if (cta == 0 && ntiles > 0) {
       const bool bf16 = ElemTraits<T>::kIsBf16;
       const uint32_t id_n = idesc_f16(128, C::kNPV, bf16, true, true);
       const uint32_t id_r = idesc_f16(128, 128, bf16, true, true);
@@ -487,28 +494,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
       const uint64_t dh1 = smem_desc_sw128(sH + C::kHBytes, kChunk, 1024);
       for (int t = 0; t < ntiles && !failed; ++t) {
         const int s = t & 1;
-        mbar_wait(smem_u32(&bars.a_full[s]), (t >> 1) & 1, a.err, &failed);
-        mbar_wait(smem_u32(&bars.h_full[s]), (t >> 1) & 1, a.err, &failed);
-        if (failed) break;
+        mbar_wait_spin(smem_u32(&bars.a_full[s]), (t >> 1) & 1, a.err, &failed);
+        mbar_wait_spin(smem_u32(&bars.h_full[s]), (t >> 1) & 1, a.err, &failed);
+        if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
         tc_fence_after();
         const uint64_t ba = s ? da1 : da0, bh = s ? dh1 : dh0;
+        if (elect_one()) {
 #pragma unroll
-        for (int j = 0; j < C::kNumPV; ++j)
+          for (int j = 0; j < C::kNumPV; ++j)
+#pragma unroll
+            for (int k = 0; k < kTile / 16; ++k)
+              umma_f16<2>(tmem + j * (C::kNPV / 2), ba + (uint64_t)((k * 2048) >> 4),
+                          bh + (uint64_t)(((k >> 1) * C::kHHalf + j * C::kCpj * kChunk + (k & 1) * 2048) >> 4),
+                          id_n, (t | k) != 0);
+          // rope: N=128 with the leader's B half holding the 64 rope dims; the other half
+          // is never read back (it lands in TMEM lanes 64-127)
 #pragma unroll
           for (int k = 0; k < kTile / 16; ++k)
-            umma_f16<2>(tmem + j * (C::kNPV / 2), ba + (uint64_t)((k * 2048) >> 4),
-                        bh + (uint64_t)(((k >> 1) * C::kHHalf + j * C::kCpj * kChunk + (k & 1) * 2048) >> 4),
-                        id_n, (t | k) != 0);
-        // rope: N=128 with the leader's B half holding the 64 rope dims; the other half
-        // is never read back (it lands in TMEM lanes 64-127)
-#pragma unroll
-        for (int k = 0; k < kTile / 16; ++k)
-          umma_f16<2>(tmem + C::kTmemRope, ba + (uint64_t)((k * 2048) >> 4),
-                      bh + (uint64_t)((C::kHNope + k * 2048) >> 4), id_r, (t | k) != 0);
-        umma_commit_pair(smem_u32(&bars.a_empty[s]), 3);
-        umma_commit_pair(smem_u32(&bars.h_empty[s]), 3);
+            umma_f16<2>(tmem + C::kTmemRope, ba + (uint64_t)((k * 2048) >> 4),
+                        bh + (uint64_t)((C::kHNope + k * 2048) >> 4), id_r, (t | k) != 0);
+          umma_commit_pair(smem_u32(&bars.a_empty[s]), 3);
+          umma_commit_pair(smem_u32(&bars.h_empty[s]), 3);
+        }
+        __syncwarp();
       }
-      if (!failed) umma_commit_pair(smem_u32(&bars.done), 3);
+      if (!failed && elect_one()) umma_commit_pair(smem_u32(&bars.done), 3);
+      __syncwarp();
     }
     __syncwarp();
   } else {
@@ -780,7 +791,9 @@ __global__ void __launch_bounds__(kThreads3, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ---- MMA: per tile and 128-column block, 8 K-steps of 16 heads ----
-    if (lane == 0) {
+    // The whole warp runs the loop (waits included); one elected lane issues each tcgen05
+    // instruction (a lone lane issues MMAs much more slowly).
+    {
       const bool bf16 = ElemTraits<T>::kIsBf16;
       const uint32_t id = idesc_f16(128, kKeyTile3, bf16, true, false);
       int na = 0, nb = 0, nt = 0;
@@ -790,30 +803,36 @@ __global__ void __launch_bounds__(kThreads3, 1)
         const bool rope = x.part == 2 * C::kDParts;
         const int nblk = rope ? 1 : C::kW / 128;
         const int ab = na & 1;
-        if (!mbar_wait_sleep(smem_u32(&bars.a_full[ab]), (na >> 1) & 1, a.err, &failed)) break;
+        mbar_wait_spin(smem_u32(&bars.a_full[ab]), (na >> 1) & 1, a.err, &failed);
+        if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
         for (int t = 0; t < x.ntiles; ++t) {
           const int s = nb % kStages3, tb = nt & 1;
-          if (!mbar_wait_sleep(smem_u32(&bars.b_full[s]), (nb / kStages3) & 1, a.err, &failed)) break;
-          if (!mbar_wait_sleep(smem_u32(&bars.t_empty[tb]), ((nt >> 1) & 1) ^ 1, a.err, &failed)) break;
+          mbar_wait_spin(smem_u32(&bars.b_full[s]), (nb / kStages3) & 1, a.err, &failed);
+          mbar_wait_spin(smem_u32(&bars.t_empty[tb]), ((nt >> 1) & 1) ^ 1, a.err, &failed);
+          if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
           tc_fence_after();
           const uint64_t db = smem_desc_sw128(sB + s * C::kTileB, 16, 1024);
-          for (int m = 0; m < nblk; ++m) {
-            // A: columns [128m, 128m+128) = two 64-column boxes (lbo = box stride); the
-            // rope part has one box, and lanes 64-127 of its result are never read
-            const uint64_t da = smem_desc_sw128(sA + ab * C::kSlice + 2 * m * C::kBox, C::kBox, 1024);
+          if (elect_one()) {
+            for (int m = 0; m < nblk; ++m) {
+              // A: columns [128m, 128m+128) = two 64-column boxes (lbo = box stride); the
+              // rope part has one box, and lanes 64-127 of its result are never read
+              const uint64_t da = smem_desc_sw128(sA + ab * C::kSlice + 2 * m * C::kBox, C::kBox, 1024);
 #pragma unroll
-            for (int k = 0; k < kHeadsPad / 16; ++k)
-              umma_f16<1>(tmem + tb * 256 + m * 128, da + (uint64_t)((k * 2048) >> 4),
-                          db + (uint64_t)(((k >> 2) * kKeyTile3 * 128 + (k & 3) * 32) >> 4), id,
-                          k != 0);
+              for (int k = 0; k < kHeadsPad / 16; ++k)
+                umma_f16<1>(tmem + tb * 256 + m * 128, da + (uint64_t)((k * 2048) >> 4),
+                            db + (uint64_t)(((k >> 2) * kKeyTile3 * 128 + (k & 3) * 32) >> 4), id,
+                            k != 0);
+            }
+            umma_commit(smem_u32(&bars.t_full[tb]));
+            umma_commit(smem_u32(&bars.b_empty[s]));
           }
-          umma_commit(smem_u32(&bars.t_full[tb]));
-          umma_commit(smem_u32(&bars.b_empty[s]));
+          __syncwarp();
           ++nb;
           ++nt;
         }
         if (failed) break;
-        umma_commit(smem_u32(&bars.a_empty[ab]));
+        if (elect_one()) umma_commit(smem_u32(&bars.a_empty[ab]));
+        __syncwarp();
         ++na;
       }
       // the MMAs issued last complete before the exit (their TMEM is freed afterwards)

@@ -210,26 +210,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTThreads, 1)
       __syncwarp();
     }
   } else if (warp == 1) {
-    if (cta == 0 && ntiles > 0 && lane == 0) {
+    // The whole warp runs the loop (waits included); one elected lane issues each tcgen05
+    // instruction (a lone lane issues MMAs much more slowly).
+    if (cta == 0 && ntiles > 0) {
       const bool bf16 = ElemTraits<T>::kIsBf16;
       const uint32_t id = idesc_f16(256, 128, bf16, false, false);
       const uint64_t dq = smem_desc_sw128(sQ, 16, 1024);
       const uint64_t dk = smem_desc_sw128(sK, 16, 1024);
-      mbar_wait(smem_u32(&bars.q_full), 0, a.err, &failed);
+      mbar_wait_spin(smem_u32(&bars.q_full), 0, a.err, &failed);
       for (int t = 0; t < ntiles && !failed; ++t) {
         const int buf = t & 1;
-        if (t >= 2) mbar_wait(smem_u32(&bars.tfree[buf]), ((t >> 1) - 1) & 1, a.err, &failed, true);
-        for (int c = 0; c < C::kChunks && !failed; ++c) {
+        if (t >= 2) mbar_wait_spin(smem_u32(&bars.tfree[buf]), ((t >> 1) - 1) & 1, a.err, &failed, true);
+        for (int c = 0; c < C::kChunks; ++c) {
           const int j = t * C::kChunks + c, s = j % kTStages;
-          if (!mbar_wait(smem_u32(&bars.full[s]), (j / kTStages) & 1, a.err, &failed, true)) break;
+          mbar_wait_spin(smem_u32(&bars.full[s]), (j / kTStages) & 1, a.err, &failed, true);
+          if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
           tc_fence_after();
+          if (elect_one()) {
 #pragma unroll
-          for (int u = 0; u < 4; ++u)
-            umma_f16<2>(tmem + 128 * buf, dk + (uint64_t)((s * C::kStage + u * 32) >> 4),
-                        dq + (uint64_t)((c * 64 * 128 + u * 32) >> 4), id, (c | u) != 0);
-          umma_commit_pair(smem_u32(&bars.empty[s]), 3);
+            for (int u = 0; u < 4; ++u)
+              umma_f16<2>(tmem + 128 * buf, dk + (uint64_t)((s * C::kStage + u * 32) >> 4),
+                          dq + (uint64_t)((c * 64 * 128 + u * 32) >> 4), id, (c | u) != 0);
+            umma_commit_pair(smem_u32(&bars.empty[s]), 3);
+          }
+          __syncwarp();
         }
-        umma_commit_pair(smem_u32(&bars.tfull[buf]), 3);
+        if (failed) break;
+        if (elect_one()) umma_commit_pair(smem_u32(&bars.tfull[buf]), 3);
+        __syncwarp();
       }
     }
     __syncwarp();
@@ -413,7 +421,8 @@ __global__ void __launch_bounds__(kIThreads, 1)
       __syncwarp();
     }
   } else if (warp == 1) {
-    if (lane == 0 && ntiles > 0) {
+    // (whole warp runs the loop, one elected lane issues; see the teacher kernel)
+    if (ntiles > 0) {
       const bool bf16 = ElemTraits<T>::kIsBf16;
       const uint32_t id_r = idesc_f16(128, kNip, bf16, false, false);   // R = KI QI^T
       const uint32_t id_q = idesc_f16(128, kNip, bf16, true, true);     // dQI^T += KI^T C
@@ -423,47 +432,54 @@ __global__ void __launch_bounds__(kIThreads, 1)
       for (int j = 0; j < nsteps && !failed; ++j) {
         const int t = j % ntiles, s = j % kIStages, rb = j & 1;
         const bool passB = j >= ntiles;
-        if (j >= 2) mbar_wait(smem_u32(&bars.rfree[rb]), ((j >> 1) - 1) & 1, a.err, &failed);
-        if (!mbar_wait(smem_u32(&bars.full[s]), (j / kIStages) & 1, a.err, &failed)) break;
+        if (j >= 2) mbar_wait_spin(smem_u32(&bars.rfree[rb]), ((j >> 1) - 1) & 1, a.err, &failed);
+        mbar_wait_spin(smem_u32(&bars.full[s]), (j / kIStages) & 1, a.err, &failed);
+        if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
         tc_fence_after();
         const uint64_t dk_k = smem_desc_sw128(sK + s * C::kStage, 16, 1024);
+        if (elect_one()) {
 #pragma unroll
-        for (int c = 0; c < 2; ++c)
+          for (int c = 0; c < 2; ++c)
 #pragma unroll
-          for (int u = 0; u < 4; ++u)
-            umma_f16<1>(tR + 64 * rb, dk_k + (uint64_t)((c * kIKeys * 128 + u * 32) >> 4),
-                        dqi_k + (uint64_t)((c * kNip * 128 + u * 32) >> 4), id_r, (c | u) != 0);
-        umma_commit(smem_u32(&bars.rfull[rb]));
-        if (!passB) {
-          umma_commit(smem_u32(&bars.empty[s]));
-          continue;
+            for (int u = 0; u < 4; ++u)
+              umma_f16<1>(tR + 64 * rb, dk_k + (uint64_t)((c * kIKeys * 128 + u * 32) >> 4),
+                          dqi_k + (uint64_t)((c * kNip * 128 + u * 32) >> 4), id_r, (c | u) != 0);
+          umma_commit(smem_u32(&bars.rfull[rb]));
+          if (!passB) umma_commit(smem_u32(&bars.empty[s]));
         }
+        __syncwarp();
+        if (!passB) continue;
         // pass B: wait for C of this tile, then dQI^T and dKI
         const int tb = t, cb = tb & 1;
-        if (!mbar_wait(smem_u32(&bars.cready[cb]), (tb >> 1) & 1, a.err, &failed)) break;
         const int db = tb & 1;
-        if (tb >= 2 && !mbar_wait(smem_u32(&bars.dfree[db]), ((tb >> 1) - 1) & 1, a.err, &failed)) break;
+        mbar_wait_spin(smem_u32(&bars.cready[cb]), (tb >> 1) & 1, a.err, &failed);
+        if (tb >= 2) mbar_wait_spin(smem_u32(&bars.dfree[db]), ((tb >> 1) - 1) & 1, a.err, &failed);
+        if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
         tc_fence_after();
         const uint64_t dc_k = smem_desc_sw128(sC + cb * C::kCBytes, 16, 1024);
         const uint64_t dc_mn = smem_desc_sw128(sC + cb * C::kCBytes, 16, 1024);
         const uint64_t dk_mn = smem_desc_sw128(sK + s * C::kStage, kIKeys * 128, 1024);
+        if (elect_one()) {
 #pragma unroll
-        for (int part = 0; part < 2; ++part) {   // C = hi + lo
-          const uint32_t po = part * kIKeys * 128;
+          for (int part = 0; part < 2; ++part) {   // C = hi + lo
+            const uint32_t po = part * kIKeys * 128;
 #pragma unroll
-          for (int k = 0; k < kIKeys / 16; ++k)   // K = keys
-            umma_f16<1>(tQ, dk_mn + (uint64_t)((k * 2048) >> 4),
-                        dc_mn + (uint64_t)((po + k * 2048) >> 4), id_q, (tb | k | part) != 0);
+            for (int k = 0; k < kIKeys / 16; ++k)   // K = keys
+              umma_f16<1>(tQ, dk_mn + (uint64_t)((k * 2048) >> 4),
+                          dc_mn + (uint64_t)((po + k * 2048) >> 4), id_q, (tb | k | part) != 0);
 #pragma unroll
-          for (int u = 0; u < kNip / 16; ++u)     // K = index heads
-            umma_f16<1>(tD + 128 * db, dc_k + (uint64_t)((po + u * 32) >> 4),
-                        dqi_mn + (uint64_t)((u * 2048) >> 4), id_d, (u | part) != 0);
+            for (int u = 0; u < kNip / 16; ++u)     // K = index heads
+              umma_f16<1>(tD + 128 * db, dc_k + (uint64_t)((po + u * 32) >> 4),
+                          dqi_mn + (uint64_t)((u * 2048) >> 4), id_d, (u | part) != 0);
+          }
+          umma_commit(smem_u32(&bars.empty[s]));
+          umma_commit(smem_u32(&bars.cfree[cb]));
+          umma_commit(smem_u32(&bars.dfull[db]));
         }
-        umma_commit(smem_u32(&bars.empty[s]));
-        umma_commit(smem_u32(&bars.cfree[cb]));
-        umma_commit(smem_u32(&bars.dfull[db]));
+        __syncwarp();
       }
-      if (!failed) umma_commit(smem_u32(&bars.qdone));
+      if (!failed && elect_one()) umma_commit(smem_u32(&bars.qdone));
+      __syncwarp();
     }
     __syncwarp();
   } else if (warp >= kIDrain0) {
