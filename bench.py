@@ -438,13 +438,112 @@ def _timed(fn, steps, warmup, stream):
     return float(np.mean([a.elapsed_time(b) for a, b in ev]))
 
 
+def run_sli(args, rank, world, local):
+    """BASELINE config 5 (indexer KL-loss gradient, S1=S2=8192, N1=128, Nidx1=64, top-2048)
+    with S1 sharded over the ranks (strong scaling): each rank computes its causal row range,
+    the fp32 dKeyIndex accumulators and the loss are summed with one NCCL all-reduce, then
+    cast.  The softmax statistics come from config 4's forward on the same query / key."""
+    import torch.distributed as dist
+    from datetime import timedelta
+    import dsa_triton_ascend_b200 as dsa
+    from dsa_triton_ascend_b200.sharding import shard_act_q, shard_rows
+    from dsa_triton_ascend_b200.synthetic import sli_prefill, valid_pairs_per_row
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    stream = torch.cuda.current_stream(dev)
+    w = sli_prefill(device=dev, seed=0)
+    S = w["q"].shape[1]
+    pairs = valid_pairs_per_row(w["si"]).cpu().numpy()
+    r0, r1 = shard_rows(pairs, world, rank)
+    cut = lambda t: t[:, r0:r1].contiguous()
+    q, qr, qi, wt, si = cut(w["q"]), cut(w["qr"]), cut(w["qi"]), cut(w["w"]), cut(w["si"])
+    aq = [shard_act_q(S, r0)]
+    _, mx, sm = dsa.sparse_flash_attention_triton(
+        q, w["k"], w["k"], si, w["scale"], actual_seq_lengths_query=aq, query_rope=qr,
+        key_rope=w["kr"], sparse_mode=3, return_softmax_lse=True)
+
+    def step(ev=None):
+        (_, _), finish = dsa.sparse_lightning_indexer_grad_kl_loss_partial(
+            q, w["k"], qi, w["ki"], wt, si, mx, sm, query_rope=qr, key_rope=w["kr"],
+            actual_seq_qlen=aq, scale_value=w["scale"])
+        if world > 1:
+            if ev is not None:
+                ev[0].record(stream)
+            dist.all_reduce(finish.key_grad_buffer)
+            if ev is not None:
+                ev[1].record(stream)
+        return finish()
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    dsa.check_device_errors(dev)
+    mk = lambda: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+    ev_r = [mk() for _ in range(args.steps)]
+    sampler = ClockSampler(local)
+    sampler.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    start, end = mk()
+    start.record(stream)
+    for i in range(args.steps):
+        step(ev_r[i])
+    end.record(stream)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    dsa.check_device_errors(dev)
+    ms_mine = start.elapsed_time(end) / args.steps
+    ar_ms = float(np.mean([a.elapsed_time(b) for a, b in ev_r])) if world > 1 else 0.0
+    mine = torch.tensor([ms_mine, ar_ms, float(pairs[r0:r1].sum())], device=dev, dtype=torch.float64)
+    if world > 1:
+        allr = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(allr, mine)
+        per_rank = [x.tolist() for x in allr]
+    else:
+        per_rank = [mine.tolist()]
+    ms = max(r[0] for r in per_rank)
+    total_pairs = int(pairs.sum())
+    flops = total_pairs * 2 * (64 * 128 * 3 + 128 * 576)
+    nbytes = total_pairs * (GATHER_BYTES_PER_PAIR + 256)
+    hbm_peak, tf_peak, peak_kind = load_peaks()
+    t_b, t_f = nbytes / (hbm_peak * 1e9) / world, flops / (tf_peak * 1e12) / world
+    bound = "hbm" if t_b >= t_f else "tensor"
+    if rank == 0:
+        line = {"metric": "SLI KL-grad TFLOP/s", "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic",
+                "config": {"workload": "BASELINE config 5 (S1=S2=8192, N1=128, Nidx1=64, top-2048), S1 sharded",
+                           "timing": "CUDA events around the steps, max over ranks",
+                           "parallelism": f"query-row shards x{world}"},
+                "roofline": {"bound": bound,
+                             "achieved": (nbytes / world / (ms * 1e-3) / 1e9) if bound == "hbm"
+                             else flops / world / (ms * 1e-3) / 1e12,
+                             "peak": hbm_peak if bound == "hbm" else tf_peak,
+                             "unit": "GB/s" if bound == "hbm" else "TFLOP/s",
+                             "frac": max(t_b, t_f) / (ms * 1e-3),
+                             "traffic": WORKLOAD_DRAM_BYTES.get("sli") if world == 1 else None,
+                             "peak_source": peak_kind},
+                "ranks": [{"rank": i, "step_ms": r[0], "allreduce_ms": r[1], "pairs": int(r[2])}
+                          for i, r in enumerate(per_rank)],
+                "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_other(args, rank, world, local):
     """Secondary workloads (configs 2, 3, 5): one GPU, device-timed, one JSON line each.
 
     With N GPUs every rank runs its own replica of the workload (weak scaling)."""
     import math as _m
     import dsa_triton_ascend_b200 as dsa
-    from dsa_triton_ascend_b200.synthetic import causal_topk_ids
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     stream = torch.cuda.current_stream(dev)
@@ -476,38 +575,17 @@ def run_other(args, rank, world, local):
         metric, unit, wl = ("LI FP8 score+top-k TFLOP/s", "TFLOP/s",
                             "config 2 geometry, FP8 indexer (B=2, S1=S2=4096, N1=64, D=128, top-2048, mode 3)")
     elif args.workload == "decode":
-        B, N1_, page, nblk, maxb, K = 32, 128, 128, 16384, 512, 2048
-        lens = torch.randint(8192, 65537, (B,), generator=g, device=dev)
-        cache = rn(nblk, page, 1, D)
-        cache_r = rn(nblk, page, 1, DR)
-        bt = torch.randperm(nblk, generator=g, device=dev)[: B * maxb].reshape(B, maxb).int()
-        q, qr = rn(B, 1, N1_, D), rn(B, 1, N1_, DR)
-        u = torch.rand(B, 65536, generator=g, device=dev)
-        u = torch.where(torch.arange(65536, device=dev)[None] < lens[:, None], u, -1.0)
-        si = torch.sort(torch.topk(u, K, dim=1).indices, dim=1).values.int().reshape(B, 1, 1, K)
-        lens_l = lens.tolist()
+        from dsa_triton_ascend_b200.synthetic import sfa_decode
+        wd = sfa_decode(device=dev, seed=0)
         fn = lambda: dsa.sparse_flash_attention_triton(
-            q, cache, cache, si, 1 / _m.sqrt(576), block_table=bt, actual_seq_lengths_kv=lens_l,
-            query_rope=qr, key_rope=cache_r, layout_kv="PA_BSND", sparse_mode=0,
-            return_softmax_lse=True, block_size=page)
-        pairs = B * K
+            wd["q"], wd["cache"], wd["cache"], wd["si"], wd["scale"], block_table=wd["block_table"],
+            actual_seq_lengths_kv=wd["lens"], query_rope=wd["qr"], key_rope=wd["cache_r"],
+            layout_kv="PA_BSND", sparse_mode=0, return_softmax_lse=True, block_size=wd["page"])
+        pairs = wd["si"].numel()
         flops, nbytes = pairs * FWD_FLOP_PER_PAIR, pairs * GATHER_BYTES_PER_PAIR
         metric, unit, wl = "SFA decode TFLOP/s", "TFLOP/s", "BASELINE config 3 (PA_BSND, B=32, S1=1, N1=128, top-2048, 16384-block pool)"
     else:
-        S, N1_, Ni, K = 8192, 128, 64, 2048
-        q, qr, k, kr = rn(1, S, N1_, D), rn(1, S, N1_, DR), rn(1, S, 1, D), rn(1, S, 1, DR)
-        qi, ki = rn(1, S, Ni, 128), rn(1, S, 1, 128)
-        w = torch.randn(1, S, Ni, generator=g, device=dev) / 8
-        si = causal_topk_ids(S, S, K, g, dev).reshape(1, S, 1, K)
-        sc = 1 / _m.sqrt(576)
-        _, mx, sm = dsa.sparse_flash_attention_triton(q, k, k, si, sc, query_rope=qr, key_rope=kr,
-                                                      sparse_mode=3, return_softmax_lse=True)
-        fn = lambda: dsa.sparse_lightning_indexer_grad_kl_loss_triton(
-            q, k, qi, ki, w, si, mx, sm, query_rope=qr, key_rope=kr, scale_value=sc)
-        pairs = int((si >= 0).sum().item())
-        flops = pairs * 2 * (64 * 128 * 3 + 128 * 576)
-        nbytes = pairs * (GATHER_BYTES_PER_PAIR + 256)
-        metric, unit, wl = "SLI KL-grad TFLOP/s", "TFLOP/s", "BASELINE config 5 (S1=S2=8192, N1=128, Nidx1=64, top-2048)"
+        return run_sli(args, rank, world, local)
     timing = "CUDA events around each call"
     if args.workload == "decode":
         # A decode step is ~70 us of GPU work, about as long as the Python call that enqueues

@@ -28,6 +28,7 @@ from .lightning_indexer import (  # noqa: F401
 )
 from .sparse_lightning_indexer_grad_kl_loss import (  # noqa: F401
     SparseLightningIndexerGradKLLossTriton,
+    sparse_lightning_indexer_grad_kl_loss_partial,
     sparse_lightning_indexer_grad_kl_loss_triton,
 )
 from .sparse_flash_attention_grad import (  # noqa: F401

@@ -141,6 +141,8 @@ def lib() -> ctypes.CDLL:
                 l.dsa_li_workspace_size.restype = _i64
                 l.dsa_sli_grad.argtypes = [ctypes.POINTER(SliParams), _p]
                 l.dsa_sli_grad.restype = ctypes.c_int
+                l.dsa_sli_cast.argtypes = [ctypes.POINTER(SliParams), _p]
+                l.dsa_sli_cast.restype = ctypes.c_int
                 l.dsa_sli_workspace_size.argtypes = [_i64, _i64, _i64]
                 l.dsa_sli_workspace_size.restype = _i64
                 for fn in (l.dsa_dense_indexer_softmax_lse, l.dsa_dense_indexer_grad_kl_loss):

@@ -783,3 +783,22 @@ extern "C" int dsa_sli_grad(const DsaSliParams* p, void* stream_) {
   }
   return DSA_ERR_INVALID_ARG;
 }
+
+// Cast of the fp32 dKeyIndex accumulator into the key_index dtype: the tail of dsa_sli_grad,
+// for callers that pass d_key_index = NULL there and reduce dki_acc themselves first (query
+// rows sharded across GPUs).
+extern "C" int dsa_sli_cast(const DsaSliParams* p, void* stream_) {
+  using namespace dsa::sli;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  if (!p || !p->dki_acc || !p->d_key_index || p->batch < 1 || p->s2 < 1) return DSA_ERR_INVALID_ARG;
+  const int64_t nk = p->batch * p->s2 * kDi;
+  const dim3 grid((unsigned)((nk + 255) / 256));
+  if (p->dtype == DSA_DTYPE_BF16)
+    sli_cast_kernel<__nv_bfloat16><<<grid, dim3(256), 0, stream>>>(
+        p->dki_acc, static_cast<__nv_bfloat16*>(p->d_key_index), nk);
+  else if (p->dtype == DSA_DTYPE_FP16)
+    sli_cast_kernel<__half><<<grid, dim3(256), 0, stream>>>(p->dki_acc, static_cast<__half*>(p->d_key_index), nk);
+  else
+    return DSA_ERR_INVALID_ARG;
+  return cudaGetLastError() == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
+}

@@ -32,6 +32,32 @@ def sparse_lightning_indexer_grad_kl_loss_triton(
     deterministic: bool = False,
 ):
     """Drop-in replacement for aclnnSparseLightningIndexerGradKLLoss (BSND, mode 3)."""
+    return _sli(query, key, query_index, key_index, weights, sparse_indices, softmax_max,
+                softmax_sum, query_rope, key_rope, actual_seq_qlen, actual_seq_klen, scale_value,
+                layout, sparse_mode, defer_cast=False)
+
+
+def sparse_lightning_indexer_grad_kl_loss_partial(
+    query, key, query_index, key_index, weights, sparse_indices, softmax_max, softmax_sum,
+    query_rope=None, key_rope=None, actual_seq_qlen=None, actual_seq_klen=None,
+    scale_value=1.0, layout="BSND", sparse_mode=3):
+    """The indexer KL-loss gradient for a caller that sums it over GPUs itself.
+
+    Same arguments as :func:`sparse_lightning_indexer_grad_kl_loss_triton` (a contiguous
+    causal row range [r0, r1) of a BSND batch is passed as its own query with
+    ``actual_seq_qlen = S1 - r0``, see ``sharding.py``).  Returns ``((dki_acc, loss),
+    finish)``: the fp32 dKeyIndex accumulator [B*S2, 128] and this call's loss [1], both
+    views of one contiguous buffer ``finish.key_grad_buffer`` (one all-reduce sums both),
+    and ``finish()``, which casts the (reduced) accumulator to the key_index dtype and
+    returns (dQueryIndex, dKeyIndex, dWeights, loss)."""
+    return _sli(query, key, query_index, key_index, weights, sparse_indices, softmax_max,
+                softmax_sum, query_rope, key_rope, actual_seq_qlen, actual_seq_klen, scale_value,
+                layout, sparse_mode, defer_cast=True)
+
+
+def _sli(query, key, query_index, key_index, weights, sparse_indices, softmax_max, softmax_sum,
+         query_rope, key_rope, actual_seq_qlen, actual_seq_klen, scale_value, layout,
+         sparse_mode, defer_cast):
     # guards: sparse_lightning_indexer_grad_kl_loss_triton.py:534-538
     if layout != "BSND":
         raise ValueError("Only BSND layout is supported in triton path")
@@ -70,8 +96,12 @@ def sparse_lightning_indexer_grad_kl_loss_triton(
     d_qi = torch.empty_like(qi)
     d_ki = torch.empty_like(ki)
     d_w = torch.empty_like(w)
-    loss = torch.empty((1,), dtype=torch.float32, device=dev)
-    dki_acc = torch.empty((B * S2, Di), dtype=torch.float32, device=dev)
+    # [dKeyIndex accumulator | loss | pad]: one buffer, so that a sharded caller sums both
+    # with a single all-reduce
+    nk = B * S2 * Di
+    flat = torch.empty(nk + 4, dtype=torch.float32, device=dev)
+    dki_acc = flat[:nk].view(B * S2, Di)
+    loss = flat[nk:nk + 1]
     ws_bytes = lib().dsa_sli_workspace_size(B, S1, topk)
     ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=dev)
     p = SliParams()
@@ -79,7 +109,7 @@ def sparse_lightning_indexer_grad_kl_loss_triton(
     p.query_index, p.key_index, p.weights = ptr(qi), ptr(ki), ptr(w)
     p.sparse_indices, p.softmax_max, p.softmax_sum = ptr(si), ptr(smax), ptr(ssum)
     p.act_q, p.act_k = ptr(act_q), ptr(act_k)
-    p.d_query_index, p.d_key_index, p.d_weights = ptr(d_qi), ptr(d_ki), ptr(d_w)
+    p.d_query_index, p.d_key_index, p.d_weights = ptr(d_qi), 0 if defer_cast else ptr(d_ki), ptr(d_w)
     p.dki_acc, p.loss = ptr(dki_acc), ptr(loss)
     p.error_flag = ptr(error_flag(dev))
     p.workspace, p.workspace_bytes = ptr(ws), ws_bytes
@@ -89,6 +119,15 @@ def sparse_lightning_indexer_grad_kl_loss_triton(
     p.dtype = H.dtype_code(query)
     p.weights_dtype = DSA_DTYPE_FP32 if w.dtype == torch.float32 else H.dtype_code(w)
     check(lib().dsa_sli_grad(p, stream_ptr(dev)), "dsa_sli_grad")
+    if defer_cast:
+        p.d_key_index = ptr(d_ki)
+
+        def finish():
+            check(lib().dsa_sli_cast(p, stream_ptr(dev)), "dsa_sli_cast")
+            return d_qi, d_ki, d_w, loss
+        finish.key_grad_buffer = flat
+        finish.keep_alive = (q, k, qr, kr, qi, ki, w, si, smax, ssum, act_q, act_k, ws)
+        return (dki_acc, loss), finish
     return d_qi, d_ki, d_w, loss
 
 

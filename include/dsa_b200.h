@@ -321,6 +321,12 @@ typedef struct DsaSliParams {
 } DsaSliParams;
 
 int dsa_sli_grad(const DsaSliParams* params, void* stream);
+
+/* Cast dki_acc into d_key_index (key_index dtype): the tail of dsa_sli_grad, for a caller
+ * that passed d_key_index = NULL there and summed dki_acc (and loss) over the GPUs that
+ * hold disjoint query rows first.  Sharding support; the reference has no counterpart
+ * (its scatter-and-cast is one call, sparse_lightning_indexer_grad_kl_loss_triton.py:268-327). */
+int dsa_sli_cast(const DsaSliParams* params, void* stream);
 int64_t dsa_sli_workspace_size(int64_t batch, int64_t s1, int64_t topk);
 
 /*

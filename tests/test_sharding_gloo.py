@@ -107,3 +107,58 @@ def test_cpulist_parsing_and_binding_without_gpu():
         assert bind_host_to_device() is False
         assert os.sched_getaffinity(0) == before
 
+
+def _sli_worker(rank, world, port, case, out_q):
+    """One rank: the indexer KL-loss gradient of its causal row shard (oracle), then the
+    all-reduce of the fp32 dKeyIndex accumulator and the loss."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import inputs as I
+    from oracle import sli
+    c = I.sli_case(*case)
+    S1 = c["q"].shape[1]
+    topk = c["si"].shape[-1]
+    S2 = c["k"].shape[1]
+    pairs = np.minimum(topk, np.maximum(S2 - S1 + np.arange(S1) + 1, 0))
+    r0, r1 = shard_rows(pairs, world, rank)
+    sl = slice(r0, r1)
+    mx, sm = sli.softmax_stats_full(c["q"], c["k"], c["qr"], c["kr"], c["scale"])
+    r = sli.sli_grad(c["q"][:, sl], c["k"], c["qr"][:, sl], c["kr"], c["qi"][:, sl], c["ki"],
+                     c["w"][:, sl], c["si"][:, sl], mx[:, :, sl], sm[:, :, sl], c["scale"],
+                     act_q=[shard_act_q(S1, r0)])
+    buf = torch.from_numpy(np.concatenate([r["dKeyIndex"].ravel(), r["loss"].ravel()]).astype(np.float32))
+    dist.all_reduce(buf)
+    dqi = [torch.zeros(0)] * world
+    dist.all_gather_object(dqi, torch.from_numpy(r["dQueryIndex"]))
+    if rank == 0:
+        out_q.put((buf.numpy(), torch.cat(dqi, dim=1).numpy()))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_two_rank_sli_matches_single_rank():
+    """Config-5 style sharding of the indexer KL loss: S1 split into two causal row ranges,
+    dKeyIndex and the loss summed by an all-reduce, dQueryIndex gathered."""
+    case = (1, 10, 40, 8, 128, 4, 128, 16, "causal_random", "fp32", 9)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_sli_worker, args=(r, 2, port, case, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    buf, dqi = q.get(timeout=240)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    import inputs as I
+    from oracle import sli
+    c = I.sli_case(*case)
+    mx, sm = sli.softmax_stats_full(c["q"], c["k"], c["qr"], c["kr"], c["scale"])
+    ref = sli.sli_grad(c["q"], c["k"], c["qr"], c["kr"], c["qi"], c["ki"], c["w"], c["si"], mx, sm,
+                       c["scale"])
+    nk = ref["dKeyIndex"].size
+    np.testing.assert_allclose(buf[:nk].reshape(ref["dKeyIndex"].shape), ref["dKeyIndex"],
+                               rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(buf[nk], ref["loss"][0], rtol=1e-5)
+    np.testing.assert_allclose(dqi, ref["dQueryIndex"], rtol=1e-5, atol=1e-6)

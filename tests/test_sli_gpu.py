@@ -68,3 +68,37 @@ def test_sli_actual_lengths():
                        c["scale"], act_q=aq, act_k=ak)
     _check(got, ref, "lens")
     assert np.all(got[0][1, 4:] == 0) and np.all(got[2][1, 4:] == 0)
+
+
+def test_sli_partial_row_shards_sum_to_full_call():
+    """Query-row shards through the partial entry point (fp32 dKeyIndex and loss left
+    unreduced, as a multi-GPU caller gets them): their sum, cast once, equals the full call."""
+    import dsa_triton_ascend_b200 as dsa
+    B, S1, S2 = 1, 40, 512
+    c = I.sli_case(B, S1, S2, 64, 512, 16, 128, 96, "causal_random", "bf16", seed=61)
+    mx, sm = sli.softmax_stats_full(c["q"], c["k"], c["qr"], c["kr"], c["scale"])
+    t = {n: cuda(c[n], "bf16") for n in ("q", "k", "qr", "kr", "qi", "ki")}
+    w = cuda(c["w"], "fp32")
+    si, mxg, smg = icuda(c["si"]), cuda(mx, "fp32"), cuda(sm, "fp32")
+    full = dsa.sparse_lightning_indexer_grad_kl_loss_triton(
+        t["q"], t["k"], t["qi"], t["ki"], w, si, mxg, smg, query_rope=t["qr"], key_rope=t["kr"],
+        scale_value=c["scale"])
+    total, fin = None, []
+    for r0, r1 in [(0, 17), (17, S1)]:
+        cut = lambda x: x[:, r0:r1].contiguous()
+        (acc, loss), finish = dsa.sparse_lightning_indexer_grad_kl_loss_partial(
+            cut(t["q"]), t["k"], cut(t["qi"]), t["ki"], cut(w), cut(si),
+            mxg[:, :, r0:r1].contiguous(), smg[:, :, r0:r1].contiguous(), query_rope=cut(t["qr"]),
+            key_rope=t["kr"], actual_seq_qlen=[S1 - r0], scale_value=c["scale"])
+        buf = finish.key_grad_buffer
+        total = buf.clone() if total is None else total + buf
+        fin.append((r0, r1, finish))
+    # the summed buffer (dKeyIndex | loss) goes back into one shard's buffer, as an
+    # all-reduce would leave it, and that shard's finish() casts it
+    r0, r1, finish = fin[-1]
+    finish.key_grad_buffer.copy_(total)
+    dqi, dki, dw, loss = finish()
+    dsa.check_device_errors()
+    torch.testing.assert_close(loss, full[3], rtol=1e-4, atol=1e-6)
+    torch.testing.assert_close(dki.float(), full[1].float(), rtol=2e-2, atol=2e-3)
+    assert torch.equal(dqi, full[0][:, r0:r1]) and torch.equal(dw, full[2][:, r0:r1])
