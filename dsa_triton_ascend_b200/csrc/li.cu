@@ -14,10 +14,15 @@
 // (lightning_indexer_triton.py:271-276); tiles past the block's last visible key are
 // never computed (the top-k pass never reads them).
 //
-// Top-k kernel: one CTA per (row, n2): 4-pass 8-bit radix select of the k-th largest
-// score over the visible prefix, ordered compaction (ties at the threshold taken in
-// ascending index order), then a bitonic sort by (score desc, index asc).  -inf slots
-// get index -1 (:353-355).  Values are returned in the query dtype (:541-542).
+// Top-k kernel: one CTA per (row, n2), output ordered by (score desc, index asc) over the
+// visible prefix.  Bucket path: one histogram of the scores over 4096 equal value buckets
+// between the row's minimum and maximum finds the bucket of the k-th score; the buckets
+// above it are scattered in descending order and every score finds its place inside its
+// bucket by counting (a few entries each for spread-out scores).  Radix path, for rows with
+// non-finite or clustered scores: 4-pass 8-bit radix select of the k-th largest, ordered
+// compaction (ties at the threshold taken in ascending index order), then a stable LSD
+// radix sort by score.  Slots past the visible keys get index -1 (:353-355).  Values are
+// returned in the query dtype (:541-542).
 //
 // FP8 indexer (no counterpart in the reference): e4m3 query and key with a positive fp32
 // scale per key row, score = key_scale * sum_g ReLU(q_g . k) * w_g (a query scale is folded
@@ -377,8 +382,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 // =====================================================================================
 constexpr int kTopkThreads = 512;
 
+// Unsigned key with the order of the float (-0 counts as +0, as in a float comparison).
 __device__ __forceinline__ uint32_t order_key(float f) {
   uint32_t u = __float_as_uint(f);
+  if (u == 0x80000000u) u = 0u;
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 __device__ __forceinline__ float key_float(uint32_t k) {
@@ -426,78 +433,147 @@ __device__ __forceinline__ int block_scan(int v, int* warp_sums, int* total) {
   return base + x - v;
 }
 
-// Bitonic sort (descending) of E * kTopkThreads 64-bit keys, thread t holding positions
-// [E t, E t + E) in registers: strides below E are exchanged inside the thread, strides
-// below 32 E between the lanes of a warp (shuffles), and only the wider ones go through
-// shared memory with a block barrier.
+// Lanes of this warp whose 8-bit `digit` equals this lane's, among the lanes in `m`
+// (8 ballots: one per digit bit).
+__device__ __forceinline__ unsigned digit_peers(unsigned m, uint32_t digit) {
+#pragma unroll
+  for (int b = 0; b < 8; ++b) {
+    const bool bit = (digit >> b) & 1u;
+    const unsigned v = __ballot_sync(0xffffffffu, bit);
+    m &= bit ? v : ~v;
+  }
+  return m;
+}
+
+constexpr int kTopkWarps = kTopkThreads / 32;
+constexpr int kHistInts = 256 * kTopkWarps;   // one 256-digit histogram per warp
+constexpr int kBuckets = 4096;                // value buckets of the bucket path
+constexpr int kMaxBucket = 64;                // a larger selected bucket sends the row to the radix path
+static_assert(2 * kHistInts >= 2 * kBuckets, "bucket counts and cursors share the histogram space");
+
+// Bucket of score x: the range [xmin, xmax] cut into kBuckets equal parts.  Subtraction,
+// multiplication by a positive scale and truncation are all monotone, so a larger score
+// never lands in a lower bucket.
+__device__ __forceinline__ int value_bucket(float x, float xmin, float scale) {
+  const int b = __float2int_rz((x - xmin) * scale);
+  return min(max(b, 0), kBuckets - 1);
+}
+
+// Stable sort of the n packed (key << 32 | index) pairs in sel by key, descending, in
+// place: least-significant-digit radix sort, 8-bit digits.  Warp w holds positions
+// [32 E w, 32 E (w + 1)) in registers (E per lane, in rounds of 32).  Each pass counts the
+// digits of every round in the warp's own histogram (ballots give the lanes with the same
+// digit, so the rank among them is a popcount and one lane adds their count), scans the
+// histograms in (digit, warp) order, which is position order within each digit, and
+// scatters.  Equal keys therefore keep their input order.  The histograms are laid out
+// [warp][digit] so that different digits fall in different shared-memory banks; the scan
+// runs down the columns (thread d owns digit d).  Two histogram buffers alternate: the
+// threads that own no digit clear the next pass's buffer during the scan.  Passes over a
+// byte in which all keys agree are skipped.  hist holds 2 * kHistInts ints.
 template <int E>
-__device__ __forceinline__ void bitonic_desc(unsigned long long* sel) {
-  constexpr int kN = E * kTopkThreads;
-  const int t = threadIdx.x;
+__device__ __forceinline__ void radix_sort_desc(unsigned long long* sel, int n, int* hist,
+                                                int* warp_sums, uint32_t* s_and_or) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const unsigned lt_mask = (1u << lane) - 1u;
   unsigned long long v[E];
+  int off[E];
+  uint32_t all_and = 0xffffffffu, all_or = 0u;
 #pragma unroll
-  for (int e = 0; e < E; ++e) v[e] = sel[E * t + e];
-  for (int size = 2; size <= kN; size <<= 1) {
-    for (int stride = size >> 1; stride >= E; stride >>= 1) {
-      if (stride >= 32 * E) {
-        // through shared memory
-#pragma unroll
-        for (int e = 0; e < E; ++e) sel[E * t + e] = v[e];
-        __syncthreads();
-        // keep the larger of the pair when this slot is the descending block's low end or
-        // the ascending block's high end; stride >= E, so that is the same for all E elements
-        const bool keep_max = (((E * t) & size) == 0) == (((E * t) & stride) == 0);
-#pragma unroll
-        for (int e = 0; e < E; ++e) {
-          const unsigned long long y = sel[(E * t + e) ^ stride];
-          v[e] = ((v[e] > y) == keep_max) ? v[e] : y;
-        }
-        __syncthreads();
-      } else {
-        const int lx = stride / E;   // partner lane distance
-        const bool keep_max = (((E * t) & size) == 0) == (((E * t) & stride) == 0);
-#pragma unroll
-        for (int e = 0; e < E; ++e) {
-          const unsigned long long y = __shfl_xor_sync(0xffffffffu, v[e], lx);
-          v[e] = ((v[e] > y) == keep_max) ? v[e] : y;
-        }
-      }
-    }
-    // strides inside the thread (compile-time, so v stays in registers)
-#pragma unroll
-    for (int st = E >> 1; st > 0; st >>= 1) {
-      if (st < size) {
-#pragma unroll
-        for (int e = 0; e < E; ++e) {
-          const int f = e ^ st;
-          if (f > e) {
-            // direction of element e's block: from the thread when size >= E, else from e
-            const bool desc = size >= E ? ((E * t) & size) == 0 : (e & size) == 0;
-            const unsigned long long x = v[e], y = v[f];
-            const bool swap = (x < y) == desc;   // keys are distinct (the index is part of them)
-            v[e] = swap ? y : x;
-            v[f] = swap ? x : y;
-          }
-        }
-      }
+  for (int r = 0; r < E; ++r) {
+    const int p = 32 * E * warp + 32 * r + lane;
+    v[r] = p < n ? sel[p] : 0ull;
+    if (p < n) {
+      all_and &= (uint32_t)(v[r] >> 32);
+      all_or |= (uint32_t)(v[r] >> 32);
     }
   }
-#pragma unroll
-  for (int e = 0; e < E; ++e) sel[E * t + e] = v[e];
+  if (threadIdx.x == 0) {
+    s_and_or[0] = 0xffffffffu;
+    s_and_or[1] = 0u;
+  }
+  for (int i = threadIdx.x; i < kHistInts / 4; i += kTopkThreads)
+    reinterpret_cast<int4*>(hist)[i] = make_int4(0, 0, 0, 0);
   __syncthreads();
+  all_and = __reduce_and_sync(0xffffffffu, all_and);
+  all_or = __reduce_or_sync(0xffffffffu, all_or);
+  if (lane == 0) {
+    atomicAnd(&s_and_or[0], all_and);
+    atomicOr(&s_and_or[1], all_or);
+  }
+  __syncthreads();
+  const uint32_t diff = s_and_or[0] ^ s_and_or[1];
+  int buf = 0;
+  for (int shift = 0; shift < 32; shift += 8) {
+    if (((diff >> shift) & 255u) == 0u) continue;   // uniform
+    int* h = hist + buf * kHistInts;
+#pragma unroll
+    for (int r = 0; r < E; ++r) {
+      const bool valid = 32 * E * warp + 32 * r + lane < n;
+      // descending order of the key = ascending order of its complement
+      const uint32_t d = ((~(uint32_t)(v[r] >> 32)) >> shift) & 255u;
+      const unsigned peers = digit_peers(__ballot_sync(0xffffffffu, valid), d);
+      const int rank = __popc(peers & lt_mask);
+      int old = 0;
+      if (valid && rank == 0) old = atomicAdd(&h[warp * 256 + d], __popc(peers));
+      old = __shfl_sync(0xffffffffu, old, (__ffs(peers) - 1) & 31);
+      off[r] = old + rank;
+    }
+    __syncthreads();
+    {
+      int tot = 0;
+      if (threadIdx.x < 256) {
+#pragma unroll
+        for (int w = 0; w < kTopkWarps; ++w) tot += h[w * 256 + threadIdx.x];
+      } else {
+        int4* z = reinterpret_cast<int4*>(hist + (buf ^ 1) * kHistInts);
+        for (int i = threadIdx.x - 256; i < kHistInts / 4; i += kTopkThreads - 256)
+          z[i] = make_int4(0, 0, 0, 0);
+      }
+      int all;
+      int run = block_scan(threadIdx.x < 256 ? tot : 0, warp_sums, &all);
+      if (threadIdx.x < 256) {
+#pragma unroll
+        for (int w = 0; w < kTopkWarps; ++w) {
+          const int c = h[w * 256 + threadIdx.x];
+          h[w * 256 + threadIdx.x] = run;
+          run += c;
+        }
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < E; ++r) {
+      if (32 * E * warp + 32 * r + lane < n) {
+        const uint32_t d = ((~(uint32_t)(v[r] >> 32)) >> shift) & 255u;
+        sel[h[warp * 256 + d] + off[r]] = v[r];
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < E; ++r) {
+      const int p = 32 * E * warp + 32 * r + lane;
+      if (p < n) v[r] = sel[p];
+    }
+    buf ^= 1;
+  }
 }
 
 template <typename T>
 __global__ void __launch_bounds__(kTopkThreads, 2) li_topk_kernel(const TopkArgs a) {
-  extern __shared__ __align__(16) uint8_t smem_raw[];
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
   const bool gmem = a.keys_in_gmem != 0;
   uint32_t* keys = reinterpret_cast<uint32_t*>(smem_raw);                       // s2_row
+  // selected pairs: KP + kMaxBucket packed entries (key << 32 | index in the radix path,
+  // key << 32 | ~index in the bucket path)
   unsigned long long* sel = reinterpret_cast<unsigned long long*>(
       smem_raw + (gmem ? 0 : ((a.s2_row * 4 + 15) / 16) * 16));
-  __shared__ int hist[256];
+  __shared__ __align__(16) int hist[2 * kHistInts];
   __shared__ int warp_sums[32];
-  __shared__ int s_digit, s_above;
+  __shared__ int s_digit, s_above, s_t;
+  __shared__ uint32_t s_and_or[2];
+  __shared__ uint32_t s_min[kTopkWarps], s_max[kTopkWarps];
   const int row = blockIdx.x, n2 = blockIdx.y;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   // batch of this query row
   int lo = 0, hi = a.B - 1;
   while (lo < hi) {
@@ -510,17 +586,115 @@ __global__ void __launch_bounds__(kTopkThreads, 2) li_topk_kernel(const TopkArgs
   if (a.q_len_dense <= 0 && s1 >= aq) lim = 0;
   lim = min(lim, a.s2_row);
   const float* src = a.scores + ((size_t)row * a.N2 + n2) * a.s2_row;
-  if (!gmem)
-    for (int i = threadIdx.x; i < lim; i += kTopkThreads) keys[i] = order_key(src[i]);
+  int32_t* oi = a.out_idx + ((size_t)row * a.N2 + n2) * a.K;
+  T* ov = a.out_val ? static_cast<T*>(a.out_val) + ((size_t)row * a.N2 + n2) * a.K : nullptr;
+  // keys into shared memory (when the row fits) and their range
+  uint32_t kmn = 0xffffffffu, kmx = 0u;
+  for (int i = threadIdx.x; i < lim; i += kTopkThreads) {
+    const uint32_t k = order_key(src[i]);
+    if (!gmem) keys[i] = k;
+    kmn = min(kmn, k);
+    kmx = max(kmx, k);
+  }
+  kmn = __reduce_min_sync(0xffffffffu, kmn);
+  kmx = __reduce_max_sync(0xffffffffu, kmx);
+  if (lane == 0) {
+    s_min[warp] = kmn;
+    s_max[warp] = kmx;
+  }
+  if (threadIdx.x == 0) s_t = 0;
   __syncthreads();
+#pragma unroll
+  for (int w = 0; w < kTopkWarps; ++w) {
+    kmn = min(kmn, s_min[w]);
+    kmx = max(kmx, s_max[w]);
+  }
   // order-preserving key of score i: from shared memory, or from the score row (L2) when
   // the row does not fit
   auto key_at = [&](int i) -> uint32_t { return gmem ? order_key(__ldg(src + i)) : keys[i]; };
+
+  // ---- bucket path: finite scores that are not all equal (uniform decision) ----
+  // One histogram of the scores over kBuckets value buckets gives, by a descending scan,
+  // the number of scores above each bucket and the bucket t holding the K-th score.  The
+  // scores of buckets >= t are scattered bucket by bucket (descending), and each finds its
+  // place in its bucket by counting the bucket's entries that order before it by
+  // (score desc, index asc); the first K places are the output.  Exact for any input; a
+  // selected bucket above kMaxBucket entries (clustered scores) takes the radix path.
+  const float xmin = key_float(kmn), xmax = key_float(kmx);
+  bool fast = lim > 0 && kmn > 0x007fffffu && kmx < 0xff800000u && kmx > kmn;
+  const float scale = fast ? (float)kBuckets / (xmax - xmin) : 0.f;
+  fast = fast && scale > 0.f && scale < 3.0e38f;
+  if (fast) {
+    int* cnt = hist;                 // [kBuckets]
+    int* cur = hist + kBuckets;      // [kBuckets]: first place of each bucket, then its end
+    for (int i = threadIdx.x; i < kBuckets / 4; i += kTopkThreads)
+      reinterpret_cast<int4*>(cnt)[i] = make_int4(0, 0, 0, 0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < lim; i += kTopkThreads)
+      atomicAdd(&cnt[value_bucket(key_float(key_at(i)), xmin, scale)], 1);
+    __syncthreads();
+    // descending scan: thread t owns buckets [kBuckets - 8 t - 8, kBuckets - 8 t)
+    constexpr int kPer = kBuckets / kTopkThreads;
+    static_assert(kPer == 8, "two int4 per thread");
+    const int b0 = kBuckets - kPer * (int)threadIdx.x - kPer;
+    const int4 lo4 = reinterpret_cast<const int4*>(cnt + b0)[0];
+    const int4 hi4 = reinterpret_cast<const int4*>(cnt + b0)[1];
+    const int c[kPer] = {hi4.w, hi4.z, hi4.y, hi4.x, lo4.w, lo4.z, lo4.y, lo4.x};   // highest first
+    int sum = 0;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) sum += c[j];
+    int all;
+    int run = block_scan(sum, warp_sums, &all);
+    const int K = a.K;
+    int st[kPer];
+    bool big = false;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      st[j] = run;
+      if (run < K && run + c[j] >= K) s_t = b0 + kPer - 1 - j;   // the bucket of the K-th score
+      big |= run < K && c[j] > kMaxBucket;
+      run += c[j];
+    }
+    reinterpret_cast<int4*>(cur + b0)[0] = make_int4(st[7], st[6], st[5], st[4]);
+    reinterpret_cast<int4*>(cur + b0)[1] = make_int4(st[3], st[2], st[1], st[0]);
+    fast = !__syncthreads_or(big);
+  }
+  if (fast) {
+    int* cnt = hist;
+    int* cur = hist + kBuckets;
+    const int K = a.K;
+    const int t = s_t;
+    for (int i = threadIdx.x; i < lim; i += kTopkThreads) {
+      const uint32_t k = key_at(i);
+      const int bk = value_bucket(key_float(k), xmin, scale);
+      if (bk >= t) sel[atomicAdd(&cur[bk], 1)] = ((unsigned long long)k << 32) | (uint32_t)(~(uint32_t)i);
+    }
+    __syncthreads();
+    const int ntot = cur[t];   // end of bucket t: every scattered entry lies below it
+    for (int q = threadIdx.x; q < ntot; q += kTopkThreads) {
+      const unsigned long long e = sel[q];
+      const int bk = value_bucket(key_float((uint32_t)(e >> 32)), xmin, scale);
+      const int end = cur[bk], start = end - cnt[bk];
+      int place = start;
+      for (int j = start; j < end; ++j) place += sel[j] > e;
+      if (place < K) {
+        oi[place] = (int32_t)(~(uint32_t)(e & 0xffffffffull));
+        if (ov) ov[place] = ElemTraits<T>::from_f(key_float((uint32_t)(e >> 32)));
+      }
+    }
+    for (int j = min(lim, K) + threadIdx.x; j < K; j += kTopkThreads) {
+      oi[j] = -1;
+      if (ov) ov[j] = ElemTraits<T>::from_f(-INFINITY);
+    }
+    return;
+  }
+
+  // ---- radix path: 4-pass radix select, ordered compaction, stable radix sort ----
   const int K = a.K;
   int nsel;
   if (lim <= K) {
     for (int i = threadIdx.x; i < lim; i += kTopkThreads)
-      sel[i] = ((unsigned long long)key_at(i) << 32) | (uint32_t)(~(uint32_t)i);
+      sel[i] = ((unsigned long long)key_at(i) << 32) | (uint32_t)i;
     nsel = lim;
   } else {
     // radix select: after the 4 passes `prefix` is the key of the K-th largest element
@@ -529,15 +703,22 @@ __global__ void __launch_bounds__(kTopkThreads, 2) li_topk_kernel(const TopkArgs
     for (int shift = 24; shift >= 0; shift -= 8) {
       for (int i = threadIdx.x; i < 256; i += kTopkThreads) hist[i] = 0;
       __syncthreads();
-      for (int i = threadIdx.x; i < lim; i += kTopkThreads) {
-        const uint32_t k = key_at(i);
-        if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255], 1);
+      // the lanes of a warp with the same digit add their count once (one atomic per
+      // distinct digit instead of one per key)
+      for (int base = 32 * warp; base < lim; base += kTopkThreads) {
+        const int i = base + lane;
+        const uint32_t k = i < lim ? key_at(i) : 0u;
+        const bool in = i < lim && (k & mask) == prefix;
+        const uint32_t d = (k >> shift) & 255u;
+        const unsigned m = __ballot_sync(0xffffffffu, in);
+        if (m == 0u) continue;   // uniform: no key of this round is still a candidate
+        const unsigned peers = digit_peers(m, d);
+        if (in && (peers & ((1u << lane) - 1u)) == 0u) atomicAdd(&hist[d], __popc(peers));
       }
       __syncthreads();
       if (threadIdx.x < 32) {
         // digit of the `remaining`-th largest key: lane l sums digits 255-8l .. 248-8l, a
         // warp prefix sum over the lanes (highest digits first) finds the lane, then the digit
-        const int lane = threadIdx.x;
         int c[8], sum = 0;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -590,7 +771,7 @@ __global__ void __launch_bounds__(kTopkThreads, 2) li_topk_kernel(const TopkArgs
     int gpos = pge & 0x1fff, epos = pge >> 13;
     for (int i = i0; i < i1; ++i) {
       const uint32_t k = key_at(i);
-      const unsigned long long comp = ((unsigned long long)k << 32) | (uint32_t)(~(uint32_t)i);
+      const unsigned long long comp = ((unsigned long long)k << 32) | (uint32_t)i;
       if (k > thr) {
         sel[gpos++] = comp;
       } else if (k == thr) {
@@ -600,40 +781,20 @@ __global__ void __launch_bounds__(kTopkThreads, 2) li_topk_kernel(const TopkArgs
     }
     nsel = K;
   }
-  for (int i = nsel + threadIdx.x; i < a.KP; i += kTopkThreads) sel[i] = 0ull;
   __syncthreads();
-  // bitonic sort, descending
-  if (a.KP >= kTopkThreads) {
-    switch (a.KP / kTopkThreads) {
-      case 1: bitonic_desc<1>(sel); break;
-      case 2: bitonic_desc<2>(sel); break;
-      case 4: bitonic_desc<4>(sel); break;
-      default: bitonic_desc<8>(sel); break;
-    }
-  } else {
-    for (int size = 2; size <= a.KP; size <<= 1) {
-      for (int stride = size >> 1; stride > 0; stride >>= 1) {
-        for (int i = threadIdx.x; i < a.KP; i += kTopkThreads) {
-          const int j = i ^ stride;
-          if (j > i) {
-            const bool desc = (i & size) == 0;
-            const unsigned long long x = sel[i], y = sel[j];
-            if (desc ? (x < y) : (x > y)) {
-              sel[i] = y;
-              sel[j] = x;
-            }
-          }
-        }
-        __syncthreads();
-      }
-    }
+  // The pairs are in ascending index order within each key (keys above the threshold
+  // first, then the ties at the threshold), so a stable sort by key, descending, orders
+  // them by (score desc, index asc).
+  switch ((a.KP + kTopkThreads - 1) / kTopkThreads) {
+    case 1: radix_sort_desc<1>(sel, nsel, hist, warp_sums, s_and_or); break;
+    case 2: radix_sort_desc<2>(sel, nsel, hist, warp_sums, s_and_or); break;
+    case 4: radix_sort_desc<4>(sel, nsel, hist, warp_sums, s_and_or); break;
+    default: radix_sort_desc<8>(sel, nsel, hist, warp_sums, s_and_or); break;
   }
-  int32_t* oi = a.out_idx + ((size_t)row * a.N2 + n2) * K;
-  T* ov = a.out_val ? static_cast<T*>(a.out_val) + ((size_t)row * a.N2 + n2) * K : nullptr;
   for (int j = threadIdx.x; j < K; j += kTopkThreads) {
     if (j < nsel) {
       const unsigned long long c = sel[j];
-      oi[j] = (int32_t)(~(uint32_t)(c & 0xffffffffull));
+      oi[j] = (int32_t)(uint32_t)(c & 0xffffffffull);
       if (ov) ov[j] = ElemTraits<T>::from_f(key_float((uint32_t)(c >> 32)));
     } else {
       oi[j] = -1;
@@ -729,9 +890,10 @@ int launch(const DsaLiParams* p, cudaStream_t stream) {
   t.q_len_dense = (int)p->q_len_dense;
   // the row's keys stay in shared memory when they fit; longer rows (decode-length key
   // caches) are read from the score matrix in each pass
-  const int64_t tsmem_row = ((int64_t)t.s2_row * 4 + 15) / 16 * 16 + (int64_t)kp * 8;
-  t.keys_in_gmem = tsmem_row > 200 * 1024 ? 1 : 0;
-  const int tsmem = t.keys_in_gmem ? kp * 8 : (int)tsmem_row;
+  const int64_t sel_bytes = (int64_t)(kp + kMaxBucket) * 8;
+  const int64_t tsmem_row = ((int64_t)t.s2_row * 4 + 15) / 16 * 16 + sel_bytes;
+  t.keys_in_gmem = tsmem_row > 190 * 1024 ? 1 : 0;   // plus 34 KB of static shared memory
+  const int tsmem = t.keys_in_gmem ? (int)sel_bytes : (int)tsmem_row;
   // values in the query dtype; fp32 for fp8 queries
   using VT = std::conditional_t<kIsFp8<T>, float, T>;
   if (cudaFuncSetAttribute(li_topk_kernel<VT>, cudaFuncAttributeMaxDynamicSharedMemorySize, tsmem) !=
