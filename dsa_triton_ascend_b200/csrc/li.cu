@@ -5,12 +5,14 @@
 //
 // score[row, n2, s2] = sum_{g in group n2} ReLU(q[row, g] . k[s2, n2]) * w[row, g]   (fp32)
 //
-// Score kernel: one CTA per (batch, block of Tq query tokens, key head n2).  The UMMA
-// computes S^T with the keys as M (128 per tile) and the block's (token, head) pairs as
-// N (Tq * G <= 256 columns), so the head reduction of one key is a row of TMEM owned by
-// one thread: ReLU, weight and sum happen in registers and each thread writes Tq scores.
-// Keys stream through a TMA ring (contiguous rows, no gather); TMEM is double buffered so
-// the epilogue of tile t overlaps the MMAs of tile t+1.  Invisible positions get -inf
+// Score kernel: persistent, one CTA per SM working through items (batch, block of Tq
+// query tokens, key head n2), heaviest first.  The UMMA computes S^T with the keys as M
+// (128 per tile) and the block's (token, head) pairs as N (Tq * G <= 256 columns), so the
+// head reduction of one key is a row of TMEM owned by one thread: ReLU, weight and sum
+// happen in registers and each thread writes Tq scores.  Q blocks arrive by TMA into a
+// double buffer, keys stream through a TMA ring (contiguous rows, no gather); TMEM is
+// double buffered so the epilogue of tile t overlaps the MMAs of tile t+1, also across
+// items.  Invisible positions get -inf
 // (lightning_indexer_triton.py:271-276); tiles past the block's last visible key are
 // never computed (the top-k pass never reads them).
 //
@@ -74,7 +76,8 @@ __device__ __forceinline__ void umma_e4m3(uint32_t d_tmem, uint64_t a_desc, uint
 }
 
 constexpr int kKeys = 128;          // keys per tile (UMMA M)
-constexpr int kThreads = 192;       // 0: TMA, 1: MMA + TMEM, 2-5: epilogue
+constexpr int kEpiWarps = 8;        // two per TMEM lane quarter
+constexpr int kThreads = 64 + 32 * kEpiWarps;   // 0: TMA, 1: MMA + TMEM, 2-9: epilogue
 
 struct Args {
   const void* q;            // [q_rows][N1][D]
@@ -87,6 +90,7 @@ struct Args {
   int* err;
   int B, N1, N2, G, D, Tq, N, nblk, q_rows_max, s2_row, s2_cap, sparse_mode, w_dtype;
   int q_len_dense;          // >0: BSND query, every batch has this many rows
+  int items;                // B * nblk * N2 work items (one block of Tq query tokens, one key head)
   // paged keys (block_table != NULL): position s2 of batch b is pool row
   // block_table[b][s2 / page] * page + s2 % page; a tile of 128 keys is fetched as boxes of
   // box_rows rows (box_rows = min(page, 128), so a box never crosses a block)
@@ -101,7 +105,8 @@ __device__ __forceinline__ float load_w(const void* w, int dtype, size_t i) {
   return __half2float(static_cast<const __half*>(w)[i]);
 }
 
-// Visible keys of query position s1 (lightning_indexer_triton.py:219-227).
+// Visible keys of query position s1 (lightning_indexer_triton.py:219-227); non-decreasing
+// in s1 below aq.
 __device__ __forceinline__ int visible_limit(int s1, int aq, int ak, int s2, int mode) {
   if (s1 >= aq) return 0;
   if (mode == 3) {
@@ -113,29 +118,61 @@ __device__ __forceinline__ int visible_limit(int s1, int aq, int ak, int s2, int
 
 template <int DP>
 struct Cfg {
-  static constexpr int kChunks = DP / 64;
+  static constexpr int kChunks = DP / 64;                   // 128-byte chunks of a row
   static constexpr int kStageBytes = kChunks * kKeys * 128;
   static constexpr int kStages = DP <= 128 ? 3 : 1;
   static constexpr int kQBytes = kChunks * 256 * 128;       // up to 256 (token, head) rows
+  static constexpr int kQBufs = DP <= 128 ? 2 : 1;          // the next item's Q lands early
   static constexpr int kOffQ = 0;
-  static constexpr int kOffK = kQBytes;
-  static constexpr int kOffW = kOffK + kStages * kStageBytes;
-  static constexpr int kOffBars = kOffW + 256 * 4;
+  static constexpr int kOffK = kQBufs * kQBytes;
+  static constexpr int kOffW = kOffK + kStages * kStageBytes;   // 2 x 256 fp32 weights
+  static constexpr int kOffBars = kOffW + 2 * 256 * 4;
 };
 
-struct __align__(16) Bars {
-  uint64_t full[3], empty[3], tfull[2], tfree[2];
+struct __align__(8) Bars {
+  uint64_t full[3], empty[3], tfull[2], tfree[2], qfull[2], qfree[2];
   uint32_t tmem_slot;
-  int lim[256];
-  int qrow[256];
 };
 
+// One work item: Tq query tokens of batch b against key head n2, keys [0, kmax) in
+// ntiles tiles of 128.
+struct Item {
+  int b, n2, s1_0, aq, ak, nrows, qbase, kbase, kmax, ntiles;
+};
+
+// Items run heaviest first (the causal block of the last tokens has the most tiles).
+__device__ __forceinline__ bool decode_item(const Args& a, int i, Item& it) {
+  const int per = a.B * a.N2;
+  const int blk = a.nblk - 1 - i / per;
+  const int rem = i % per;
+  it.b = rem / a.N2;
+  it.n2 = rem % a.N2;
+  it.s1_0 = blk * a.Tq;
+  it.aq = __ldg(a.act_q + it.b);
+  it.ak = __ldg(a.act_k + it.b);
+  it.nrows = a.q_len_dense > 0 ? a.q_len_dense : it.aq;
+  it.qbase = __ldg(a.q_row_base + it.b);
+  it.kbase = a.block_table == nullptr ? __ldg(a.k_row_base + it.b) : 0;
+  // the visible limit grows with the token, so the block's last live token has the most
+  const int hi = min(min(it.s1_0 + a.Tq, it.nrows), it.aq) - 1;
+  it.kmax = hi >= it.s1_0 ? visible_limit(hi, it.aq, it.ak, a.s2_cap, a.sparse_mode) : 0;
+  it.ntiles = (it.kmax + kKeys - 1) / kKeys;
+  return it.ntiles > 0;
+}
+
+// Persistent score kernel, one CTA per SM.  CTA c takes items c, 2G-1-c, 2G+c, ... (G CTAs;
+// the heaviest-first order then spreads the work evenly).  Warp 0 streams each item's Q
+// block (TMA, double buffered so that it lands during the previous item) and its key
+// tiles (3-stage ring); warp 1 issues the UMMAs S^T[key, (token, head)] into one of two
+// 256-column TMEM accumulators; warps 2-9 reduce them: ReLU, weight and sum over each
+// token's heads, one key per thread, two warps per TMEM lane quarter splitting the columns.
 // GF > 0: the head-group size G is the compile-time GF (32, 64 or 128) and N = 256, so
-// every 32-column TMEM load belongs to one token and the epilogue is straight-line code;
-// GF == 0 handles any G.
+// every 32-column TMEM load belongs to one token; GF == 0 handles any G (one warp per
+// quarter does all N columns).
 template <int DP, typename T, int GF>
 __global__ void __launch_bounds__(kThreads, 1)
-    li_score_kernel(const __grid_constant__ CUtensorMap kmap, const Args a) {
+    li_score_kernel(const __grid_constant__ CUtensorMap kmap,
+                    const __grid_constant__ CUtensorMap qmap, const Args a) {
   using C = Cfg<DP>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   Bars& bars = *reinterpret_cast<Bars*>(smem_raw + C::kOffBars);
@@ -147,56 +184,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) report_error(a.err, kErrMisaligned);
     return;
   }
-  const int b = blockIdx.x / a.nblk;
-  const int s1_0 = (blockIdx.x % a.nblk) * a.Tq;
-  const int n2 = blockIdx.y;
-  const int aq = __ldg(a.act_q + b), ak = __ldg(a.act_k + b);
-  const int nrows_b = a.q_len_dense > 0 ? a.q_len_dense : aq;
-  if (s1_0 >= nrows_b) return;   // uniform
-  const int qbase = __ldg(a.q_row_base + b);
-  const int kbase = a.block_table == nullptr ? __ldg(a.k_row_base + b) : 0;
   const int N = a.N, G = a.G, Tq = a.Tq;
-
-  // ---- per token: visible limit and query row; block key range ----
-  int kmax = 0;
-  for (int tq = threadIdx.x; tq < Tq; tq += kThreads) {
-    const int s1 = s1_0 + tq;
-    const bool exists = s1 < nrows_b;
-    const int lim = exists ? visible_limit(s1, aq, ak, a.s2_cap, a.sparse_mode) : 0;
-    bars.lim[tq] = exists ? lim : -1;
-    bars.qrow[tq] = qbase + s1;
-  }
-  // ---- Q block (N rows x DP, zero padded) and weights into smem ----
-  const T* q = static_cast<const T*>(a.q);
-  uint8_t* gQ = smem_raw + C::kOffQ;
-  // 16-byte pieces: 8 elements of 16 bits or 16 of fp8; a 128-byte chunk holds kEpc elements
-  constexpr int kEP = 16 / (int)sizeof(T);
-  constexpr int kPieces = C::kChunks * 8;
-  constexpr int kEpc = 128 / (int)sizeof(T);
-  for (int i = threadIdx.x; i < N * kPieces; i += kThreads) {
-    const int r = i / kPieces, piece = i % kPieces;
-    const int tq = r / G, g = r % G;
-    const int d0 = piece * kEP;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    const int s1 = s1_0 + tq;
-    if (tq < Tq && s1 < nrows_b && d0 < a.D) {
-      const T* src = q + ((size_t)(qbase + s1) * a.N1 + n2 * G + g) * a.D + d0;
-      if (d0 + kEP <= a.D) {
-        v = *reinterpret_cast<const uint4*>(src);
-      } else {
-        T tmp[kEP];
-        for (int e = 0; e < kEP; ++e) tmp[e] = d0 + e < a.D ? src[e] : ElemTraits<T>::from_f(0.f);
-        v = *reinterpret_cast<const uint4*>(tmp);
-      }
-    }
-    *reinterpret_cast<uint4*>(gQ + (piece / 8) * N * 128 + sw128_offset(r, piece % 8)) = v;
-  }
-  for (int r = threadIdx.x; r < N; r += kThreads) {
-    const int tq = r / G, g = r % G, s1 = s1_0 + tq;
-    w_s[r] = (tq < Tq && s1 < nrows_b)
-                 ? load_w(a.w, a.w_dtype, (size_t)(qbase + s1) * a.N1 + n2 * G + g)
-                 : 0.f;
-  }
+  constexpr int kEpc = 128 / (int)sizeof(T);   // elements per 128-byte chunk
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(smem_u32(&bars.full[s]), 1);
@@ -204,7 +193,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(smem_u32(&bars.tfull[s]), 1);
-      mbar_init(smem_u32(&bars.tfree[s]), 4);
+      mbar_init(smem_u32(&bars.tfree[s]), kEpiWarps);
+      mbar_init(smem_u32(&bars.qfull[s]), 1);
+      mbar_init(smem_u32(&bars.qfree[s]), 1);
     }
     fence_mbarrier_init();
   }
@@ -212,56 +203,83 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc<1>(smem_u32(&bars.tmem_slot), 512);
     tmem_relinquish<1>();
   }
-  fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  for (int tq = 0; tq < Tq; ++tq) kmax = max(kmax, bars.lim[tq]);
-  const int ntiles = (kmax + kKeys - 1) / kKeys;
   const uint32_t tmem = bars.tmem_slot;
   bool failed = false;
+  const int ncta = gridDim.x, cta = blockIdx.x;
+  auto item_at = [&](int r) { return r * ncta + ((r & 1) ? ncta - 1 - cta : cta); };
 
   if (warp == 0) {
+    // ---- producer: Q block per item, then its key tiles ----
     if (lane == 0) {
-      for (int t = 0; t < ntiles && !failed; ++t) {
-        const int s = t % C::kStages;
-        if (!mbar_wait(smem_u32(&bars.empty[s]), ((t / C::kStages) & 1) ^ 1, a.err, &failed)) break;
-        const uint32_t fb = smem_u32(&bars.full[s]);
-        mbar_arrive_expect_tx(fb, C::kStageBytes);
-        if (a.block_table == nullptr) {
-          for (int c = 0; c < C::kChunks; ++c)
-            tma_load_3d(sK + s * C::kStageBytes + c * kKeys * 128, &kmap, fb, kEpc * c, n2,
-                        kbase + kKeys * t);
-        } else {
-          for (int r0 = 0; r0 < kKeys; r0 += a.box_rows) {
-            const int tok = kKeys * t + r0;
-            const int pidx = tok / a.page;
-            // no block: a box that lies wholly before the pool, which the TMA unit fills
-            // with zeros (those positions are past the row's visible keys anyway)
-            int prow = -a.box_rows;
-            if (pidx < a.max_blocks) {
-              const int blk = __ldg(a.block_table + (size_t)b * a.max_blocks + pidx);
-              if (blk >= 0) prow = blk * a.page + tok % a.page;
-            }
+      const uint32_t qtx = (uint32_t)(Tq * G * 128 * C::kChunks);
+      int gt = 0, jq = 0;
+      for (int r = 0; !failed; ++r) {
+        const int i = item_at(r);
+        if (i >= a.items) break;
+        Item it;
+        if (!decode_item(a, i, it)) continue;
+        const int qb = jq % C::kQBufs;
+        if (jq >= C::kQBufs &&
+            !mbar_wait(smem_u32(&bars.qfree[qb]), ((jq / C::kQBufs) - 1) & 1, a.err, &failed))
+          break;
+        const uint32_t qf = smem_u32(&bars.qfull[qb]);
+        mbar_arrive_expect_tx(qf, qtx);
+        for (int c = 0; c < C::kChunks; ++c)
+          tma_load_3d(sQ + qb * C::kQBytes + c * N * 128, &qmap, qf, kEpc * c, it.n2 * G,
+                      it.qbase + it.s1_0);
+        for (int t = 0; t < it.ntiles; ++t, ++gt) {
+          const int s = gt % C::kStages;
+          if (!mbar_wait(smem_u32(&bars.empty[s]), ((gt / C::kStages) & 1) ^ 1, a.err, &failed))
+            break;
+          const uint32_t fb = smem_u32(&bars.full[s]);
+          mbar_arrive_expect_tx(fb, C::kStageBytes);
+          if (a.block_table == nullptr) {
             for (int c = 0; c < C::kChunks; ++c)
-              tma_load_3d(sK + s * C::kStageBytes + c * kKeys * 128 + r0 * 128, &kmap, fb, kEpc * c,
-                          n2, prow);
+              tma_load_3d(sK + s * C::kStageBytes + c * kKeys * 128, &kmap, fb, kEpc * c, it.n2,
+                          it.kbase + kKeys * t);
+          } else {
+            for (int r0 = 0; r0 < kKeys; r0 += a.box_rows) {
+              const int tok = kKeys * t + r0;
+              const int pidx = tok / a.page;
+              // no block: a box that lies wholly before the pool, which the TMA unit fills
+              // with zeros (those positions are past the row's visible keys anyway)
+              int prow = -a.box_rows;
+              if (pidx < a.max_blocks) {
+                const int blk = __ldg(a.block_table + (size_t)it.b * a.max_blocks + pidx);
+                if (blk >= 0) prow = blk * a.page + tok % a.page;
+              }
+              for (int c = 0; c < C::kChunks; ++c)
+                tma_load_3d(sK + s * C::kStageBytes + c * kKeys * 128 + r0 * 128, &kmap, fb,
+                            kEpc * c, it.n2, prow);
+            }
           }
         }
+        ++jq;
       }
     }
     __syncwarp();
   } else if (warp == 1) {
-    // The whole warp runs the loop (waits included); one elected lane issues each tcgen05
-    // instruction (a lone lane issues MMAs much more slowly).
-    {
-      const bool bf16 = ElemTraits<T>::kIsBf16;
-      const uint32_t id = idesc_f16(128, N, bf16, false, false);
-      const uint64_t dq = smem_desc_sw128(sQ, 16, 1024);
-      for (int t = 0; t < ntiles && !failed; ++t) {
-        const int s = t % C::kStages, buf = t & 1;
-        if (t >= 2) mbar_wait_spin(smem_u32(&bars.tfree[buf]), ((t >> 1) - 1) & 1, a.err, &failed);
-        mbar_wait_spin(smem_u32(&bars.full[s]), (t / C::kStages) & 1, a.err, &failed);
+    // ---- MMA issuer: the whole warp runs the loop (waits included); one elected lane
+    // issues each tcgen05 instruction (a lone lane issues MMAs much more slowly) ----
+    const bool bf16 = ElemTraits<T>::kIsBf16;
+    const uint32_t id = idesc_f16(128, N, bf16, false, false);
+    int gt = 0, jq = 0;
+    for (int r = 0; !failed; ++r) {
+      const int i = item_at(r);
+      if (i >= a.items) break;
+      Item it;
+      if (!decode_item(a, i, it)) continue;
+      const int qb = jq % C::kQBufs;
+      mbar_wait_spin(smem_u32(&bars.qfull[qb]), (jq / C::kQBufs) & 1, a.err, &failed);
+      if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
+      const uint64_t dq = smem_desc_sw128(sQ + qb * C::kQBytes, 16, 1024);
+      for (int t = 0; t < it.ntiles; ++t, ++gt) {
+        const int s = gt % C::kStages, buf = gt & 1;
+        if (gt >= 2) mbar_wait_spin(smem_u32(&bars.tfree[buf]), ((gt >> 1) - 1) & 1, a.err, &failed);
+        mbar_wait_spin(smem_u32(&bars.full[s]), (gt / C::kStages) & 1, a.err, &failed);
         if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
         tc_fence_after();
         const uint64_t dk = smem_desc_sw128(sK + s * C::kStageBytes, 16, 1024);
@@ -271,105 +289,137 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int u = 0; u < 4; ++u) {   // 32 bytes of K per MMA (16 bf16 / fp16, 32 fp8)
               const uint64_t ka = dk + (uint64_t)((c * kKeys * 128 + u * 32) >> 4);
-              const uint64_t qb = dq + (uint64_t)((c * N * 128 + u * 32) >> 4);
-              if constexpr (kIsFp8<T>) umma_e4m3(tmem + 256 * buf, ka, qb, id, (c | u) != 0);
-              else umma_f16<1>(tmem + 256 * buf, ka, qb, id, (c | u) != 0);
+              const uint64_t qd = dq + (uint64_t)((c * N * 128 + u * 32) >> 4);
+              if constexpr (kIsFp8<T>) umma_e4m3(tmem + 256 * buf, ka, qd, id, (c | u) != 0);
+              else umma_f16<1>(tmem + 256 * buf, ka, qd, id, (c | u) != 0);
             }
           umma_commit(smem_u32(&bars.empty[s]));
           umma_commit(smem_u32(&bars.tfull[buf]));
+          if (t == it.ntiles - 1) umma_commit(smem_u32(&bars.qfree[qb]));
         }
         __syncwarp();
       }
+      ++jq;
     }
     __syncwarp();
   } else {
     // ---- epilogue: one key per thread, ReLU * w summed over each token's G heads ----
-    const int qd = warp & 3;
+    const int e = warp - 2;                 // 0..7
+    const int et = threadIdx.x - 64;        // 0..255: this thread's weight slot
+    const int qd = warp & 3;                // TMEM lane quarter
+    const int half = e >> 2;                // GF > 0: columns [128 half, 128 half + 128)
     const uint32_t lane_addr = (uint32_t)(32 * qd) << 16;
-    for (int t = 0; t < ntiles; ++t) {
-      const int buf = t & 1;
-      mbar_wait(smem_u32(&bars.tfull[buf]), (t >> 1) & 1, a.err, &failed);
-      const bool wfail = __any_sync(0xffffffffu, failed);
-      tc_fence_after();
-      const int key = kKeys * t + 32 * qd + lane;
-      // fp8 keys carry a positive per-key scale: key_scale * sum_g w_g ReLU(q_g . k)
-      float ks = 1.f;
-      if (a.kscale != nullptr && key < kmax) {
-        int krow = -1;
-        if (a.block_table == nullptr) {
-          krow = kbase + key;
-        } else if (key / a.page < a.max_blocks) {
-          const int blk = __ldg(a.block_table + (size_t)b * a.max_blocks + key / a.page);
-          if (blk >= 0) krow = blk * a.page + key % a.page;
-        }
-        ks = krow >= 0 ? __ldg(a.kscale + (size_t)krow * a.N2 + n2) : 0.f;
+    int gt = 0, jq = 0;
+    for (int r = 0;; ++r) {
+      const int i = item_at(r);
+      if (i >= a.items) break;
+      Item it;
+      if (!decode_item(a, i, it)) continue;
+      float* wb = w_s + (jq & 1) * 256;
+      // this item's weights (slot = token * G + head); the buffer was last read for the item
+      // before the previous one, which every epilogue warp finished before the last barrier
+      if (et < N) {
+        const int tq = et / G, g = et % G, s1 = it.s1_0 + tq;
+        wb[et] = (tq < Tq && s1 < it.nrows)
+                     ? load_w(a.w, a.w_dtype, (size_t)(it.qbase + s1) * a.N1 + it.n2 * G + g)
+                     : 0.f;
       }
-      auto emit = [&](int tq, float v) {
-        const int lim = bars.lim[tq];
-        if (lim >= 0 && key < a.s2_row) {
-          float* dst = a.scores + ((size_t)bars.qrow[tq] * a.N2 + n2) * a.s2_row + key;
-          *dst = key < lim ? v * ks : -INFINITY;
+      if (named_bar_or(1, 32 * kEpiWarps, failed)) {
+        failed = true;
+        break;
+      }
+      for (int t = 0; t < it.ntiles; ++t, ++gt) {
+        const int buf = gt & 1;
+        mbar_wait(smem_u32(&bars.tfull[buf]), (gt >> 1) & 1, a.err, &failed);
+        const bool wfail = __any_sync(0xffffffffu, failed);
+        tc_fence_after();
+        const int key = kKeys * t + 32 * qd + lane;
+        // fp8 keys carry a positive per-key scale: key_scale * sum_g w_g ReLU(q_g . k)
+        float ks = 1.f;
+        if (a.kscale != nullptr && key < it.kmax) {
+          int krow = -1;
+          if (a.block_table == nullptr) {
+            krow = it.kbase + key;
+          } else if (key / a.page < a.max_blocks) {
+            const int blk = __ldg(a.block_table + (size_t)it.b * a.max_blocks + key / a.page);
+            if (blk >= 0) krow = blk * a.page + key % a.page;
+          }
+          ks = krow >= 0 ? __ldg(a.kscale + (size_t)krow * a.N2 + it.n2) : 0.f;
         }
-      };
-      if constexpr (GF > 0) {
-        // 256 columns = 256 / GF tokens x GF heads; four independent partial sums per
-        // 32-column load, weights read four at a time (the same for every thread)
-        float acc = 0.f;
-#pragma unroll 1
-        for (int c0 = 0; c0 < 256; c0 += 32) {
-          uint32_t r[32];
+        auto emit = [&](int tq, float v) {
+          const int s1 = it.s1_0 + tq;
+          if (s1 < it.nrows && key < a.s2_row) {
+            const int lim = visible_limit(s1, it.aq, it.ak, a.s2_cap, a.sparse_mode);
+            float* dst = a.scores + ((size_t)(it.qbase + s1) * a.N2 + it.n2) * a.s2_row + key;
+            *dst = key < lim ? v * ks : -INFINITY;
+          }
+        };
+        if constexpr (GF > 0) {
+          // 128 columns per warp in four 32-column loads, the next load in flight while
+          // this one is reduced; four independent partial sums per load
+          const uint32_t tb = tmem + lane_addr + 256 * buf + 128 * half;
+          uint32_t ra[32], rb[32];
+#pragma unroll
+          for (int i2 = 0; i2 < 32; ++i2) ra[i2] = rb[i2] = 0u;
           if (!wfail) {
-            tmem_ld32(tmem + lane_addr + 256 * buf + c0, r);
-            tmem_ld_wait();
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = 0u;
+            tmem_ld32(tb, ra);
+            tmem_ld_wait_regs(ra);
           }
-          const float4* w4 = reinterpret_cast<const float4*>(w_s + c0);
-          float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
+          float acc = 0.f;
 #pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            const float4 w = w4[i / 4];
-            p0 = fmaf(fmaxf(__uint_as_float(r[i]), 0.f), w.x, p0);
-            p1 = fmaf(fmaxf(__uint_as_float(r[i + 1]), 0.f), w.y, p1);
-            p2 = fmaf(fmaxf(__uint_as_float(r[i + 2]), 0.f), w.z, p2);
-            p3 = fmaf(fmaxf(__uint_as_float(r[i + 3]), 0.f), w.w, p3);
-          }
-          acc += (p0 + p1) + (p2 + p3);
-          if ((c0 + 32) % GF == 0) {
-            emit(c0 / GF, acc);
-            acc = 0.f;
-          }
-        }
-      } else {
-        int tok = 0, gcount = 0;
-        float acc = 0.f;
-        for (int c0 = 0; c0 < N; c0 += 32) {
-          uint32_t r[32];
-          if (!wfail) {
-            tmem_ld32(tmem + lane_addr + 256 * buf + c0, r);
-            tmem_ld_wait();
-          } else {
+          for (int cc = 0; cc < 4; ++cc) {
+            uint32_t(&cur)[32] = (cc & 1) ? rb : ra;
+            uint32_t(&nxt)[32] = (cc & 1) ? ra : rb;
+            if (cc + 1 < 4 && !wfail) tmem_ld32(tb + 32 * (cc + 1), nxt);
+            const int c0 = 128 * half + 32 * cc;
+            const float4* w4 = reinterpret_cast<const float4*>(wb + c0);
+            float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = 0u;
+            for (int i2 = 0; i2 < 32; i2 += 4) {
+              const float4 w = w4[i2 / 4];
+              p0 = fmaf(fmaxf(__uint_as_float(cur[i2]), 0.f), w.x, p0);
+              p1 = fmaf(fmaxf(__uint_as_float(cur[i2 + 1]), 0.f), w.y, p1);
+              p2 = fmaf(fmaxf(__uint_as_float(cur[i2 + 2]), 0.f), w.z, p2);
+              p3 = fmaf(fmaxf(__uint_as_float(cur[i2 + 3]), 0.f), w.w, p3);
+            }
+            acc += (p0 + p1) + (p2 + p3);
+            if ((c0 + 32) % GF == 0) {
+              emit(c0 / GF, acc);
+              acc = 0.f;
+            }
+            if (cc + 1 < 4 && !wfail) tmem_ld_wait_regs(nxt);
           }
+        } else if (half == 0) {
+          int tok = 0, gcount = 0;
+          float acc = 0.f;
+          for (int c0 = 0; c0 < N; c0 += 32) {
+            uint32_t rr[32];
+            if (!wfail) {
+              tmem_ld32(tmem + lane_addr + 256 * buf + c0, rr);
+              tmem_ld_wait();
+            } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            if (tok < Tq) {
-              acc = fmaf(fmaxf(__uint_as_float(r[i]), 0.f), w_s[c0 + i], acc);
-              if (++gcount == G) {
-                emit(tok, acc);
-                ++tok;
-                gcount = 0;
-                acc = 0.f;
+              for (int i2 = 0; i2 < 32; ++i2) rr[i2] = 0u;
+            }
+#pragma unroll
+            for (int i2 = 0; i2 < 32; ++i2) {
+              if (tok < Tq) {
+                acc = fmaf(fmaxf(__uint_as_float(rr[i2]), 0.f), wb[c0 + i2], acc);
+                if (++gcount == G) {
+                  emit(tok, acc);
+                  ++tok;
+                  gcount = 0;
+                  acc = 0.f;
+                }
               }
             }
           }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&bars.tfree[buf]));
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&bars.tfree[buf]));
+      ++jq;
     }
   }
   tc_fence_before();
@@ -803,16 +853,32 @@ __global__ void __launch_bounds__(kTopkThreads, 2) li_topk_kernel(const TopkArgs
   }
 }
 
+// SMs of the current device (persistent grid), cached per device
+inline int sm_count() {
+  static int cached[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1)
+      n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
 template <int DP, typename T, int GF>
-int launch_score(const CUtensorMap& kmap, const Args& a, int64_t batch, int64_t n2,
+int launch_score(const CUtensorMap& kmap, const CUtensorMap& qmap, const Args& a,
                  cudaStream_t stream) {
   using C = Cfg<DP>;
   auto k = li_score_kernel<DP, T, GF>;
   const int smem = C::kOffBars + (int)sizeof(Bars);
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return DSA_ERR_CUDA;
-  if (a.nblk > 0)
-    k<<<dim3((unsigned)(batch * a.nblk), (unsigned)n2), dim3(kThreads), smem, stream>>>(kmap, a);
+  if (a.items > 0) {
+    const int grid = a.items < sm_count() ? a.items : sm_count();
+    k<<<dim3((unsigned)grid), dim3(kThreads), smem, stream>>>(kmap, qmap, a);
+  }
   return DSA_OK;
 }
 
@@ -834,6 +900,15 @@ int launch(const DsaLiParams* p, cudaStream_t stream) {
                 : make_tmap_3d_16b(&kmap, p->key, bf16, p->d, p->n2, p->kv_rows, p->d * esz,
                                    (uint64_t)p->n2 * p->d * esz, 64, 1, box_rows);
   if (!mapped) return DSA_ERR_TMA_DESCRIPTOR;
+  // query viewed as {D, N1, q_rows}; box {one 128-byte chunk, G heads, Tq tokens}: the
+  // (token, head) rows of one item in one load per chunk
+  CUtensorMap qmap;
+  const bool qmapped =
+      kIsFp8<T> ? make_tmap_3d_8b(&qmap, p->query, p->d, p->n1, p->q_rows, (uint64_t)p->d,
+                                  (uint64_t)p->n1 * p->d, 128, (uint32_t)G, (uint32_t)Tq)
+                : make_tmap_3d_16b(&qmap, p->query, bf16, p->d, p->n1, p->q_rows, p->d * esz,
+                                   (uint64_t)p->n1 * p->d * esz, 64, (uint32_t)G, (uint32_t)Tq);
+  if (!qmapped) return DSA_ERR_TMA_DESCRIPTOR;
   Args a;
   a.q = p->query;
   a.w = p->weights;
@@ -852,6 +927,9 @@ int launch(const DsaLiParams* p, cudaStream_t stream) {
   a.N = N;
   a.q_rows_max = (int)p->q_len_max;
   a.nblk = (int)((p->q_len_max + Tq - 1) / Tq);
+  const int64_t items = (int64_t)p->batch * a.nblk * p->n2;
+  if (items > INT32_MAX) return DSA_ERR_INVALID_ARG;
+  a.items = (int)items;
   a.s2_row = (int)p->s2_row;
   a.s2_cap = (int)p->s2_cap;
   a.sparse_mode = p->sparse_mode;
@@ -863,10 +941,10 @@ int launch(const DsaLiParams* p, cudaStream_t stream) {
   a.box_rows = box_rows;
   a.kscale = kIsFp8<T> ? p->key_scale : nullptr;
   int rc;
-  if (N == 256 && G == 64) rc = launch_score<DP, T, 64>(kmap, a, p->batch, p->n2, stream);
-  else if (N == 256 && G == 32) rc = launch_score<DP, T, 32>(kmap, a, p->batch, p->n2, stream);
-  else if (N == 256 && G == 128) rc = launch_score<DP, T, 128>(kmap, a, p->batch, p->n2, stream);
-  else rc = launch_score<DP, T, 0>(kmap, a, p->batch, p->n2, stream);
+  if (N == 256 && G == 64) rc = launch_score<DP, T, 64>(kmap, qmap, a, stream);
+  else if (N == 256 && G == 32) rc = launch_score<DP, T, 32>(kmap, qmap, a, stream);
+  else if (N == 256 && G == 128) rc = launch_score<DP, T, 128>(kmap, qmap, a, stream);
+  else rc = launch_score<DP, T, 0>(kmap, qmap, a, stream);
   if (rc != DSA_OK) return rc;
 
   TopkArgs t;
