@@ -232,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       it.qbase + it.s1_0);
         for (int t = 0; t < it.ntiles; ++t, ++gt) {
           const int s = gt % C::kStages;
-          if (!mbar_wait(smem_u32(&bars.empty[s]), ((gt / C::kStages) & 1) ^ 1, a.err, &failed))
+          if (!mbar_wait_spin(smem_u32(&bars.empty[s]), ((gt / C::kStages) & 1) ^ 1, a.err, &failed))
             break;
           const uint32_t fb = smem_u32(&bars.full[s]);
           mbar_arrive_expect_tx(fb, C::kStageBytes);
@@ -330,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       for (int t = 0; t < it.ntiles; ++t, ++gt) {
         const int buf = gt & 1;
-        mbar_wait(smem_u32(&bars.tfull[buf]), (gt >> 1) & 1, a.err, &failed);
+        mbar_wait_spin(smem_u32(&bars.tfull[buf]), (gt >> 1) & 1, a.err, &failed);
         const bool wfail = __any_sync(0xffffffffu, failed);
         tc_fence_after();
         const int key = kKeys * t + 32 * qd + lane;
