@@ -50,7 +50,7 @@ FWD_DRAM_BYTES_PER_PAIR = (49.38 + 2.23) * 1e6 / PROFILE_PAIRS
 # DRAM traffic of one call of each secondary workload at the size bench.py runs, from one ncu
 # capture of the library's kernels (profiles/secondary_workloads_traffic.md)
 WORKLOAD_DRAM_BYTES = {
-    "li": (138.45 + 39.17 + 67.69 + 47.88) * 1e6,            # score + top-k
+    "li": (138.45 + 52.63 + 67.75 + 49.59) * 1e6,            # score + top-k (profiles/li_score_topk_config2.md)
     "decode": (0.33 + 84.43 + 0.10 + 16.92) * 1e6,           # prep + forward + combine
     "sli": (1284.81 + 58.37 + 260.75 + 109.38 + 4.20) * 1e6,  # teacher + index + cast
 }
