@@ -18,21 +18,27 @@ struct RowInfo {
   bool active;
 };
 
+// Row information once the row's batch b is known.
+template <class A>
+__device__ __forceinline__ RowInfo row_info_in(const A& a, int row, int b) {
+  RowInfo ri;
+  ri.b = b;
+  ri.s1 = row - __ldg(a.q_row_base + b);
+  ri.aq = __ldg(a.act_q + b);
+  ri.ak = __ldg(a.act_k + b);
+  ri.threshold = a.sparse_mode == 0 ? ri.ak : ri.ak - ri.aq + ri.s1 + 1;
+  ri.active = ri.s1 < ri.aq && ri.threshold > 0;
+  return ri;
+}
+
 template <class A>
 __device__ __forceinline__ RowInfo row_info(const A& a, int row) {
-  RowInfo ri;
   int lo = 0, hi = a.B - 1;
   while (lo < hi) {  // last batch whose first row <= row
     int mid = (lo + hi + 1) >> 1;
     if (__ldg(a.q_row_base + mid) <= row) lo = mid; else hi = mid - 1;
   }
-  ri.b = lo;
-  ri.s1 = row - __ldg(a.q_row_base + lo);
-  ri.aq = __ldg(a.act_q + lo);
-  ri.ak = __ldg(a.act_k + lo);
-  ri.threshold = a.sparse_mode == 0 ? ri.ak : ri.ak - ri.aq + ri.s1 + 1;
-  ri.active = ri.s1 < ri.aq && ri.threshold > 0;
-  return ri;
+  return row_info_in(a, row, lo);
 }
 
 // Entry j of the (block-expanded) index row -> key position, or -1 if masked.
@@ -102,52 +108,70 @@ __global__ void __launch_bounds__(128) sfa_prep_kernel(const A a, int32_t* ws_ro
 
 // The same compaction with one 512-thread block per query row, for calls with few rows
 // (decode): the warp-per-row kernel would walk a 2048-entry row in 64 dependent steps
-// (index, then page table) on a handful of SMs.  Two passes over the row: count the valid
-// entries of each warp's segment, then write them at the warp's offset, in index order.
+// (index, then page table) on a handful of SMs.  The block finds the row's batch with one
+// parallel look at the row-base table (no dependent search), then each thread resolves
+// kPrepPer consecutive entries at once (their loads in flight together) and one block
+// scan of the per-thread counts places them in index order; rows longer than
+// 512 * kPrepPer entries take several such rounds.
 constexpr int kPrepBlockThreads = 512;
+constexpr int kPrepPer = 8;
 
 template <class A>
-__global__ void __launch_bounds__(kPrepBlockThreads) sfa_prep_block_kernel(const A a, int32_t* ws_rows,
+__global__ void __launch_bounds__(kPrepBlockThreads, 1) sfa_prep_block_kernel(const A a, int32_t* ws_rows,
                                                                            int32_t* ws_count) {
-  __shared__ int cnt[kPrepBlockThreads / 32];
+  constexpr int kWarps = kPrepBlockThreads / 32;
+  __shared__ int warp_sums[kWarps];
+  __shared__ int s_batch;
   const int row = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const RowInfo ri = row_info(a, row);
-  const int nent = a.topk * a.block;
-  constexpr int kWarps = kPrepBlockThreads / 32;
-  const int seg = ((nent + kPrepBlockThreads - 1) / kPrepBlockThreads) * 32;   // per warp
-  const int j0 = warp * seg, j1 = min(nent, j0 + seg);
-  const int32_t* row_idx = a.idx + (size_t)row * a.topk;
-  int have = 0;
-  if (ri.active) {
-#pragma unroll 4
-    for (int base = j0; base < j1; base += 32) {
-      const int j = base + lane;
-      const int kp = j < j1 ? key_at(a, ri, row_idx, j) : -1;
-      have += __popc(__ballot_sync(0xffffffffu, kp >= 0));
-    }
-  }
-  if (lane == 0) cnt[warp] = have;
+  if (threadIdx.x == 0) s_batch = 0;
   __syncthreads();
-  int off = 0, total = 0;
+  // the last batch whose first row <= row: the one with base <= row < next base
+  for (int b = threadIdx.x; b < a.B; b += kPrepBlockThreads) {
+    const int base = __ldg(a.q_row_base + b);
+    const int next = b + 1 < a.B ? __ldg(a.q_row_base + b + 1) : 0x7fffffff;
+    if (base <= row && row < next) s_batch = b;
+  }
+  __syncthreads();
+  const RowInfo ri = row_info_in(a, row, s_batch);
+  const int nent = ri.active ? a.topk * a.block : 0;
+  const int32_t* row_idx = a.idx + (size_t)row * a.topk;
+  int32_t* out = ws_rows + (size_t)row * a.topk * a.block;
+  int done = 0;   // entries written by the previous rounds (uniform)
+  for (int r0 = 0; r0 < nent; r0 += kPrepBlockThreads * kPrepPer) {
+    const int j0 = r0 + threadIdx.x * kPrepPer;
+    int kr[kPrepPer];
+    int have = 0;
 #pragma unroll
-  for (int w = 0; w < kWarps; ++w) {
-    off += w < warp ? cnt[w] : 0;
-    total += cnt[w];
-  }
-  if (ri.active) {
-    int32_t* out = ws_rows + (size_t)row * nent + off;
-    int done = 0;
-#pragma unroll 4
-    for (int base = j0; base < j1; base += 32) {
-      const int j = base + lane;
-      const int kp = j < j1 ? key_at(a, ri, row_idx, j) : -1;
-      const unsigned m = __ballot_sync(0xffffffffu, kp >= 0);
-      if (kp >= 0) out[done + __popc(m & ((1u << lane) - 1u))] = key_row(a, ri.b, kp);
-      done += __popc(m);
+    for (int e = 0; e < kPrepPer; ++e) {
+      const int kp = j0 + e < nent ? key_at(a, ri, row_idx, j0 + e) : -1;
+      kr[e] = kp >= 0 ? key_row(a, ri.b, kp) : -1;
+      have += kp >= 0;
     }
+    // block exclusive scan of `have` (thread order = entry order)
+    int x = have;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    int before = 0, total = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const int v = warp_sums[w];
+      before += w < warp ? v : 0;
+      total += v;
+    }
+    int pos = done + before + x - have;
+#pragma unroll
+    for (int e = 0; e < kPrepPer; ++e)
+      if (kr[e] >= 0) out[pos++] = kr[e];
+    done += total;
+    __syncthreads();   // warp_sums is rewritten by the next round
   }
-  if (threadIdx.x == 0) ws_count[row] = ri.active ? total : 0;
+  if (threadIdx.x == 0) ws_count[row] = done;
 }
 
 // Compaction pre-pass for `num_rows` rows: one block per row when there are few rows,
