@@ -316,6 +316,36 @@ def main():
     value = flops_total / (ms_step * 1e-3) / 1e12
     tokens_per_s = S1 / (ms_step * 1e-3)
 
+    # ---- the same step with the merged key gradient (key == value, as autograd uses it):
+    # dK + dV in one fp32 accumulator, one all-reduce of [dkv | dkr]; an extra field, the
+    # headline above is the 5-output operator ----
+    def bwd_merged(out, mx, sm):
+        _, finish = dsa.sparse_flash_attention_grad_partial(
+            q, k, k, si, dout, out, mx, sm, scale, query_rope=qr, key_rope=kr,
+            actual_seq_lengths_query=aq, sparse_mode=3, merge_key_grads=True)
+        if world > 1:
+            dist.all_reduce(finish.key_grad_buffer)
+        return finish()
+
+    m_steps = max(2, min(args.steps, 5))
+    out_m, mx_m, sm_m = fwd()
+    for _ in range(2):
+        bwd_merged(out_m, mx_m, sm_m)
+    ev_m = [mk() for _ in range(m_steps)]
+    barrier()
+    torch.cuda.synchronize(dev)
+    for a_, b_ in ev_m:
+        a_.record(stream)
+        bwd_merged(out_m, mx_m, sm_m)
+        b_.record(stream)
+    torch.cuda.synchronize(dev)
+    dsa.check_device_errors(dev)
+    tm = torch.tensor([float(np.mean([a_.elapsed_time(b_) for a_, b_ in ev_m]))], device=dev)
+    if world > 1:
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+    bwd_merged_ms = float(tm.item())
+    del out_m, mx_m, sm_m
+
     # ---- end to end through the public API with host buffers (pinned) ----
     # Inputs in pinned host memory; the public streaming entry point copies them in, runs
     # the forward and backward in row chunks and copies every result out, with the copies
@@ -407,6 +437,14 @@ def main():
                             "bytes_per_step": my_pairs * BWD_SCATTER_BYTES_PER_PAIR,
                             "target": "fp32 key-gradient accumulators, L2-resident",
                             "gbs_over_bwd": my_pairs * BWD_SCATTER_BYTES_PER_PAIR / ((bwd_ms - ar_ms) * 1e-3) / 1e9},
+            "merged_key_grad": {
+                "bwd_ms": bwd_merged_ms,
+                "step_ms": fwd_ms + bwd_merged_ms,
+                "value": flops_total / ((fwd_ms + bwd_merged_ms) * 1e-3) / 1e12,
+                "unit": "TFLOP/s",
+                "scatter_bytes_per_pair": 4 * (D + DR),
+                "note": "key == value (MLA): dK + dV accumulated as one (the autograd path); "
+                        "forward time from the headline run, backward timed separately"},
             "ranks": [{"rank": i, "step_ms": r[0], "fwd_ms": r[1], "bwd_ms": r[2],
                        "allreduce_ms": r[3], "pairs": int(r[4])} for i, r in enumerate(per_rank)],
             "step_ms_max_min": [max(r[0] for r in per_rank), min(r[0] for r in per_rank)],

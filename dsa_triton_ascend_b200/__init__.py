@@ -33,6 +33,7 @@ from .sparse_lightning_indexer_grad_kl_loss import (  # noqa: F401
 )
 from .sparse_flash_attention_grad import (  # noqa: F401
     SparseFlashAttentionGradTriton,
+    sparse_flash_attention_grad_merged,
     sparse_flash_attention_grad_partial,
     sparse_flash_attention_grad_triton,
 )

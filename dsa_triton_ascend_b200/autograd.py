@@ -21,7 +21,7 @@ import torch
 
 from .lightning_indexer import lightning_indexer_triton
 from .sparse_flash_attention import sparse_flash_attention_triton
-from .sparse_flash_attention_grad import sparse_flash_attention_grad_triton
+from .sparse_flash_attention_grad import sparse_flash_attention_grad_merged
 from .sparse_lightning_indexer_grad_kl_loss import sparse_lightning_indexer_grad_kl_loss_triton
 
 
@@ -52,11 +52,12 @@ class SparseFlashAttentionFunction(torch.autograd.Function):
     def backward(ctx, d_out, _d_smax, _d_ssum):
         query, key, query_rope, key_rope, sparse_indices, out, smax, ssum = ctx.saved_tensors
         scale, mode, aq, ak, block, layout = ctx.cfg
-        dq, dk, dv, dqr, dkr = sparse_flash_attention_grad_triton(
-            query, key, key, sparse_indices, d_out.contiguous(), out, smax, ssum, scale,
+        # key == value: the merged kernels accumulate dK + dV directly
+        dq, dkv, dqr, dkr = sparse_flash_attention_grad_merged(
+            query, key, sparse_indices, d_out.contiguous(), out, smax, ssum, scale,
             query_rope=query_rope, key_rope=key_rope, actual_seq_lengths_query=aq,
             actual_seq_lengths_kv=ak, sparse_block_size=block, layout=layout, sparse_mode=mode)
-        return dq, dk + dv, dqr, dkr, None, None, None, None, None, None, None
+        return dq, dkv, dqr, dkr, None, None, None, None, None, None, None
 
 
 class IndexerKLLossFunction(torch.autograd.Function):

@@ -608,6 +608,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
 // form runs at the L2 reduction ceiling, and no shared-memory transpose is needed.
 // The reductions are the bound (4352 bytes per valid pair at D = 512).
 //
+// Merged key gradient (dv_acc == NULL): key and value are one tensor (MLA), so the caller
+// wants dK + dV only.  A merged part takes both slots, the Q slice and the dO slice of its
+// columns, and each tile runs dS^T Q and then P^T dO into the same TMEM accumulator (two
+// B-ring entries: the dS tile, then the P tile).  Parts per row: D / 256 merged + the
+// rope part; the reductions drop to 4 (D + 64) bytes per valid pair.
+//
 // Roles: warp 0 (one lane) loads the item slices into two slots and the dS / P tiles
 // through a 3-stage ring, so the next item's slice arrives while the current item's last
 // tiles run; warp 1 (one lane) issues the MMAs into two TMEM buffers; warps 2-17 drain
@@ -647,14 +653,33 @@ struct Item3 {
 };
 
 template <int D>
-__device__ __forceinline__ Item3 item3(const Args& a, int it) {
+__device__ __forceinline__ Item3 item3(const Args& a, int it, int nparts) {
   Item3 x;
-  x.row = it / Cfg3<D>::kParts;
-  x.part = it % Cfg3<D>::kParts;
+  x.row = it / nparts;
+  x.part = it % nparts;
   const RowInfo ri = row_info(a, x.row);
   x.nvalid = ri.active ? __ldg(a.ws_count + x.row) : 0;
   x.ntiles = (x.nvalid + kKeyTile3 - 1) / kKeyTile3;
   return x;
+}
+
+// What a part computes: rope (dKr: Qr and dS), dK (Q, dS), dV (dO, P) or, merged, dK + dV
+// of its columns (Q and dS, then dO and P).
+struct Part3 {
+  bool rope, is_dv, mixed;
+  int col0, nbox;
+};
+
+template <int D>
+__device__ __forceinline__ Part3 part3(int part, bool merged) {
+  using C = Cfg3<D>;
+  Part3 k;
+  k.rope = part == (merged ? C::kDParts : 2 * C::kDParts);
+  k.mixed = merged && !k.rope;
+  k.is_dv = !merged && !k.rope && part >= C::kDParts;
+  k.col0 = k.rope ? 0 : (part % C::kDParts) * C::kW;
+  k.nbox = k.rope ? 1 : C::kW / 64;
+  return k;
 }
 
 // One drain warp's share of a finished tile: NK keys (TMEM columns) x 32 output columns
@@ -719,7 +744,9 @@ __global__ void __launch_bounds__(kThreads3, 1)
   }
   // uniform across the CTA: an error flagged by an earlier kernel skips the work
   const bool abort = a.err != nullptr && *reinterpret_cast<volatile int*>(a.err) != 0;
-  const int nitems = abort ? 0 : a.num_rows * C::kParts;
+  const bool merged = a.dv_acc == nullptr;
+  const int nparts = merged ? C::kDParts + 1 : C::kParts;
+  const int nitems = abort ? 0 : a.num_rows * nparts;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2; ++s) {
@@ -747,43 +774,48 @@ __global__ void __launch_bounds__(kThreads3, 1)
   if (warp == 0) {
     // ---- TMA: item slices (2 slots), dS / P tiles (ring) ----
     if (lane == 0) {
-      int na = 0, nb = 0;
+      int ua0 = 0, ua1 = 0, nb = 0, ni = 0;   // loads per A slot, B entries, non-empty items
       for (int it = blockIdx.x; it < nitems && !failed; it += gridDim.x) {
-        const Item3 x = item3<D>(a, it);
+        const Item3 x = item3<D>(a, it, nparts);
         if (x.ntiles == 0) continue;
-        const bool rope = x.part == 2 * C::kDParts;
-        const bool is_dv = !rope && x.part >= C::kDParts;
-        const CUtensorMap* am = rope ? &maps.qr : is_dv ? &maps.dout : &maps.q;
-        const CUtensorMap* bm = is_dv ? &maps.pp : &maps.ds;
-        const int col0 = rope ? 0 : (x.part % C::kDParts) * C::kW;
-        const int nbox = rope ? 1 : C::kW / 64;
-        {
-          const int ab = na & 1;
-          if (!mbar_wait_sleep(smem_u32(&bars.a_empty[ab]), ((na >> 1) & 1) ^ 1, a.err, &failed)) break;
-          const uint32_t fb = smem_u32(&bars.a_full[ab]);
-          mbar_arrive_expect_tx(fb, nbox * C::kBox);
-          for (int c = 0; c < nbox; ++c)
-            tma_load_2d(sA + ab * C::kSlice + c * C::kBox, am, fb, col0 + 64 * c, x.row * a.N1);
-          ++na;
-        }
-        const int krow0 = x.row * a.kp;   // first scratch row (key slot) of this query row
-        for (int t = 0; t < x.ntiles; ++t) {
-          const int s = nb % kStages3;
-          if (!mbar_wait_sleep(smem_u32(&bars.b_empty[s]), ((nb / kStages3) & 1) ^ 1, a.err, &failed))
+        const Part3 pk = part3<D>(x.part, merged);
+        // slots: a merged part fills both (Q, dO); otherwise one, alternating per item
+        const int nsl = pk.mixed ? 2 : 1;
+        for (int h = 0; h < nsl; ++h) {
+          const int ab = pk.mixed ? h : (merged ? 0 : (ni & 1));
+          const CUtensorMap* am = pk.rope ? &maps.qr
+                                  : (pk.is_dv || (pk.mixed && h == 1)) ? &maps.dout : &maps.q;
+          if (!mbar_wait_sleep(smem_u32(&bars.a_empty[ab]), ((ab ? ua1 : ua0) & 1) ^ 1, a.err, &failed))
             break;
-          const uint32_t fb = smem_u32(&bars.b_full[s]);
-          mbar_arrive_expect_tx(fb, C::kTileB);
-          for (int c = 0; c < 2; ++c)   // heads [64c, 64c+64) of the tile's 128 keys
-            tma_load_2d(sB + s * C::kTileB + c * kKeyTile3 * 128, bm, fb, 64 * c,
-                        krow0 + t * kKeyTile3);
-          ++nb;
+          const uint32_t fb = smem_u32(&bars.a_full[ab]);
+          mbar_arrive_expect_tx(fb, pk.nbox * C::kBox);
+          for (int c = 0; c < pk.nbox; ++c)
+            tma_load_2d(sA + ab * C::kSlice + c * C::kBox, am, fb, pk.col0 + 64 * c, x.row * a.N1);
+          if (ab) ++ua1; else ++ua0;
         }
+        if (failed) break;
+        const int krow0 = x.row * a.kp;   // first scratch row (key slot) of this query row
+        for (int t = 0; t < x.ntiles && !failed; ++t) {
+          for (int e = 0; e < nsl; ++e) {   // the tile's dS entry, then (merged) its P entry
+            const CUtensorMap* bm = (pk.is_dv || e == 1) ? &maps.pp : &maps.ds;
+            const int s = nb % kStages3;
+            if (!mbar_wait_sleep(smem_u32(&bars.b_empty[s]), ((nb / kStages3) & 1) ^ 1, a.err, &failed))
+              break;
+            const uint32_t fb = smem_u32(&bars.b_full[s]);
+            mbar_arrive_expect_tx(fb, C::kTileB);
+            for (int c = 0; c < 2; ++c)   // heads [64c, 64c+64) of the tile's 128 keys
+              tma_load_2d(sB + s * C::kTileB + c * kKeyTile3 * 128, bm, fb, 64 * c,
+                          krow0 + t * kKeyTile3);
+            ++nb;
+          }
+        }
+        ++ni;
       }
       // on a failure, let the copies already issued land before the exit
       if (failed) {
         bool f2 = false;
-        for (int i = na > 2 ? na - 2 : 0; i < na; ++i)
-          mbar_wait(smem_u32(&bars.a_full[i & 1]), (i >> 1) & 1, a.err, &f2);
+        if (ua0 > 0) mbar_wait(smem_u32(&bars.a_full[0]), (ua0 - 1) & 1, a.err, &f2);
+        if (ua1 > 0) mbar_wait(smem_u32(&bars.a_full[1]), (ua1 - 1) & 1, a.err, &f2);
         for (int i = nb > kStages3 ? nb - kStages3 : 0; i < nb; ++i)
           mbar_wait(smem_u32(&bars.b_full[i % kStages3]), (i / kStages3) & 1, a.err, &f2);
       }
@@ -796,44 +828,56 @@ __global__ void __launch_bounds__(kThreads3, 1)
     {
       const bool bf16 = ElemTraits<T>::kIsBf16;
       const uint32_t id = idesc_f16(128, kKeyTile3, bf16, true, false);
-      int na = 0, nb = 0, nt = 0;
+      int ua0 = 0, ua1 = 0, nb = 0, nt = 0, ni = 0;   // uses per A slot, B entries, tiles, items
       for (int it = blockIdx.x; it < nitems && !failed; it += gridDim.x) {
-        const Item3 x = item3<D>(a, it);
+        const Item3 x = item3<D>(a, it, nparts);
         if (x.ntiles == 0) continue;
-        const bool rope = x.part == 2 * C::kDParts;
-        const int nblk = rope ? 1 : C::kW / 128;
-        const int ab = na & 1;
-        mbar_wait_spin(smem_u32(&bars.a_full[ab]), (na >> 1) & 1, a.err, &failed);
+        const Part3 pk = part3<D>(x.part, merged);
+        const int nblk = pk.rope ? 1 : C::kW / 128;
+        const int nsl = pk.mixed ? 2 : 1;
+        const int ab1 = merged ? 0 : (ni & 1);   // the slot of a single-slot part
+        for (int h = 0; h < nsl; ++h) {
+          const int ab = pk.mixed ? h : ab1;
+          mbar_wait_spin(smem_u32(&bars.a_full[ab]), (ab ? ua1 : ua0) & 1, a.err, &failed);
+        }
         if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
         for (int t = 0; t < x.ntiles; ++t) {
-          const int s = nb % kStages3, tb = nt & 1;
-          mbar_wait_spin(smem_u32(&bars.b_full[s]), (nb / kStages3) & 1, a.err, &failed);
+          const int tb = nt & 1;
           mbar_wait_spin(smem_u32(&bars.t_empty[tb]), ((nt >> 1) & 1) ^ 1, a.err, &failed);
-          if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
-          tc_fence_after();
-          const uint64_t db = smem_desc_sw128(sB + s * C::kTileB, 16, 1024);
-          if (elect_one()) {
-            for (int m = 0; m < nblk; ++m) {
-              // A: columns [128m, 128m+128) = two 64-column boxes (lbo = box stride); the
-              // rope part has one box, and lanes 64-127 of its result are never read
-              const uint64_t da = smem_desc_sw128(sA + ab * C::kSlice + 2 * m * C::kBox, C::kBox, 1024);
+          for (int e = 0; e < nsl; ++e) {
+            const int s = nb % kStages3;
+            const int ab = pk.mixed ? e : ab1;
+            mbar_wait_spin(smem_u32(&bars.b_full[s]), (nb / kStages3) & 1, a.err, &failed);
+            if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
+            tc_fence_after();
+            const uint64_t db = smem_desc_sw128(sB + s * C::kTileB, 16, 1024);
+            if (elect_one()) {
+              for (int m = 0; m < nblk; ++m) {
+                // A: columns [128m, 128m+128) = two 64-column boxes (lbo = box stride); the
+                // rope part has one box, and lanes 64-127 of its result are never read
+                const uint64_t da = smem_desc_sw128(sA + ab * C::kSlice + 2 * m * C::kBox, C::kBox, 1024);
 #pragma unroll
-              for (int k = 0; k < kHeadsPad / 16; ++k)
-                umma_f16<1>(tmem + tb * 256 + m * 128, da + (uint64_t)((k * 2048) >> 4),
-                            db + (uint64_t)(((k >> 2) * kKeyTile3 * 128 + (k & 3) * 32) >> 4), id,
-                            k != 0);
+                for (int k = 0; k < kHeadsPad / 16; ++k)
+                  umma_f16<1>(tmem + tb * 256 + m * 128, da + (uint64_t)((k * 2048) >> 4),
+                              db + (uint64_t)(((k >> 2) * kKeyTile3 * 128 + (k & 3) * 32) >> 4), id,
+                              (e | k) != 0);
+              }
+              umma_commit(smem_u32(&bars.b_empty[s]));
+              if (e == nsl - 1) umma_commit(smem_u32(&bars.t_full[tb]));
+              // the slot's last reads of this item: free it for the next item's slice
+              if (t == x.ntiles - 1) umma_commit(smem_u32(&bars.a_empty[ab]));
             }
-            umma_commit(smem_u32(&bars.t_full[tb]));
-            umma_commit(smem_u32(&bars.b_empty[s]));
+            __syncwarp();
+            ++nb;
           }
-          __syncwarp();
-          ++nb;
+          if (failed) break;
           ++nt;
         }
         if (failed) break;
-        if (elect_one()) umma_commit(smem_u32(&bars.a_empty[ab]));
-        __syncwarp();
-        ++na;
+        for (int h = 0; h < nsl; ++h) {
+          if (pk.mixed ? h : ab1) ++ua1; else ++ua0;
+        }
+        ++ni;
       }
       // the MMAs issued last complete before the exit (their TMEM is freed afterwards)
       if (nt > 0) {
@@ -848,13 +892,13 @@ __global__ void __launch_bounds__(kThreads3, 1)
     const int cg = (warp - 2) >> 2;    // column group 0..3
     int nt = 0;
     for (int it = blockIdx.x; it < nitems; it += gridDim.x) {
-      const Item3 x = item3<D>(a, it);
+      const Item3 x = item3<D>(a, it, nparts);
       if (x.ntiles == 0) continue;
-      const bool rope = x.part == 2 * C::kDParts;
-      const bool is_dv = !rope && x.part >= C::kDParts;
-      float* acc = rope ? a.dkr_acc : is_dv ? a.dv_acc : a.dk_acc;
+      const Part3 pk = part3<D>(x.part, merged);
+      const bool rope = pk.rope;
+      float* acc = rope ? a.dkr_acc : pk.is_dv ? a.dv_acc : a.dk_acc;   // merged: dK + dV
       const int ld = rope ? 64 : D;
-      const int col0 = rope ? 0 : (x.part % C::kDParts) * C::kW;
+      const int col0 = pk.col0;
       const int nk = rope ? 32 : C::kW / 4;   // keys of a tile per column group: 64 or 32
       const int c_off = cg * nk;              // TMEM column of the share within a buffer
       const int mblk = c_off >> 7, key0 = c_off & 127;
@@ -919,7 +963,7 @@ int cast_all(const DsaSfaBwdParams* p, cudaStream_t stream) {
   const float* src[3] = {p->dk_acc, p->dkr_acc, p->dv_acc};
   void* dst[3] = {p->dk, p->dkr, p->dv};
   for (int i = 0; i < 3; ++i) {
-    if (!dst[i]) continue;
+    if (!dst[i] || !src[i]) continue;
     const int64_t threads = (n[i] + 3) / 4;
     cast_kernel<T><<<dim3((unsigned)((threads + 255) / 256)), dim3(256), 0, stream>>>(
         src[i], static_cast<T*>(dst[i]), n[i]);
@@ -1017,7 +1061,8 @@ int launch(const DsaSfaBwdParams* p, cudaStream_t stream) {
   if (!p->accumulate &&
       (cudaMemsetAsync(p->dk_acc, 0, sizeof(float) * p->kv_rows * D, stream) != cudaSuccess ||
        cudaMemsetAsync(p->dkr_acc, 0, sizeof(float) * p->kv_rows * 64, stream) != cudaSuccess ||
-       cudaMemsetAsync(p->dv_acc, 0, sizeof(float) * p->kv_rows * D, stream) != cudaSuccess))
+       (p->dv_acc &&
+        cudaMemsetAsync(p->dv_acc, 0, sizeof(float) * p->kv_rows * D, stream) != cudaSuccess)))
     return DSA_ERR_CUDA;
   launch_prep(a, const_cast<int32_t*>(a.ws_rows), const_cast<int32_t*>(a.ws_count), p->num_rows,
               stream);
@@ -1047,7 +1092,7 @@ int launch(const DsaSfaBwdParams* p, cudaStream_t stream) {
     const int smem = Cfg3<D>::kOffBars + (int)sizeof(Bars3);
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return DSA_ERR_CUDA;
-    const int64_t items = p->num_rows * Cfg3<D>::kParts;
+    const int64_t items = p->num_rows * (p->dv_acc ? Cfg3<D>::kParts : Cfg3<D>::kDParts + 1);
     const int grid = (int)(items < sm_count() ? items : sm_count());
     k<<<dim3((unsigned)grid), dim3(kThreads3), smem, stream>>>(m3, a);
   }
@@ -1075,7 +1120,7 @@ extern "C" int dsa_sfa_bwd(const DsaSfaBwdParams* p, void* stream_) {
       p->sparse_block_size < 1 || p->kv_rows < 1 || !p->q || !p->q_rope || !p->key ||
       !p->key_rope || !p->d_out || !p->out || !p->softmax_max || !p->softmax_sum ||
       !p->sparse_indices || !p->act_q || !p->act_k || !p->q_row_base || !p->dq || !p->dqr ||
-      !p->dk_acc || !p->dkr_acc || !p->dv_acc)
+      !p->dk_acc || !p->dkr_acc || (!p->dv_acc && p->dv))
     return DSA_ERR_INVALID_ARG;
   if (!p->block_table && !p->k_row_base) return DSA_ERR_INVALID_ARG;
   if (!p->workspace || (reinterpret_cast<uintptr_t>(p->workspace) & 255u) != 0 ||
@@ -1097,7 +1142,8 @@ extern "C" int dsa_sfa_bwd(const DsaSfaBwdParams* p, void* stream_) {
 
 extern "C" int dsa_sfa_bwd_cast(const DsaSfaBwdParams* p, void* stream_) {
   using namespace dsa::sfa_bwd;
-  if (!p || !p->dk_acc || !p->dkr_acc || !p->dv_acc || p->kv_rows < 1) return DSA_ERR_INVALID_ARG;
+  if (!p || !p->dk_acc || !p->dkr_acc || (!p->dv_acc && p->dv) || p->kv_rows < 1)
+    return DSA_ERR_INVALID_ARG;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   if (p->dtype == DSA_DTYPE_BF16) return cast_all<__nv_bfloat16>(p, stream);
   if (p->dtype == DSA_DTYPE_FP16) return cast_all<__half>(p, stream);

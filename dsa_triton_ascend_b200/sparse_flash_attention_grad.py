@@ -25,7 +25,7 @@ _VALID_N1 = (1, 2, 4, 8, 16, 32, 64, 128)
 def _sfa_grad(query, key, value, sparse_indices, d_out, out, softmax_max, softmax_sum,
               scale_value, query_rope, key_rope, actual_seq_lengths_query,
               actual_seq_lengths_kv, sparse_block_size, layout, sparse_mode, pre_tokens,
-              next_tokens, deterministic, defer_cast, accumulators=None):
+              next_tokens, deterministic, defer_cast, accumulators=None, merged=False):
     # guards: sparse_flash_attention_grad_triton.py:428-438
     if pre_tokens != INT64_MAX or next_tokens != INT64_MAX:
         raise ValueError("pre_tokens/next_tokens only support default INT64_MAX")
@@ -94,22 +94,28 @@ def _sfa_grad(query, key, value, sparse_indices, d_out, out, softmax_max, softma
     dqr = torch.empty_like(qr)
     flat = None
     if accumulators is None:
-        # one contiguous fp32 buffer [dk | dkr | dv], so a multi-GPU caller can sum the key
-        # gradients of all ranks with a single all-reduce
-        flat = torch.empty(kv_rows * (2 * D + D_ROPE), dtype=torch.float32, device=dev)
+        # one contiguous fp32 buffer [dk | dkr | dv] ([dk + dv | dkr] when merged), so a
+        # multi-GPU caller can sum the key gradients of all ranks with a single all-reduce
+        nacc = D + D_ROPE + (0 if merged else D)
+        flat = torch.empty(kv_rows * nacc, dtype=torch.float32, device=dev)
         dk_acc = flat[: kv_rows * D].view(kv_rows, D)
         dkr_acc = flat[kv_rows * D: kv_rows * (D + D_ROPE)].view(kv_rows, D_ROPE)
-        dv_acc = flat[kv_rows * (D + D_ROPE):].view(kv_rows, D)
+        dv_acc = None if merged else flat[kv_rows * (D + D_ROPE):].view(kv_rows, D)
     else:
-        dk_acc, dkr_acc, dv_acc = accumulators
+        dk_acc, dkr_acc, dv_acc = (tuple(accumulators) + (None,))[:3]
+        if merged:
+            dv_acc = None
         for t, n in ((dk_acc, D), (dkr_acc, D_ROPE), (dv_acc, D)):
-            if (t.dtype != torch.float32 or not t.is_contiguous() or t.device != dev
+            if t is None and merged:
+                continue
+            if (t is None or t.dtype != torch.float32 or not t.is_contiguous() or t.device != dev
                     or t.numel() != kv_rows * n):
                 raise ValueError("accumulators must be contiguous fp32 [kv_rows, dim] on the "
                                  "query's device")
     kshape = key.shape
     dk = torch.empty(kshape, dtype=key.dtype, device=dev)
-    dv = torch.empty(kshape, dtype=value.dtype if value is not None else key.dtype, device=dev)
+    dv = None if merged else torch.empty(
+        kshape, dtype=value.dtype if value is not None else key.dtype, device=dev)
     dkr = torch.empty(key_rope.shape, dtype=key_rope.dtype, device=dev)
     ws_bytes = lib().dsa_sfa_bwd_workspace_size(num_rows, topk, int(sparse_block_size))
     ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=dev)
@@ -119,8 +125,11 @@ def _sfa_grad(query, key, value, sparse_indices, d_out, out, softmax_max, softma
     p.d_out, p.out, p.softmax_max, p.softmax_sum = ptr(do), ptr(o), ptr(smax), ptr(ssum)
     p.sparse_indices, p.act_q, p.act_k = ptr(si), ptr(act_q), ptr(act_k)
     p.q_row_base, p.k_row_base, p.block_table = ptr(q_base), ptr(k_base), 0
-    p.dq, p.dqr, p.dk, p.dkr, p.dv = ptr(dq), ptr(dqr), ptr(dk), ptr(dkr), ptr(dv)
-    p.dk_acc, p.dkr_acc, p.dv_acc = ptr(dk_acc), ptr(dkr_acc), ptr(dv_acc)
+    # merged: dv and dv_acc NULL; the kernels add dS^T Q + P^T dO into dk_acc
+    p.dq, p.dqr, p.dk, p.dkr = ptr(dq), ptr(dqr), ptr(dk), ptr(dkr)
+    p.dv = 0 if merged else ptr(dv)
+    p.dk_acc, p.dkr_acc = ptr(dk_acc), ptr(dkr_acc)
+    p.dv_acc = 0 if merged else ptr(dv_acc)
     p.error_flag = ptr(error_flag(dev))
     p.workspace, p.workspace_bytes = ptr(ws), ws_bytes
     p.num_rows, p.batch, p.n1, p.d, p.topk = num_rows, B, N1, D, topk
@@ -135,13 +144,13 @@ def _sfa_grad(query, key, value, sparse_indices, d_out, out, softmax_max, softma
     if defer_cast:
         def finish():
             check(lib().dsa_sfa_bwd_cast(p, stream_ptr(dev)), "dsa_sfa_bwd_cast")
-            return dq, dk, dv, dqr, dkr
+            return (dq, dk, dqr, dkr) if merged else (dq, dk, dv, dqr, dkr)
         finish.query_grads = (dq, dqr)   # ready before the cast (they need no reduction)
-        # the three accumulators as one contiguous fp32 tensor (None when the caller passed
-        # its own accumulators)
+        # the accumulators as one contiguous fp32 tensor (None when the caller passed its
+        # own accumulators)
         finish.key_grad_buffer = flat
-        return (dk_acc, dkr_acc, dv_acc), finish
-    return dq, dk, dv, dqr, dkr
+        return ((dk_acc, dkr_acc) if merged else (dk_acc, dkr_acc, dv_acc)), finish
+    return (dq, dk, dqr, dkr) if merged else (dq, dk, dv, dqr, dkr)
 
 
 def sparse_flash_attention_grad_triton(
@@ -173,8 +182,26 @@ def sparse_flash_attention_grad_triton(
                      next_tokens, deterministic, defer_cast=False)
 
 
+def sparse_flash_attention_grad_merged(query, key, sparse_indices, d_out, out, softmax_max,
+                                       softmax_sum, scale_value=1.0, **kw):
+    """Backward for key == value (MLA-absorb: one latent tensor is both): returns
+    (d_query, d_key, d_query_rope, d_key_rope) with d_key = dK + dV, the gradient the
+    reference's bprop hands back for the shared tensor (sparse_flash_attention_grad_triton.py:66).
+
+    Same arguments as :func:`sparse_flash_attention_grad_triton` without ``value``.  The
+    kernels accumulate dS^T Q + P^T dO into one fp32 buffer, which halves the scattered
+    key-gradient bytes (4 (D + 64) per valid pair instead of 4 (2 D + 64))."""
+    args = dict(query_rope=None, key_rope=None, actual_seq_lengths_query=None,
+                actual_seq_lengths_kv=None, sparse_block_size=1, layout="BSND", sparse_mode=3,
+                pre_tokens=INT64_MAX, next_tokens=INT64_MAX, deterministic=False)
+    args.update(kw)
+    return _sfa_grad(query, key, key, sparse_indices, d_out, out, softmax_max, softmax_sum,
+                     scale_value, defer_cast=False, merged=True, **args)
+
+
 def sparse_flash_attention_grad_partial(query, key, value, sparse_indices, d_out, out,
-                                        softmax_max, softmax_sum, scale_value=1.0, **kw):
+                                        softmax_max, softmax_sum, scale_value=1.0,
+                                        merge_key_grads=False, **kw):
     """Backward for a caller that reduces the key gradients itself (e.g. across GPUs).
 
     Same arguments as :func:`sparse_flash_attention_grad_triton`, plus ``accumulators``:
@@ -184,6 +211,10 @@ def sparse_flash_attention_grad_partial(query, key, value, sparse_indices, d_out
     which the caller may all-reduce in place, and ``finish()`` which casts them to the key
     dtype and returns the usual 5-tuple.  Fresh accumulators are views of one contiguous
     buffer, ``finish.key_grad_buffer``, so one all-reduce of it sums all three.
+
+    ``merge_key_grads=True`` (key == value): the accumulators are ``(dkv_acc, dkr_acc)``
+    with dkv = dK + dV, and ``finish()`` returns (d_query, d_key, d_query_rope, d_key_rope)
+    as :func:`sparse_flash_attention_grad_merged` does.
     """
     args = dict(query_rope=None, key_rope=None, actual_seq_lengths_query=None,
                 actual_seq_lengths_kv=None, sparse_block_size=1, layout="BSND", sparse_mode=3,
@@ -191,7 +222,7 @@ def sparse_flash_attention_grad_partial(query, key, value, sparse_indices, d_out
                 accumulators=None)
     args.update(kw)
     return _sfa_grad(query, key, value, sparse_indices, d_out, out, softmax_max, softmax_sum,
-                     scale_value, defer_cast=True, **args)
+                     scale_value, defer_cast=True, merged=bool(merge_key_grads), **args)
 
 
 class SparseFlashAttentionGradTriton(torch.nn.Module):

@@ -154,7 +154,7 @@ def sfa_fwd(q, k, qr, kr, tok_idx, scale, act_q=None, act_k=None, sparse_mode=3,
 
 
 def sfa_bwd(q, k, qr, kr, tok_idx, d_out, out, smax, ssum, scale, act_q=None, act_k=None,
-            sparse_mode=3, dtype="bf16", rounding="golden"):
+            sparse_mode=3, dtype="bf16", rounding="golden", round_out=True):
     """SFA backward on BSND numpy inputs; restates ``sparse_flash_attention_grad_triton.py:189-308``.
 
     P = exp(s - max) / sum (sum <= 0 -> 1, :232-234), delta = rowsum(dO*O) (:237),
@@ -163,6 +163,8 @@ def sfa_bwd(q, k, qr, kr, tok_idx, d_out, out, smax, ssum, scale, act_q=None, ac
     (dq, dk, dv, dqr, dkr) rounded to ``dtype``.  ``rounding="kernel"`` additionally rounds P
     and dS to ``dtype`` before the three products, as the reference kernel does
     (``dS.to(k_full.dtype)``, ``P_t.to(do_sub.dtype)``, :271-298); the golden keeps them fp32.
+    ``round_out=False`` returns the five gradients in fp32 (for sums such as dk + dv, which a
+    merged caller rounds once).
     """
     q = np.asarray(q, np.float32); k = np.asarray(k, np.float32)
     qr = np.asarray(qr, np.float32); kr = np.asarray(kr, np.float32)
@@ -199,5 +201,5 @@ def sfa_bwd(q, k, qr, kr, tok_idx, d_out, out, smax, ssum, scale, act_q=None, ac
             np.add.at(dk[b, :, 0, :], pos, dS.T @ q[b, s1])
             np.add.at(dkr[b, :, 0, :], pos, dS.T @ qr[b, s1])
             np.add.at(dv[b, :, 0, :], pos, P.T @ do[b, s1])
-    r = lambda x: round_to(x, dtype)
+    r = (lambda x: round_to(x, dtype)) if round_out else (lambda x: x)
     return r(dq), r(dk), r(dv), r(dqr), r(dkr)

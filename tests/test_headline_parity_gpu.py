@@ -97,6 +97,16 @@ def test_config4_geometry_key_gradients_in_full():
                       sparse_mode=3, rounding="kernel")
     for g, r, n in zip(grads, ref, ("dq", "dk", "dv", "dq_rope", "dk_rope")):
         assert_close(_np(g), r, what=n)
+    # key == value: the merged kernels' dK + dV at the same geometry
+    mdq, mdkv, mdqr, mdkr = dsa.sparse_flash_attention_grad_merged(
+        w["q"], w["k"], w["si"], w["dout"], out, mx, sm, w["scale"], query_rope=w["qr"],
+        key_rope=w["kr"], sparse_mode=3)
+    dsa.check_device_errors()
+    _, fdk, fdv, _, _ = sfa.sfa_bwd(q, k, qr, kr, si, do, _np(out), _np(mx), _np(sm), w["scale"],
+                                    sparse_mode=3, rounding="kernel", round_out=False)
+    assert_close(_np(mdkv), sfa.round_to(fdk + fdv, "bf16"), what="dk + dv")
+    assert_close(_np(mdkr), ref[4], what="dk_rope (merged call)")
+    np.testing.assert_array_equal(_np(mdq), _np(grads[0]))
 
 
 def test_config3_decode_real_shape_all_rows():

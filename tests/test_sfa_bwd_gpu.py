@@ -97,3 +97,63 @@ def test_bwd_tnd_matches_bsnd():
     for gi, ri, key in zip(res, ref, NAMES):
         lens = lq if key in ("dq", "dqr") else lk
         assert_close(host(gi), cat(ri, lens), what="tnd " + key)
+
+
+def _bwd_merged(c, out, mx, sm, dt, mode, blk=1):
+    from dsa_triton_ascend_b200 import sparse_flash_attention_grad_merged, check_device_errors
+    res = sparse_flash_attention_grad_merged(
+        cuda(c["q"], dt), cuda(c["k"], dt), icuda(c["si"]), cuda(c["dout"], dt), cuda(out, dt),
+        cuda(mx, "fp32"), cuda(sm, "fp32"), c["scale"], query_rope=cuda(c["qr"], dt),
+        key_rope=cuda(c["kr"], dt), sparse_block_size=blk, sparse_mode=mode)
+    check_device_errors()
+    return [host(t) for t in res]
+
+
+@pytest.mark.parametrize("N1,D,dt,blk", [(128, 512, "bf16", 1), (64, 256, "fp16", 1),
+                                         (16, 128, "bf16", 4), (1, 512, "bf16", 1)])
+def test_bwd_merged_key_gradient(N1, D, dt, blk):
+    """key == value: the merged kernels return dK + dV (one fp32 accumulator) equal to the
+    oracle's dk + dv, and the query gradients equal the 5-output call's."""
+    c = I.sfa_case(2, 4, 300, N1, D, 96 // blk, blk, 3, dt, seed=300 + N1)
+    tok = sfa.expand_block_indices(c["si"], blk)
+    out, mx, sm = sfa.sfa_fwd(c["q"], c["k"], c["qr"], c["kr"], tok, c["scale"], sparse_mode=3,
+                              dtype=dt)
+    dq, dkv, dqr, dkr = _bwd_merged(c, out, mx, sm, dt, 3, blk)
+    rdq, rdk, rdv, rdqr, rdkr = sfa.sfa_bwd(c["q"], c["k"], c["qr"], c["kr"], tok, c["dout"], out,
+                                            mx, sm, c["scale"], sparse_mode=3, dtype=dt,
+                                            rounding="kernel")
+    assert_close(dq, rdq, what="dq")
+    assert_close(dqr, rdqr, what="dqr")
+    assert_close(dkr, rdkr, what="dkr")
+    # the merged gradient is the fp32 sum rounded once (not the sum of two rounded terms)
+    _, fdk, fdv, _, _ = sfa.sfa_bwd(c["q"], c["k"], c["qr"], c["kr"], tok, c["dout"], out, mx, sm,
+                                    c["scale"], sparse_mode=3, dtype=dt, rounding="kernel",
+                                    round_out=False)
+    assert_close(dkv, sfa.round_to(fdk + fdv, dt), what="dk + dv")
+    five = _bwd(c, out, mx, sm, dt, 3, blk)
+    np.testing.assert_array_equal(dq, five[0])
+    np.testing.assert_array_equal(dqr, five[3])
+
+
+def test_bwd_merged_partial_accumulators_match_separate():
+    """The fp32 accumulators of the merged partial call equal dk_acc + dv_acc of the
+    separate one (same products, summed in another order), and one buffer holds both."""
+    import torch
+    from dsa_triton_ascend_b200 import sparse_flash_attention_grad_partial, check_device_errors
+    c = I.sfa_case(1, 6, 512, 128, 512, 256, 1, 3, "bf16", seed=41)
+    out, mx, sm = sfa.sfa_fwd(c["q"], c["k"], c["qr"], c["kr"], c["si"], c["scale"],
+                              sparse_mode=3, dtype="bf16")
+    args = (cuda(c["q"]), cuda(c["k"]), cuda(c["k"]), icuda(c["si"]), cuda(c["dout"]), cuda(out),
+            cuda(mx, "fp32"), cuda(sm, "fp32"), c["scale"])
+    kw = dict(query_rope=cuda(c["qr"]), key_rope=cuda(c["kr"]))
+    (dk, dkr, dv), fin = sparse_flash_attention_grad_partial(*args, **kw)
+    (dkv, dkr2), fin2 = sparse_flash_attention_grad_partial(*args, merge_key_grads=True, **kw)
+    torch.cuda.synchronize()
+    check_device_errors()
+    assert fin2.key_grad_buffer.numel() == dkv.numel() + dkr2.numel()
+    ref = (dk + dv).cpu().numpy()
+    np.testing.assert_allclose(dkv.cpu().numpy(), ref, rtol=1e-4, atol=1e-5 * np.abs(ref).max())
+    np.testing.assert_allclose(dkr2.cpu().numpy(), dkr.cpu().numpy(), rtol=1e-4,
+                               atol=1e-5 * np.abs(dkr.cpu().numpy()).max())
+    dq, dkv_b, dqr, dkr_b = fin2()
+    assert dkv_b.shape == c["k"].shape and dkr_b.shape == c["kr"].shape
