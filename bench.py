@@ -43,10 +43,11 @@ BWD_SCATTER_BYTES_PER_PAIR = 4 * (2 * D + DR)
 # `ncu --set full` capture of the last 256 query rows of config 4 (524,288 pairs; command and
 # figures in profiles/sfa_kernels_config4_rows256_full.md), scaled to a launch by its pairs.
 # Backward: K1 + K2 + K3, plus the delta kernel's read of dO and O (2 x N1 x D x 2 B a row).
+# Build of the capture: the kernels of commit cb19fcd.
 PROFILE_PAIRS = 524288
-BWD_DRAM_BYTES_PER_PAIR = (94.85 + 215.33 + 146.08 + 20.42 + 396.22 + 26.15) * 1e6 / PROFILE_PAIRS
+BWD_DRAM_BYTES_PER_PAIR = (103.11 + 218.89 + 146.14 + 19.40 + 398.23 + 30.89) * 1e6 / PROFILE_PAIRS
 BWD_DRAM_BYTES_PER_ROW = 2 * N1 * D * 2
-FWD_DRAM_BYTES_PER_PAIR = (49.38 + 2.23) * 1e6 / PROFILE_PAIRS
+FWD_DRAM_BYTES_PER_PAIR = (49.35 + 1.95) * 1e6 / PROFILE_PAIRS
 # DRAM traffic of one call of each secondary workload at the size bench.py runs, from one ncu
 # capture of the library's kernels (profiles/secondary_workloads_traffic.md)
 WORKLOAD_DRAM_BYTES = {
