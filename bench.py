@@ -215,7 +215,7 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
     import dsa_triton_ascend_b200 as dsa
-    from dsa_triton_ascend_b200.sharding import shard_act_q, shard_rows
+    from dsa_triton_ascend_b200.sharding import SFA_ROW_COST, shard_act_q, shard_rows
     from dsa_triton_ascend_b200.synthetic import sfa_prefill, valid_pairs_per_row
 
     w = sfa_prefill(device=dev)
@@ -223,7 +223,7 @@ def main():
     pairs = valid_pairs_per_row(w["si"]).cpu().numpy()
     if args.rows:
         pairs[: S1 - args.rows] = 0
-    r0, r1 = shard_rows(pairs, world, rank)
+    r0, r1 = shard_rows(pairs, world, rank, row_cost=SFA_ROW_COST)
     if args.rows:
         r0 = max(r0, S1 - args.rows)
     my_pairs = int(pairs[r0:r1].sum())

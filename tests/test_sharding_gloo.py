@@ -20,6 +20,15 @@ def test_shard_rows_balances_pairs():
         assert all(bounds[i][1] == bounds[i + 1][0] for i in range(world - 1))
         share = [pairs[a:b].sum() for a, b in bounds]
         assert max(share) - min(share) <= 2048
+        # with a per-row cost the rank of the short causal rows takes fewer of them
+        from dsa_triton_ascend_b200.sharding import SFA_ROW_COST
+        cb = [shard_rows(pairs, world, r, row_cost=SFA_ROW_COST) for r in range(world)]
+        assert cb[0][0] == 0 and cb[-1][1] == len(pairs)
+        assert all(cb[i][1] == cb[i + 1][0] for i in range(world - 1))
+        cost = [pairs[a:b].sum() + SFA_ROW_COST * (b - a) for a, b in cb]
+        assert max(cost) - min(cost) <= 2 * (2048 + SFA_ROW_COST)   # a row at each end
+        if world > 1:
+            assert cb[0][1] - cb[0][0] < bounds[0][1] - bounds[0][0]
 
 
 def _free_port():
