@@ -154,6 +154,9 @@ int dsa_sfa_fwd_noalloc(const DsaSfaFwdParams* params, void* stream);
  * multi-GPU one that all-reduces the fp32 buffers) finishes with dsa_sfa_bwd_cast().
  * The key gradients are scatter-added with fp32 vector reductions, so their summation order
  * is not deterministic (as in the reference, which rejects deterministic=True).
+ * Merged key gradient: with dv_acc = NULL (and dv = NULL) the call is for key == value (one
+ * latent tensor, MLA-absorb) and accumulates dK + dV into dk_acc (cast into dk), the sum the
+ * reference's bprop forms for that tensor; half the scattered bytes of separate dK and dV.
  */
 typedef struct DsaSfaBwdParams {
   const void* q;
