@@ -54,6 +54,7 @@ WORKLOAD_DRAM_BYTES = {
     "li": (138.45 + 52.63 + 67.75 + 49.59) * 1e6,            # score + top-k (profiles/li_score_topk_config2.md)
     "decode": (0.33 + 84.43 + 0.10 + 16.92) * 1e6,           # prep + forward + combine
     "sli": (1284.81 + 58.37 + 260.75 + 109.38 + 4.20) * 1e6,  # teacher + index + cast
+    "dense": (1361.01 + 128.45 + 412.56 + 124.68) * 1e6,      # teacher + index (profiles/dense_indexer_loss_config5.md)
 }
 
 
@@ -188,11 +189,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="sfa", choices=["sfa", "li", "li_fp8", "decode", "sli"],
+    ap.add_argument("--workload", default="sfa", choices=["sfa", "li", "li_fp8", "decode", "sli", "dense"],
                     help="sfa: config 4 forward+backward (the headline); li: config 2 indexer; "
                          "li_fp8: config 2 geometry through the FP8 indexer (e4m3 query / key, "
                          "per-key scales); decode: config 3 paged forward; sli: config 5 "
-                         "indexer KL-loss grad")
+                         "indexer KL-loss grad; dense: the dense indexer KL loss (every "
+                         "visible key) at config-5 geometry, one key head")
     ap.add_argument("--rows", type=int, default=0,
                     help="profiling aid: time only the last ROWS query rows of config 4 "
                          "(each sees the full 2048 keys); 0 = the whole workload")
@@ -623,6 +625,25 @@ def run_other(args, rank, world, local):
         pairs = wd["si"].numel()
         flops, nbytes = pairs * FWD_FLOP_PER_PAIR, pairs * GATHER_BYTES_PER_PAIR
         metric, unit, wl = "SFA decode TFLOP/s", "TFLOP/s", "BASELINE config 3 (PA_BSND, B=32, S1=1, N1=128, top-2048, 16384-block pool)"
+    elif args.workload == "dense":
+        # config-5 geometry, one key head: the KL loss over every visible key (33.6 M
+        # causal pairs); the teacher's softmax statistics are those of full causal attention,
+        # from the forward over all keys
+        from dsa_triton_ascend_b200.synthetic import sli_prefill
+        w = sli_prefill(device=dev, seed=0)
+        S = w["q"].shape[1]
+        ids = torch.arange(S, dtype=torch.int32, device=dev).view(1, 1, 1, S).expand(1, S, 1, S).contiguous()
+        _, mx_d, sm_d = dsa.sparse_flash_attention_triton(
+            w["q"], w["k"], w["k"], ids, w["scale"], query_rope=w["qr"], key_rope=w["kr"],
+            sparse_mode=3, return_softmax_lse=True)
+        del ids
+        fn = lambda: dsa.dense_loss_backward_triton(
+            w["q"], w["k"], w["qi"], w["ki"], w["w"], mx_d, sm_d, scale_value=w["scale"],
+            query_rope=w["qr"], key_rope=w["kr"])
+        pairs = S * (S + 1) // 2
+        flops, nbytes = pairs * 2 * (64 * 128 * 3 + 128 * 576), pairs * (GATHER_BYTES_PER_PAIR + 256)
+        metric, unit, wl = ("dense indexer KL-grad TFLOP/s", "TFLOP/s",
+                            "config 5 geometry, dense (every visible key; S1=S2=8192, N1=128, N2=1, Nidx1=64)")
     else:
         return run_sli(args, rank, world, local)
     timing = "CUDA events around each call"

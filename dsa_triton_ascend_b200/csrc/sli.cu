@@ -286,7 +286,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTThreads, 1)
 constexpr int kIKeys = 128;      // keys per tile (UMMA M)
 constexpr int kNip = 64;         // index heads padded to 64
 constexpr int kDi = 128;         // index head dim
-constexpr int kIStages = 3;
 constexpr int kIDrain0 = 6;      // first dKI drain warp
 constexpr int kIDrainWarps = 8;  // two per TMEM lane quadrant, 64 columns each
 constexpr int kIGather1 = kIDrain0 + kIDrainWarps;   // extra gather warps after the drains
@@ -296,18 +295,19 @@ constexpr int kIGathers = 3;     // warp 0 + 2: a thread issues one gather4 ever
 constexpr int kIThreads = 32 * (kIGather1 + kIGathers - 1);   // 0, 14-16: gathers, 1: MMA,
                                                                // 2-5: epilogue, 6-13: drains
 
+template <int STG>
 struct ICfg {
   static constexpr int kQiBytes = 2 * kNip * 128;           // [dim chunk][64 heads][128 B]
   static constexpr int kStage = 2 * kIKeys * 128;           // [dim chunk][128 keys][128 B]
   static constexpr int kCBytes = 2 * kIKeys * 128;          // C = hi + lo: 2 x [128 keys][64 heads]
   static constexpr int kOffQi = 0;
   static constexpr int kOffK = kQiBytes;
-  static constexpr int kOffC = kOffK + kIStages * kStage;
+  static constexpr int kOffC = kOffK + STG * kStage;
   static constexpr int kOffStage = kOffC + 2 * kCBytes;       // drain staging, 32 x 33 floats per drain warp
   // dW column sums (128 x 65 floats) reuse the key ring: they are formed after the last
   // tile's MMAs, when no gather or MMA touches the ring any more
   static constexpr int kOffRed = kOffK;
-  static_assert(128 * 65 * 4 <= kIStages * kStage, "dW sums fit the key ring");
+  static_assert(128 * 65 * 4 <= STG * kStage, "dW sums fit the key ring");
   static constexpr int kOffI = kOffStage + kIDrainWarps * 32 * 33 * 4;   // I then dI: topk floats
 };
 
@@ -315,21 +315,22 @@ struct IMaps {
   CUtensorMap ki;
 };
 
+template <int STG>
 struct __align__(16) IBars {
-  uint64_t full[kIStages], empty[kIStages], rfull[2], rfree[2], cready[2], cfree[2], dfull[2], dfree[2], qdone;
+  uint64_t full[STG], empty[STG], rfull[2], rfree[2], cready[2], cfree[2], dfull[2], dfree[2], qdone;
   uint32_t tmem_slot;
   float w[kNip];
   float red[8];
   float stat[4];
 };
 
-template <typename T>
+template <typename T, int STG>
 __global__ void __launch_bounds__(kIThreads, 1)
     sli_index_kernel(const __grid_constant__ IMaps maps, const Args a) {
-  using C = ICfg;
+  using C = ICfg<STG>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const int topk_pad = (a.topk + 3) & ~3;
-  IBars& bars = *reinterpret_cast<IBars*>(smem_raw + C::kOffI + topk_pad * 4);
+  IBars<STG>& bars = *reinterpret_cast<IBars<STG>*>(smem_raw + C::kOffI + topk_pad * 4);
   float* Ibuf = reinterpret_cast<float*>(smem_raw + C::kOffI);
   const uint32_t sbase = smem_u32(smem_raw);
   const uint32_t sQi = sbase + C::kOffQi, sK = sbase + C::kOffK, sC = sbase + C::kOffC;
@@ -364,7 +365,7 @@ __global__ void __launch_bounds__(kIThreads, 1)
     bars.w[g] = wv;
   }
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kIStages; ++s) {
+    for (int s = 0; s < STG; ++s) {
       mbar_init(smem_u32(&bars.full[s]), 1);
       mbar_init(smem_u32(&bars.empty[s]), 1);
     }
@@ -404,13 +405,13 @@ __global__ void __launch_bounds__(kIThreads, 1)
     const int c = item / (kIKeys / 4), g = item % (kIKeys / 4);
     const int filler = key_row_of(a, b, row, 0);
     for (int j = 0; j < nsteps && !failed; ++j) {
-      const int t = j % ntiles, s = j % kIStages;
+      const int t = j % ntiles, s = j % STG;
       const int e0 = kIKeys * t + 4 * g;
       int rr[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e)
         rr[e] = issuer && e0 + e < n ? key_row_of(a, b, row, e0 + e) : filler;
-      mbar_wait(smem_u32(&bars.empty[s]), ((j / kIStages) & 1) ^ 1, a.err, &failed);
+      mbar_wait(smem_u32(&bars.empty[s]), ((j / STG) & 1) ^ 1, a.err, &failed);
       failed = __any_sync(0xffffffffu, failed);
       if (failed) break;
       const uint32_t fb = smem_u32(&bars.full[s]);
@@ -430,10 +431,10 @@ __global__ void __launch_bounds__(kIThreads, 1)
       const uint64_t dqi_k = smem_desc_sw128(sQi, 16, 1024);
       const uint64_t dqi_mn = smem_desc_sw128(sQi, kNip * 128, 1024);
       for (int j = 0; j < nsteps && !failed; ++j) {
-        const int t = j % ntiles, s = j % kIStages, rb = j & 1;
+        const int t = j % ntiles, s = j % STG, rb = j & 1;
         const bool passB = j >= ntiles;
         if (j >= 2) mbar_wait_spin(smem_u32(&bars.rfree[rb]), ((j >> 1) - 1) & 1, a.err, &failed);
-        mbar_wait_spin(smem_u32(&bars.full[s]), (j / kIStages) & 1, a.err, &failed);
+        mbar_wait_spin(smem_u32(&bars.full[s]), (j / STG) & 1, a.err, &failed);
         if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
         tc_fence_after();
         const uint64_t dk_k = smem_desc_sw128(sK + s * C::kStage, 16, 1024);
@@ -725,6 +726,12 @@ int launch(const DsaSliParams* p, cudaStream_t stream) {
       !make_tmap_2d_16b(&tm.kr, p->key_rope, bf16, krows, 64, 128, 64, 1) ||
       !make_tmap_2d_16b(&im.ki, p->key_index, bf16, krows, kDi, kDi * 2, 64, 1))
     return DSA_ERR_TMA_DESCRIPTOR;
+  // the index kernel keeps a row's topk scores in shared memory: three key stages when
+  // they leave room, two otherwise (rows of up to 8192 entries); checked before any launch
+  const int ipad = ((a.topk + 3) & ~3) * 4;
+  const int ismem3 = ICfg<3>::kOffI + ipad + (int)sizeof(IBars<3>);
+  const int ismem2 = ICfg<2>::kOffI + ipad + (int)sizeof(IBars<2>);
+  if (ismem2 > 232448) return DSA_ERR_INVALID_ARG;
   if (cudaMemsetAsync(p->dki_acc, 0, sizeof(float) * krows * kDi, stream) != cudaSuccess ||
       cudaMemsetAsync(p->loss, 0, sizeof(float), stream) != cudaSuccess)
     return DSA_ERR_CUDA;
@@ -736,9 +743,9 @@ int launch(const DsaSliParams* p, cudaStream_t stream) {
     k<<<dim3(2 * (unsigned)a.rows), dim3(kTThreads), smem, stream>>>(tm, a);
   }
   {
-    auto k = sli_index_kernel<T>;
-    const int smem = ICfg::kOffI + ((a.topk + 3) & ~3) * 4 + (int)sizeof(IBars);
-    if (smem > 232448) return DSA_ERR_INVALID_ARG;
+    const bool three = ismem3 <= 232448;
+    auto k = three ? sli_index_kernel<T, 3> : sli_index_kernel<T, 2>;
+    const int smem = three ? ismem3 : ismem2;
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return DSA_ERR_CUDA;
     k<<<dim3((unsigned)a.rows), dim3(kIThreads), smem, stream>>>(im, a);

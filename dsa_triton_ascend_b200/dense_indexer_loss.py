@@ -157,6 +157,48 @@ def dense_lightning_indexer_softmax_lse_triton(
         pre_tokens=pre_tokens, next_tokens=next_tokens)
 
 
+# MQA calls (one key head) whose shapes the SLI kernels take run through them: the dense
+# KL loss over every visible key is the sparse one with the index set 0..S2-1, since the
+# SLI's window keeps the first min(topK, act_k - act_q + s1 + 1) entries of a row
+# (sparse_lightning_indexer_grad_kl_loss_triton.py:74-110) -- exactly the keys the dense
+# reference sees (dense_loss_backward_triton.py:182-397) -- and the student softmax it
+# forms over that set is the one the dense index statistics describe.  The tensor-core
+# kernels then do the work; other shapes use the kernels of csrc/dense.cu.
+_SLI_MAX_KEYS = 8192
+
+
+def _full_query_lengths(actual_seq_qlen, S1):
+    """True when no query row lies past its batch's actual length (the SLI window does not
+    drop such rows; the dense loss gives them nothing)."""
+    if actual_seq_qlen is None:
+        return True
+    if isinstance(actual_seq_qlen, int):
+        return actual_seq_qlen == S1
+    if isinstance(actual_seq_qlen, (list, tuple)):
+        return all(int(x) == S1 for x in actual_seq_qlen)
+    return False
+
+
+def _sli_route_ok(query, key, query_index, N2, D, N1, actual_seq_qlen):
+    Ni, Di = query_index.shape[2], query_index.shape[3]
+    return (N2 == 1 and Di == 128 and Ni <= 64 and N1 <= 128 and D in (128, 256, 512)
+            and key.shape[1] <= _SLI_MAX_KEYS and query.dtype in (torch.bfloat16, torch.float16)
+            and _full_query_lengths(actual_seq_qlen, query.shape[1]))
+
+
+def _dense_via_sli(query, key, query_index, key_index, weights, softmax_max, softmax_sum,
+                   scale_value, query_rope, key_rope, act_q, act_k):
+    from .sparse_lightning_indexer_grad_kl_loss import sparse_lightning_indexer_grad_kl_loss_triton
+    B, S1 = query.shape[0], query.shape[1]
+    S2 = key.shape[1]
+    ids = torch.arange(S2, dtype=torch.int32, device=query.device)
+    si = ids.view(1, 1, 1, S2).expand(B, S1, 1, S2)
+    return sparse_lightning_indexer_grad_kl_loss_triton(
+        query, key, query_index, key_index, weights, si, softmax_max, softmax_sum,
+        query_rope=query_rope, key_rope=key_rope, actual_seq_qlen=act_q, actual_seq_klen=act_k,
+        scale_value=scale_value, layout="BSND", sparse_mode=3)
+
+
 def dense_loss_backward_triton(
     query, key, query_index, key_index, weights, softmax_max, softmax_sum,
     softmax_max_index=None, softmax_sum_index=None, scale_value=1.0,
@@ -165,7 +207,9 @@ def dense_loss_backward_triton(
 ):
     """Dense indexer KL-loss backward: (dQueryIndex, dKeyIndex, dWeights, loss [1] fp32, the
     KL divergence summed over query rows).  Without softmax_max_index / softmax_sum_index the
-    index statistics are computed first (dense_loss_backward_triton.py:752-814)."""
+    index statistics are computed first (dense_loss_backward_triton.py:752-814).  MQA calls
+    within the SLI kernels' limits run on them (tensor cores); they form the index softmax
+    over the visible keys themselves, which given statistics of the same inputs describe."""
     d_rope = _validate_inputs(query, key, query_index, key_index, weights, softmax_max,
                               softmax_sum, layout, sparse_mode, query_rope, key_rope,
                               pre_tokens, next_tokens)
@@ -177,6 +221,13 @@ def dense_loss_backward_triton(
     S2, N2 = key.shape[1], key.shape[2]
     Di = query_index.shape[3]
     dev = query.device
+    if _sli_route_ok(query, key, query_index, N2, D, N1, actual_seq_qlen):
+        if softmax_max_index is not None and (softmax_max_index.dtype != torch.float32
+                                              or softmax_sum_index.dtype != torch.float32):
+            raise TypeError("softmax_max_index and softmax_sum_index must be float32")
+        return _dense_via_sli(query, key, query_index, key_index, weights, softmax_max,
+                              softmax_sum, scale_value, query_rope, key_rope, actual_seq_qlen,
+                              actual_seq_klen)
     act_q = H.lens_tensor(actual_seq_qlen, B, S1, dev)
     act_k = H.lens_tensor(actual_seq_klen, B, S2, dev)
     q, k, qi, ki, w = (t.contiguous() for t in (query, key, query_index, key_index, weights))

@@ -119,3 +119,44 @@ def test_dense_grad_mqa_bf16_actual_lengths_fp32_weights():
     _close(dw, rdw, "dWeights")
     _close(loss, np.array([rloss]), "loss")
     assert float(dqi[1, 2].abs().max()) == 0.0
+
+
+@pytest.mark.parametrize("D,Ni,dt,rope", [(512, 64, "bf16", True), (128, 32, "fp16", False)])
+def test_dense_grad_mqa_tensor_core_route(D, Ni, dt, rope):
+    """MQA with the SLI kernels' shapes (one key head, D_idx 128, at most 64 index heads):
+    the call runs on the tensor-core SLI kernels over the index set 0..S2-1; it must equal
+    the dense oracle and the CUDA-core dense kernels, with given and with computed index
+    statistics, and with a batch whose keys end early."""
+    import dsa_triton_ascend_b200 as dsa
+    import dsa_triton_ascend_b200.dense_indexer_loss as dil
+    B, S1, S2, N1, N2, Di = 2, 24, 160, 32, 1, 128
+    q, k, qr, kr, qi, ki, w = _inputs(B, S1, S2, N1, N2, D, Ni, Di, dt=dt, seed=11)
+    w = I.randn(np.random.default_rng(12), (B, S1, Ni), "fp32", scale=0.5)
+    if not rope:
+        qr = kr = None
+    act_k = [S2, 150]
+    scale = 1.0 / np.sqrt(D + (64 if rope else 0))
+    smax, ssum = dense.attention_stats(q, k, qr, kr, scale, None, act_k)
+    imax, isum = dense.dense_lse(qi, ki, w, None, act_k)
+    ref = dense.dense_grad(q, k, qr, kr, qi, ki, w, smax, ssum, imax, isum, scale, None, act_k)
+    tq, tk, tqi, tki = (_t(x, dt) for x in (q, k, qi, ki))
+    tw, tsm, tss = _t(w, "fp32"), _t(smax, "fp32"), _t(ssum, "fp32")
+    kw = dict(scale_value=scale, actual_seq_klen=act_k)
+    if rope:
+        kw.update(query_rope=_t(qr, dt), key_rope=_t(kr, dt))
+    assert dil._sli_route_ok(tq, tk, tqi, 1, D, N1, None)
+    mx, sm = dsa.dense_lightning_indexer_softmax_lse_triton(tqi, tki, tw, actual_seq_klen=act_k)
+    got = [dsa.dense_loss_backward_triton(tq, tk, tqi, tki, tw, tsm, tss, **kw),
+           dsa.dense_loss_backward_triton(tq, tk, tqi, tki, tw, tsm, tss, mx, sm, **kw)]
+    saved = dil._SLI_MAX_KEYS
+    try:
+        dil._SLI_MAX_KEYS = 0           # the CUDA-core kernels for the same call
+        cuda_core = dsa.dense_loss_backward_triton(tq, tk, tqi, tki, tw, tsm, tss, **kw)
+    finally:
+        dil._SLI_MAX_KEYS = saved
+    torch.cuda.synchronize()
+    for out in got + [cuda_core]:
+        for g, r, name in zip(out, ref, ("dQueryIndex", "dKeyIndex", "dWeights", "loss")):
+            _close(g, np.atleast_1d(r), name)
+    for g, c in zip(got[0], cuda_core):
+        torch.testing.assert_close(g.float(), c.float(), rtol=2e-2, atol=2e-3)
