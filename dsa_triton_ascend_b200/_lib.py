@@ -62,6 +62,7 @@ class SfaBwdParams(ctypes.Structure):
         ("max_blocks", _i64), ("s2_cap", _i64),
         ("scale", ctypes.c_float), ("sparse_mode", ctypes.c_int32), ("dtype", ctypes.c_int32),
         ("defer_cast", ctypes.c_int32), ("accumulate", ctypes.c_int32),
+        ("teacher", _p),
     ]
 
 
@@ -88,6 +89,7 @@ class SliParams(ctypes.Structure):
         ("batch", _i64), ("s1", _i64), ("s2", _i64), ("n1", _i64), ("d", _i64),
         ("n_index", _i64), ("d_index", _i64), ("topk", _i64),
         ("scale", ctypes.c_float), ("dtype", ctypes.c_int32), ("weights_dtype", ctypes.c_int32),
+        ("teacher", _p),
     ]
 
 

@@ -65,6 +65,7 @@ struct Args {
   float* dk_acc;
   float* dkr_acc;
   float* dv_acc;
+  float* teacher;           // NULL or [num_rows][topk]: (1/N1) sum_h P of each valid entry (K1)
   const int32_t* ws_rows;
   const int32_t* ws_count;
   void* ds;        // [num_rows][kp][128 heads] scratch (key-major), dtype of the inputs
@@ -312,6 +313,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads1, 1)
       const bool valid = e < nvalid;
       uint4* ds_row = reinterpret_cast<uint4*>(static_cast<T*>(a.ds) + ((size_t)row * a.kp + e) * kHeadsPad);
       uint4* p_row = reinterpret_cast<uint4*>(static_cast<T*>(a.pp) + ((size_t)row * a.kp + e) * kHeadsPad);
+      float psum = 0.f;   // sum over this thread's 64 heads of P (fp32, before rounding)
 #pragma unroll 1
       for (int h0 = hbase; h0 < hbase + 64; h0 += 16) {
         uint32_t sr[16], pr[16];
@@ -334,6 +336,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads1, 1)
             p[x] = pe;
             g[x] = valid ? pe * (__uint_as_float(pr[2 * i + x]) - hc.z) * a.scale : 0.f;
           }
+          psum += p[0] + p[1];
           pk_p[i] = ElemTraits<T>::pack2(p[0], p[1]);
           pk_s[i] = ElemTraits<T>::pack2(g[0], g[1]);
         }
@@ -341,6 +344,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads1, 1)
         st_global_v8(ds_row + h0 / 8, pk_s);
         st_global_v8(p_row + h0 / 8, pk_p);
       }
+      // the indexer loss's teacher: (1/N1) sum_h P; the two head halves of a key add theirs
+      if (a.teacher != nullptr && valid && !wfail)
+        atomicAdd(a.teacher + (size_t)row * a.topk + e, psum * (1.f / (float)a.N1));
       tc_fence_before();
       named_bar(1, 32 * kElemWarps1);
       if (warp == 2 && lane == 0) mbar_arrive_cluster(b ? lead_f1 : lead_f0);
@@ -1024,6 +1030,7 @@ int launch(const DsaSfaBwdParams* p, cudaStream_t stream) {
   a.dk_acc = p->dk_acc;
   a.dkr_acc = p->dkr_acc;
   a.dv_acc = p->dv_acc;
+  a.teacher = p->teacher;
   a.err = p->error_flag;
   char* ws = static_cast<char*>(p->workspace);
   a.ws_rows = reinterpret_cast<const int32_t*>(ws);
@@ -1123,6 +1130,7 @@ extern "C" int dsa_sfa_bwd(const DsaSfaBwdParams* p, void* stream_) {
       !p->dk_acc || !p->dkr_acc || (!p->dv_acc && p->dv))
     return DSA_ERR_INVALID_ARG;
   if (!p->block_table && !p->k_row_base) return DSA_ERR_INVALID_ARG;
+  if (p->teacher && p->sparse_block_size != 1) return DSA_ERR_INVALID_ARG;
   if (!p->workspace || (reinterpret_cast<uintptr_t>(p->workspace) & 255u) != 0 ||
       p->workspace_bytes < dsa_sfa_bwd_workspace_size(p->num_rows, p->topk, p->sparse_block_size))
     return DSA_ERR_INVALID_ARG;

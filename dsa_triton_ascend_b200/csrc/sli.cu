@@ -702,7 +702,9 @@ int launch(const DsaSliParams* p, cudaStream_t stream) {
   a.ssum = p->softmax_sum;
   a.act_q = p->act_q;
   a.act_k = p->act_k;
-  a.p = static_cast<float*>(p->workspace);
+  // the teacher distribution: a caller's (e.g. from the attention backward), else this
+  // call's own teacher pass writes it into the workspace
+  a.p = p->teacher ? const_cast<float*>(p->teacher) : static_cast<float*>(p->workspace);
   a.dqi = p->d_query_index;
   a.dki_acc = p->dki_acc;
   a.dw = p->d_weights;
@@ -735,7 +737,7 @@ int launch(const DsaSliParams* p, cudaStream_t stream) {
   if (cudaMemsetAsync(p->dki_acc, 0, sizeof(float) * krows * kDi, stream) != cudaSuccess ||
       cudaMemsetAsync(p->loss, 0, sizeof(float), stream) != cudaSuccess)
     return DSA_ERR_CUDA;
-  {
+  if (!p->teacher) {
     auto k = sli_teacher_kernel<D, T>;
     const int smem = TCfg<D>::kOffBars + (int)sizeof(TBars);
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
@@ -772,12 +774,13 @@ extern "C" int dsa_sli_grad(const DsaSliParams* p, void* stream_) {
   if (!p || !p->query || !p->key || !p->query_rope || !p->key_rope || !p->query_index ||
       !p->key_index || !p->weights || !p->sparse_indices || !p->softmax_max || !p->softmax_sum ||
       !p->act_q || !p->act_k || !p->d_query_index || !p->d_weights || !p->dki_acc || !p->loss ||
-      !p->workspace)
+      (!p->workspace && !p->teacher))
     return DSA_ERR_INVALID_ARG;
   if (p->batch < 1 || p->s1 < 1 || p->s2 < 1 || p->n1 < 1 || p->n1 > 128 || p->n_index < 1 ||
       p->n_index > kNip || p->d_index != kDi || p->topk < 1 || p->topk > 8192)
     return DSA_ERR_INVALID_ARG;
-  if (p->workspace_bytes < dsa_sli_workspace_size(p->batch, p->s1, p->topk)) return DSA_ERR_INVALID_ARG;
+  if (!p->teacher && p->workspace_bytes < dsa_sli_workspace_size(p->batch, p->s1, p->topk))
+    return DSA_ERR_INVALID_ARG;
   const int D = (int)p->d;
   if (p->dtype == DSA_DTYPE_BF16) {
     if (D == 512) return launch<512, __nv_bfloat16>(p, stream);

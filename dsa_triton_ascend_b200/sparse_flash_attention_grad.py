@@ -25,7 +25,8 @@ _VALID_N1 = (1, 2, 4, 8, 16, 32, 64, 128)
 def _sfa_grad(query, key, value, sparse_indices, d_out, out, softmax_max, softmax_sum,
               scale_value, query_rope, key_rope, actual_seq_lengths_query,
               actual_seq_lengths_kv, sparse_block_size, layout, sparse_mode, pre_tokens,
-              next_tokens, deterministic, defer_cast, accumulators=None, merged=False):
+              next_tokens, deterministic, defer_cast, accumulators=None, merged=False,
+              teacher=None):
     # guards: sparse_flash_attention_grad_triton.py:428-438
     if pre_tokens != INT64_MAX or next_tokens != INT64_MAX:
         raise ValueError("pre_tokens/next_tokens only support default INT64_MAX")
@@ -140,6 +141,12 @@ def _sfa_grad(query, key, value, sparse_indices, d_out, out, softmax_max, softma
     p.dtype = H.dtype_code(query)
     p.defer_cast = 1 if defer_cast else 0
     p.accumulate = 0 if accumulators is None else 1
+    if teacher is not None:
+        # fp32 [num_rows, topk], zeroed: K1 adds (1/N1) sum_h P of each valid entry
+        if (teacher.dtype != torch.float32 or not teacher.is_contiguous()
+                or teacher.numel() != num_rows * topk or int(sparse_block_size) != 1):
+            raise ValueError("teacher must be a contiguous fp32 [rows, topk] buffer (block size 1)")
+        p.teacher = ptr(teacher)
     check(lib().dsa_sfa_bwd(p, stream_ptr(dev)), "dsa_sfa_bwd")
     if defer_cast:
         def finish():

@@ -57,7 +57,7 @@ def sparse_lightning_indexer_grad_kl_loss_partial(
 
 def _sli(query, key, query_index, key_index, weights, sparse_indices, softmax_max, softmax_sum,
          query_rope, key_rope, actual_seq_qlen, actual_seq_klen, scale_value, layout,
-         sparse_mode, defer_cast):
+         sparse_mode, defer_cast, teacher=None):
     # guards: sparse_lightning_indexer_grad_kl_loss_triton.py:534-538
     if layout != "BSND":
         raise ValueError("Only BSND layout is supported in triton path")
@@ -102,8 +102,16 @@ def _sli(query, key, query_index, key_index, weights, sparse_indices, softmax_ma
     flat = torch.empty(nk + 4, dtype=torch.float32, device=dev)
     dki_acc = flat[:nk].view(B * S2, Di)
     loss = flat[nk:nk + 1]
-    ws_bytes = lib().dsa_sli_workspace_size(B, S1, topk)
-    ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=dev)
+    if teacher is not None:
+        # the attention backward's (1/N1) sum_h P per entry: no teacher pass, no workspace
+        if (teacher.dtype != torch.float32 or not teacher.is_contiguous()
+                or teacher.numel() != B * S1 * topk):
+            raise ValueError("teacher must be a contiguous fp32 [B*S1, topk] buffer")
+        ws_bytes = 0
+        ws = torch.empty(4, dtype=torch.uint8, device=dev)
+    else:
+        ws_bytes = lib().dsa_sli_workspace_size(B, S1, topk)
+        ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=dev)
     p = SliParams()
     p.query, p.key, p.query_rope, p.key_rope = ptr(q), ptr(k), ptr(qr), ptr(kr)
     p.query_index, p.key_index, p.weights = ptr(qi), ptr(ki), ptr(w)
@@ -113,6 +121,7 @@ def _sli(query, key, query_index, key_index, weights, sparse_indices, softmax_ma
     p.dki_acc, p.loss = ptr(dki_acc), ptr(loss)
     p.error_flag = ptr(error_flag(dev))
     p.workspace, p.workspace_bytes = ptr(ws), ws_bytes
+    p.teacher = ptr(teacher) if teacher is not None else 0
     p.batch, p.s1, p.s2, p.n1, p.d = B, S1, S2, N1, D
     p.n_index, p.d_index, p.topk = Ni, Di, topk
     p.scale = float(scale_value)

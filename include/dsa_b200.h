@@ -201,6 +201,11 @@ typedef struct DsaSfaBwdParams {
   int32_t defer_cast;            /* 1: leave the key gradients in the fp32 buffers */
   int32_t accumulate;            /* 1: add into dk_acc / dkr_acc / dv_acc instead of zeroing
                                     them first (query rows processed in several calls) */
+  float* teacher;                /* NULL, or fp32 [num_rows][topk], zeroed by the caller: the
+                                    call adds (1/n1) sum_h P[row, key, h] of each valid entry
+                                    at its place among the row's valid entries -- the
+                                    attention distribution the indexer KL loss takes as its
+                                    teacher (see DsaSliParams.teacher).  sparse_block_size 1. */
 } DsaSfaBwdParams;
 
 int dsa_sfa_bwd(const DsaSfaBwdParams* params, void* stream);
@@ -321,6 +326,11 @@ typedef struct DsaSliParams {
   float scale;
   int32_t dtype;
   int32_t weights_dtype;
+  const float* teacher;          /* NULL, or the teacher distribution p [batch*s1][topk] fp32
+                                    (as dsa_sfa_bwd's teacher output gives it): the call then
+                                    skips its own teacher pass, reads p from here and needs
+                                    no workspace.  Valid when each row's valid entries come
+                                    first in sparse_indices (an indexer top-k row is so). */
 } DsaSliParams;
 
 int dsa_sli_grad(const DsaSliParams* params, void* stream);
