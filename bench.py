@@ -189,12 +189,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="sfa", choices=["sfa", "li", "li_fp8", "decode", "sli", "dense"],
+    ap.add_argument("--workload", default="sfa", choices=["sfa", "li", "li_fp8", "decode", "sli", "dense", "dsa_step"],
                     help="sfa: config 4 forward+backward (the headline); li: config 2 indexer; "
                          "li_fp8: config 2 geometry through the FP8 indexer (e4m3 query / key, "
                          "per-key scales); decode: config 3 paged forward; sli: config 5 "
                          "indexer KL-loss grad; dense: the dense indexer KL loss (every "
-                         "visible key) at config-5 geometry, one key head")
+                         "visible key) at config-5 geometry, one key head; dsa_step: one "
+                         "training step of the indexer -> attention -> KL-loss layer")
     ap.add_argument("--rows", type=int, default=0,
                     help="profiling aid: time only the last ROWS query rows of config 4 "
                          "(each sees the full 2048 keys); 0 = the whole workload")
@@ -625,6 +626,36 @@ def run_other(args, rank, world, local):
         pairs = wd["si"].numel()
         flops, nbytes = pairs * FWD_FLOP_PER_PAIR, pairs * GATHER_BYTES_PER_PAIR
         metric, unit, wl = "SFA decode TFLOP/s", "TFLOP/s", "BASELINE config 3 (PA_BSND, B=32, S1=1, N1=128, top-2048, 16384-block pool)"
+    elif args.workload == "dsa_step":
+        # one training step (forward + backward) of SparseAttentionWithIndexer at config
+        # 4 / 5 geometry: lightning indexer top-2048, sparse attention, indexer KL loss
+        from dsa_triton_ascend_b200.synthetic import sli_prefill
+        w = sli_prefill(device=dev, seed=0)
+        S = w["q"].shape[1]
+        leaves = {n: w[n].clone().requires_grad_(True) for n in ("q", "k", "qr", "kr", "qi", "ki")}
+        leaves["w"] = w["w"].clone().requires_grad_(True)
+        g_out = torch.randn(w["q"].shape, generator=g, device=dev).to(torch.bfloat16)
+        layers = {f: dsa.SparseAttentionWithIndexer(scale_value=w["scale"], sparse_count=2048,
+                                                     teacher_from_backward=f) for f in (False, True)}
+
+        def make_step(fused):
+            def step():
+                for t in leaves.values():
+                    t.grad = None
+                out, loss = layers[fused](leaves["q"], leaves["k"], leaves["qr"], leaves["kr"],
+                                          leaves["qi"], leaves["ki"], leaves["w"])
+                ((out * g_out).float().sum() + loss).backward()
+            return step
+        fn = make_step(False)
+        pairs = int(np.minimum(np.arange(1, S + 1), 2048).sum())   # causal top-2048 pairs
+        lip = S * (S + 1) // 2
+        flops = (lip * 2 * 64 * 128 + pairs * (FWD_FLOP_PER_PAIR + BWD_FLOP_PER_PAIR)
+                 + pairs * 2 * (64 * 128 * 3 + 128 * 576))
+        nbytes = pairs * (GATHER_BYTES_PER_PAIR * 3 + 256)
+        metric, unit, wl = ("DSA layer training step TFLOP/s", "TFLOP/s",
+                            "config 4/5 geometry: indexer top-2048 (64 heads x 128) -> sparse attention "
+                            "(S1=S2=8192, N1=128, D=512+64) fwd + bwd -> indexer KL loss")
+        extra_fns = {"teacher_from_backward": make_step(True)}
     elif args.workload == "dense":
         # config-5 geometry, one key head: the KL loss over every visible key (33.6 M
         # causal pairs); the teacher's softmax statistics are those of full causal attention,
@@ -663,6 +694,11 @@ def run_other(args, rank, world, local):
             timing = f"CUDA events around each call (graph capture failed: {str(e)[:80]})"
     ms = _timed(fn, args.steps, max(args.warmup, 3), stream)
     dsa.check_device_errors(dev)
+    extra = {}
+    for name, f2 in (extra_fns.items() if "extra_fns" in locals() else []):
+        ms2 = _timed(f2, args.steps, max(args.warmup, 3), stream)
+        dsa.check_device_errors(dev)
+        extra[name] = {"ms_per_step": ms2, "value": flops / (ms2 * 1e-3) / 1e12, "unit": unit}
     t_b, t_f = nbytes / (hbm_peak * 1e9), flops / (tf_peak * 1e12)
     bound = "hbm" if t_b >= t_f else "tensor"
     line = {"metric": metric, "value": flops / (ms * 1e-3) / 1e12 * world, "unit": unit,
@@ -677,6 +713,7 @@ def run_other(args, rank, world, local):
                          "frac": max(t_b, t_f) / (ms * 1e-3),
                          "traffic": WORKLOAD_DRAM_BYTES.get(args.workload),
                          "peak_source": peak_kind}}
+    line.update(extra)
     if rank == 0:
         print(json.dumps(line), flush=True)
 
