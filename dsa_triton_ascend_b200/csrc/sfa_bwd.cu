@@ -68,6 +68,7 @@ struct Args {
   float* teacher;           // NULL or [num_rows][topk]: (1/N1) sum_h P of each valid entry (K1)
   const int32_t* ws_rows;
   const int32_t* ws_count;
+  const int4* runs;  // NULL, or [num_rows / 2 rounded up][3] key runs of row pairs (K3 grouped)
   void* ds;        // [num_rows][kp][128 heads] scratch (key-major), dtype of the inputs
   void* pp;        // [num_rows][kp][128 heads]
   const float* delta;   // [num_rows][N1] rowsum(dO * O), from sfa_bwd_delta_kernel
@@ -597,6 +598,160 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
 }
 
 // =====================================================================================
+// Row pairs for K3.  Adjacent query rows share many keys (a causal top-k picks from nearly
+// the same window), and K3 reduces every (row, key) product into the key's fp32 accumulator
+// row.  Grouped, the two rows' products for a shared key are summed in TMEM first (one GEMM
+// with K = 2 x 128 heads) and reach L2 once.  This pass reorders each row's compacted key
+// list into runs -- keys of row 0 only, keys of both rows, keys of row 1 only -- with the
+// shared run listed in the same order in both rows, so that the run's dS / P slots are
+// consecutive in either row's scratch and a K3 tile of it is one TMA box per row.  K1 and
+// K2 take the list in any order.
+// One CTA per pair: a shared-memory hash set of the pair's keys (open addressing) marks each
+// key with the rows that hold it; block scans over the two lists then rank the keys of each
+// run in list order: row 0's keys keep row 0's order (own run, then shared run), row 1 lists
+// the shared run in row 0's order and then its own keys in its own order.  The result
+// depends only on the two lists (not on which thread won a hash slot), so a call is
+// reproducible and a call over a row range that starts on an even row orders every pair as
+// the whole call does.  A pair with an empty row, or whose lists hold a key twice, keeps its
+// order and is described as two unshared runs.
+// runs[pair][r] = (mask of member rows, length, first slot in row 0, first slot in row 1),
+// in the order K3 walks them: row 0 only, shared, row 1 only.
+// =====================================================================================
+constexpr int kGroupThreads = 512;
+
+__device__ __forceinline__ uint32_t group_hash(int k, int lg) {
+  return ((uint32_t)k * 2654435761u) >> (32 - lg);
+}
+
+// shared memory of one pair: keys [H], words [H] (member mask | shared rank << 2), and the
+// table slot of every list entry [H / 2]
+inline int group_smem_bytes(int lg) { return 10 << lg; }
+
+__global__ void __launch_bounds__(kGroupThreads) sfa_bwd_group_kernel(const Args a,
+                                                                      int32_t* ws_rows,
+                                                                      int4* runs, int lg) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ uint64_t warp_sum[kGroupThreads / 32];
+  __shared__ int dup;
+  const int H = 1 << lg;   // >= 2 x the pair's keys: the probe loops end
+  int* keys = reinterpret_cast<int*>(smem_raw);
+  uint32_t* word = reinterpret_cast<uint32_t*>(keys + H);
+  int* slot_of = reinterpret_cast<int*>(word + H);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r0 = 2 * blockIdx.x, r1 = r0 + 1;
+  const size_t nent = (size_t)a.topk * a.block;
+  const bool abort = a.err != nullptr && *reinterpret_cast<volatile int*>(a.err) != 0;
+  auto count = [&](int r) {
+    if (r >= a.num_rows || abort) return 0;
+    const RowInfo ri = row_info(a, r);
+    return ri.active ? __ldg(a.ws_count + r) : 0;
+  };
+  const int n0 = count(r0), n1 = count(r1);
+  int4* out = runs + 3 * blockIdx.x;
+  auto unshared = [&]() {
+    if (threadIdx.x == 0) {
+      out[0] = make_int4(1, n0, 0, 0);
+      out[1] = make_int4(3, 0, 0, 0);
+      out[2] = make_int4(2, n1, 0, 0);
+    }
+  };
+  if (n0 == 0 || n1 == 0 || 2 * (n0 + n1) > H) {   // uniform over the block
+    unshared();
+    return;
+  }
+  for (int i = threadIdx.x; i < H; i += kGroupThreads) {
+    keys[i] = -1;
+    word[i] = 0u;
+  }
+  if (threadIdx.x == 0) dup = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < n0 + n1; i += kGroupThreads) {
+    const int g = i >= n0;
+    const int k = ws_rows[(size_t)(g ? r1 : r0) * nent + (g ? i - n0 : i)];
+    uint32_t h = group_hash(k, lg);
+    for (int probe = 0; probe < H; ++probe) {
+      const int prev = atomicCAS(&keys[h], -1, k);
+      if (prev == -1 || prev == k) {
+        if (atomicOr(&word[h], 1u << g) & (1u << g)) dup = 1;   // listed twice in row g
+        slot_of[i] = (int)h;
+        break;
+      }
+      h = (h + 1) & (uint32_t)(H - 1);
+    }
+  }
+  __syncthreads();
+  if (dup) {   // uniform: read after the barrier
+    unshared();
+    return;
+  }
+  // each thread ranks a contiguous chunk of either list; counts in 16-bit fields: row 0's
+  // own keys (0), row 0's shared keys (1), row 1's own keys (2), each at most 4096
+  const int p0 = (n0 + kGroupThreads - 1) / kGroupThreads;
+  const int p1 = (n1 + kGroupThreads - 1) / kGroupThreads;
+  const int i0 = min(n0, (int)threadIdx.x * p0), i1 = min(n0, i0 + p0);
+  const int j0 = min(n1, (int)threadIdx.x * p1), j1 = min(n1, j0 + p1);
+  uint64_t c = 0;
+  for (int i = i0; i < i1; ++i) c += (word[slot_of[i]] & 3u) == 1u ? 1ull : 1ull << 16;
+  for (int j = j0; j < j1; ++j)
+    if ((word[slot_of[n0 + j]] & 3u) == 2u) c += 1ull << 32;
+  uint64_t v = c;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint64_t y = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += y;
+  }
+  if (lane == 31) warp_sum[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    uint64_t w = lane < kGroupThreads / 32 ? warp_sum[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint64_t y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < kGroupThreads / 32) warp_sum[lane] = w;
+  }
+  __syncthreads();
+  uint64_t e = v - c + (warp > 0 ? warp_sum[warp - 1] : 0);
+  const uint64_t tot = warp_sum[kGroupThreads / 32 - 1];
+  const int c1 = (int)(tot & 0xffff), c3 = (int)((tot >> 16) & 0xffff), c2 = (int)(tot >> 32);
+  // every list entry was read into the table above, so the lists are rewritten in place
+  for (int i = i0; i < i1; ++i) {
+    const int h = slot_of[i];
+    const uint32_t w = word[h];
+    int pos;
+    if ((w & 3u) == 1u) {
+      pos = (int)(e & 0xffff);
+      e += 1;
+    } else {
+      const int r = (int)((e >> 16) & 0xffff);
+      pos = c1 + r;
+      e += 1ull << 16;
+      word[h] = w | ((uint32_t)r << 2);   // row 1 places the key at the same rank
+    }
+    ws_rows[(size_t)r0 * nent + pos] = keys[h];
+  }
+  __syncthreads();
+  for (int j = j0; j < j1; ++j) {
+    const int h = slot_of[n0 + j];
+    const uint32_t w = word[h];
+    int pos;
+    if ((w & 3u) == 2u) {
+      pos = c3 + (int)((e >> 32) & 0xffff);
+      e += 1ull << 32;
+    } else {
+      pos = (int)(w >> 2);
+    }
+    ws_rows[(size_t)r1 * nent + pos] = keys[h];
+  }
+  if (threadIdx.x == 0) {
+    out[0] = make_int4(1, c1, 0, 0);
+    out[1] = make_int4(3, c3, c1, 0);
+    out[2] = make_int4(2, c2, 0, c3);
+  }
+}
+
+// =====================================================================================
 // K3: dK = dS^T Q, dV = P^T dO, dKr = dS^T Qr  (scatter-add into fp32)
 // =====================================================================================
 // Work items are (query row, part) pairs.  Parts split the output columns so that a part's
@@ -619,6 +774,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
 // columns, and each tile runs dS^T Q and then P^T dO into the same TMEM accumulator (two
 // B-ring entries: the dS tile, then the P tile).  Parts per row: D / 256 merged + the
 // rope part; the reductions drop to 4 (D + 64) bytes per valid pair.
+//
+// Grouped mode (runs != NULL, 5-output calls): an item is a pair of adjacent rows and a part,
+// and its tiles walk the pair's three key runs (sfa_bwd_group_kernel).  Slot g holds row g's
+// slice; a tile of the shared run takes two B entries, row 0's dS (or P) tile and then row
+// 1's, into one TMEM accumulator, so a shared key is reduced once for both rows.  A slot is
+// released after the last tile that reads it, so the next item's row-0 slice loads while
+// the row-1-only run still runs.
 //
 // Roles: warp 0 (one lane) loads the item slices into two slots and the dS / P tiles
 // through a 3-stage ring, so the next item's slice arrives while the current item's last
@@ -653,20 +815,100 @@ struct __align__(16) Bars3 {
 
 constexpr int kThreads3 = 18 * 32;   // warp 0: TMA, 1: MMA, 2-17: drain
 
-// One K3 work item; every role walks the same sequence.
+// One K3 work item: a query row (or, grouped, a row pair) and a column part.  Its keys come
+// as up to three runs (mask of member rows, length, first slot in row 0, in row 1); a
+// single row is one run of all its keys.  Every role walks the same sequence.
 struct Item3 {
-  int row, part, nvalid, ntiles;
+  int row0, part, ntiles;
+  int4 r0, r1, r2;   // the runs in walking order
 };
+
+__device__ __forceinline__ int tiles3(int len) { return (len + kKeyTile3 - 1) / kKeyTile3; }
+
+// work items of a call: (rows, or row pairs) x parts
+__device__ __forceinline__ int groups3(const Args& a) {
+  return a.runs != nullptr ? (a.num_rows + 1) / 2 : a.num_rows;
+}
 
 template <int D>
 __device__ __forceinline__ Item3 item3(const Args& a, int it, int nparts) {
   Item3 x;
-  x.row = it / nparts;
+  const int g = it / nparts;
   x.part = it % nparts;
-  const RowInfo ri = row_info(a, x.row);
-  x.nvalid = ri.active ? __ldg(a.ws_count + x.row) : 0;
-  x.ntiles = (x.nvalid + kKeyTile3 - 1) / kKeyTile3;
+  if (a.runs != nullptr) {
+    x.row0 = 2 * g;
+    x.r0 = __ldg(a.runs + 3 * g);
+    x.r1 = __ldg(a.runs + 3 * g + 1);
+    x.r2 = __ldg(a.runs + 3 * g + 2);
+  } else {
+    x.row0 = g;
+    const RowInfo ri = row_info(a, g);
+    x.r0 = make_int4(1, ri.active ? __ldg(a.ws_count + g) : 0, 0, 0);
+    x.r1 = x.r2 = make_int4(0, 0, 0, 0);
+  }
+  x.ntiles = tiles3(x.r0.y) + tiles3(x.r1.y) + tiles3(x.r2.y);
   return x;
+}
+
+// Tile t of an item: member rows, keys (<= 128) and first slot in row 0 / row 1
+struct Tile3 {
+  int mask, len, off0, off1;
+};
+
+__device__ __forceinline__ Tile3 tile3(const Item3& x, int t) {
+  const int n0 = tiles3(x.r0.y), n1 = tiles3(x.r1.y);
+  const bool in2 = t >= n0 + n1, in1 = !in2 && t >= n0;
+  t -= in2 ? n0 + n1 : in1 ? n0 : 0;
+  Tile3 y;
+  y.mask = in2 ? x.r2.x : in1 ? x.r1.x : x.r0.x;
+  y.len = min(kKeyTile3, (in2 ? x.r2.y : in1 ? x.r1.y : x.r0.y) - kKeyTile3 * t);
+  y.off0 = (in2 ? x.r2.z : in1 ? x.r1.z : x.r0.z) + kKeyTile3 * t;
+  y.off1 = (in2 ? x.r2.w : in1 ? x.r1.w : x.r0.w) + kKeyTile3 * t;
+  return y;
+}
+
+// Grouped mode: the last tile of the item that reads row g (-1: the row has no keys)
+__device__ __forceinline__ int last_tile3(const Item3& x, int g) {
+  int end = tiles3(x.r0.y), last = ((x.r0.x >> g) & 1) && x.r0.y > 0 ? end - 1 : -1;
+  end += tiles3(x.r1.y);
+  if (((x.r1.x >> g) & 1) && x.r1.y > 0) last = end - 1;
+  end += tiles3(x.r2.y);
+  if (((x.r2.x >> g) & 1) && x.r2.y > 0) last = end - 1;
+  return last;
+}
+
+// The B entries of a tile: A slot, first scratch row (key slot) of the 128-key box, P or dS.
+struct Entry3 {
+  int slot, srow;
+  bool p;
+};
+
+__device__ __forceinline__ int entries3(const Args& a, const Item3& x, const Tile3& y, bool mixed,
+                                        bool is_dv, int ab1, Entry3 (&en)[2]) {
+  if (mixed) {   // merged part: the dS tile (slot 0, Q), then the P tile (slot 1, dO)
+    en[0] = {0, x.row0 * a.kp + y.off0, false};
+    en[1] = {1, x.row0 * a.kp + y.off0, true};
+    return 2;
+  }
+  if (a.runs == nullptr) {
+    en[0] = {ab1, x.row0 * a.kp + y.off0, is_dv};
+    return 1;
+  }
+  const Entry3 e1 = {1, (x.row0 + 1) * a.kp + y.off1, is_dv};
+  en[0] = (y.mask & 1) ? Entry3{0, x.row0 * a.kp + y.off0, is_dv} : e1;
+  en[1] = e1;
+  return (y.mask & 1) + ((y.mask >> 1) & 1);
+}
+
+// The A slots an item loads (bit s: slot s) and, per slot, its last reading tile.
+__device__ __forceinline__ int slots3(const Args& a, const Item3& x, bool mixed, int ab1,
+                                      int (&last)[2]) {
+  last[0] = last[1] = x.ntiles - 1;
+  if (mixed) return 3;
+  if (a.runs == nullptr) return 1 << ab1;
+  last[0] = last_tile3(x, 0);
+  last[1] = last_tile3(x, 1);
+  return (last[0] >= 0 ? 1 : 0) | (last[1] >= 0 ? 2 : 0);
 }
 
 // What a part computes: rope (dKr: Qr and dS), dK (Q, dS), dV (dO, P) or, merged, dK + dV
@@ -752,7 +994,7 @@ __global__ void __launch_bounds__(kThreads3, 1)
   const bool abort = a.err != nullptr && *reinterpret_cast<volatile int*>(a.err) != 0;
   const bool merged = a.dv_acc == nullptr;
   const int nparts = merged ? C::kDParts + 1 : C::kParts;
-  const int nitems = abort ? 0 : a.num_rows * nparts;
+  const int nitems = abort ? 0 : groups3(a) * nparts;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2; ++s) {
@@ -785,33 +1027,39 @@ __global__ void __launch_bounds__(kThreads3, 1)
         const Item3 x = item3<D>(a, it, nparts);
         if (x.ntiles == 0) continue;
         const Part3 pk = part3<D>(x.part, merged);
-        // slots: a merged part fills both (Q, dO); otherwise one, alternating per item
-        const int nsl = pk.mixed ? 2 : 1;
-        for (int h = 0; h < nsl; ++h) {
-          const int ab = pk.mixed ? h : (merged ? 0 : (ni & 1));
+        // slots: a merged part fills both (Q, dO); a grouped item one per member row with
+        // keys; otherwise one, alternating per item
+        const int ab1 = merged ? 0 : (ni & 1);
+        int last[2];
+        const int used = slots3(a, x, pk.mixed, ab1, last);
+        for (int ab = 0; ab < 2; ++ab) {
+          if (!((used >> ab) & 1)) continue;
           const CUtensorMap* am = pk.rope ? &maps.qr
-                                  : (pk.is_dv || (pk.mixed && h == 1)) ? &maps.dout : &maps.q;
+                                  : (pk.is_dv || (pk.mixed && ab == 1)) ? &maps.dout : &maps.q;
+          const int qrow = x.row0 + (a.runs != nullptr ? ab : 0);
           if (!mbar_wait_sleep(smem_u32(&bars.a_empty[ab]), ((ab ? ua1 : ua0) & 1) ^ 1, a.err, &failed))
             break;
           const uint32_t fb = smem_u32(&bars.a_full[ab]);
           mbar_arrive_expect_tx(fb, pk.nbox * C::kBox);
           for (int c = 0; c < pk.nbox; ++c)
-            tma_load_2d(sA + ab * C::kSlice + c * C::kBox, am, fb, pk.col0 + 64 * c, x.row * a.N1);
+            tma_load_2d(sA + ab * C::kSlice + c * C::kBox, am, fb, pk.col0 + 64 * c, qrow * a.N1);
           if (ab) ++ua1; else ++ua0;
         }
         if (failed) break;
-        const int krow0 = x.row * a.kp;   // first scratch row (key slot) of this query row
         for (int t = 0; t < x.ntiles && !failed; ++t) {
-          for (int e = 0; e < nsl; ++e) {   // the tile's dS entry, then (merged) its P entry
-            const CUtensorMap* bm = (pk.is_dv || e == 1) ? &maps.pp : &maps.ds;
+          Entry3 en[2];
+          const int ne = entries3(a, x, tile3(x, t), pk.mixed, pk.is_dv, ab1, en);
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            if (e >= ne) break;
+            const CUtensorMap* bm = en[e].p ? &maps.pp : &maps.ds;
             const int s = nb % kStages3;
             if (!mbar_wait_sleep(smem_u32(&bars.b_empty[s]), ((nb / kStages3) & 1) ^ 1, a.err, &failed))
               break;
             const uint32_t fb = smem_u32(&bars.b_full[s]);
             mbar_arrive_expect_tx(fb, C::kTileB);
-            for (int c = 0; c < 2; ++c)   // heads [64c, 64c+64) of the tile's 128 keys
-              tma_load_2d(sB + s * C::kTileB + c * kKeyTile3 * 128, bm, fb, 64 * c,
-                          krow0 + t * kKeyTile3);
+            for (int c = 0; c < 2; ++c)   // heads [64c, 64c+64) of the tile's 128 key slots
+              tma_load_2d(sB + s * C::kTileB + c * kKeyTile3 * 128, bm, fb, 64 * c, en[e].srow);
             ++nb;
           }
         }
@@ -840,19 +1088,24 @@ __global__ void __launch_bounds__(kThreads3, 1)
         if (x.ntiles == 0) continue;
         const Part3 pk = part3<D>(x.part, merged);
         const int nblk = pk.rope ? 1 : C::kW / 128;
-        const int nsl = pk.mixed ? 2 : 1;
         const int ab1 = merged ? 0 : (ni & 1);   // the slot of a single-slot part
-        for (int h = 0; h < nsl; ++h) {
-          const int ab = pk.mixed ? h : ab1;
-          mbar_wait_spin(smem_u32(&bars.a_full[ab]), (ab ? ua1 : ua0) & 1, a.err, &failed);
-        }
-        if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
+        int last[2];
+        const int used = slots3(a, x, pk.mixed, ab1, last);
+        int waited = 0;   // slots whose slice this item has seen land
         for (int t = 0; t < x.ntiles; ++t) {
           const int tb = nt & 1;
+          Entry3 en[2];
+          const int ne = entries3(a, x, tile3(x, t), pk.mixed, pk.is_dv, ab1, en);
           mbar_wait_spin(smem_u32(&bars.t_empty[tb]), ((nt >> 1) & 1) ^ 1, a.err, &failed);
-          for (int e = 0; e < nsl; ++e) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            if (e >= ne) break;
             const int s = nb % kStages3;
-            const int ab = pk.mixed ? e : ab1;
+            const int ab = en[e].slot;
+            if (!((waited >> ab) & 1)) {
+              mbar_wait_spin(smem_u32(&bars.a_full[ab]), (ab ? ua1 : ua0) & 1, a.err, &failed);
+              waited |= 1 << ab;
+            }
             mbar_wait_spin(smem_u32(&bars.b_full[s]), (nb / kStages3) & 1, a.err, &failed);
             if (__any_sync(0xffffffffu, failed)) { failed = true; break; }
             tc_fence_after();
@@ -869,9 +1122,9 @@ __global__ void __launch_bounds__(kThreads3, 1)
                               (e | k) != 0);
               }
               umma_commit(smem_u32(&bars.b_empty[s]));
-              if (e == nsl - 1) umma_commit(smem_u32(&bars.t_full[tb]));
+              if (e == ne - 1) umma_commit(smem_u32(&bars.t_full[tb]));
               // the slot's last reads of this item: free it for the next item's slice
-              if (t == x.ntiles - 1) umma_commit(smem_u32(&bars.a_empty[ab]));
+              if (t == (ab ? last[1] : last[0])) umma_commit(smem_u32(&bars.a_empty[ab]));
             }
             __syncwarp();
             ++nb;
@@ -880,9 +1133,8 @@ __global__ void __launch_bounds__(kThreads3, 1)
           ++nt;
         }
         if (failed) break;
-        for (int h = 0; h < nsl; ++h) {
-          if (pk.mixed ? h : ab1) ++ua1; else ++ua0;
-        }
+        if (used & 1) ++ua0;
+        if (used & 2) ++ua1;
         ++ni;
       }
       // the MMAs issued last complete before the exit (their TMEM is freed afterwards)
@@ -910,12 +1162,15 @@ __global__ void __launch_bounds__(kThreads3, 1)
       const int mblk = c_off >> 7, key0 = c_off & 127;
       const bool lanes_ok = !rope || q < 2;   // rope: 64 output columns
       float* gcol = acc + col0 + mblk * 128 + 32 * q + lane - (lane & 1);
-      const int32_t* rows = a.ws_rows + (size_t)x.row * a.topk * a.block;
-      // accumulator rows of the share's keys of tile t (-1: no key)
+      const size_t nent = (size_t)a.topk * a.block;
+      // accumulator rows of the share's keys of tile t (-1: no key); the keys of a tile are
+      // listed in the key list of any of its member rows (the first)
       auto load_rows = [&](int t, int (&r)[2]) {
-        const int k0 = t * kKeyTile3 + key0;
-        r[0] = k0 + lane < x.nvalid ? __ldg(rows + k0 + lane) : -1;
-        r[1] = nk == 64 && k0 + 32 + lane < x.nvalid ? __ldg(rows + k0 + 32 + lane) : -1;
+        const Tile3 y = tile3(x, t);
+        const int g0 = (y.mask & 1) ? 0 : 1;
+        const int32_t* rows = a.ws_rows + (size_t)(x.row0 + g0) * nent + (g0 ? y.off1 : y.off0);
+        r[0] = key0 + lane < y.len ? __ldg(rows + key0 + lane) : -1;
+        r[1] = nk == 64 && key0 + 32 + lane < y.len ? __ldg(rows + key0 + 32 + lane) : -1;
       };
       int kr[2];
       load_rows(0, kr);
@@ -994,6 +1249,16 @@ inline int sm_count() {
 // key slots per row in the P / dS scratch: whole K1 pair tiles (256 keys)
 inline int64_t padded_keys(int64_t nent) { return (nent + 255) / 256 * 256; }
 inline int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
+// run table of the row pairs (K3 grouped mode)
+inline int64_t runs_bytes(int64_t num_rows) { return align256((num_rows + 1) / 2 * 3 * 16); }
+// hash table of one row pair (log2 of its entries): at least twice the pair's keys; pairs of
+// longer key lists than kGroupMaxKeys per row stay ungrouped
+constexpr int64_t kGroupMaxKeys = 4096;
+inline int group_lg(int64_t nent) {
+  int lg = 10;
+  while ((int64_t(1) << lg) < 4 * nent) ++lg;
+  return lg;
+}
 
 template <int D, typename T>
 int launch(const DsaSfaBwdParams* p, cudaStream_t stream) {
@@ -1042,6 +1307,12 @@ int launch(const DsaSfaBwdParams* p, cudaStream_t stream) {
   a.pp = ws;
   ws += align256(p->num_rows * kHeadsPad * kp * 2);
   a.delta = reinterpret_cast<const float*>(ws);
+  ws += align256(4 * p->num_rows * kHeadsPad);
+  // row pairs share their keys' reductions in K3 (5-output calls; the merged mode's two
+  // slots already hold Q and dO, and the teacher is indexed by the untouched key order)
+  const bool grouped = p->dv_acc != nullptr && p->teacher == nullptr && p->num_rows >= 2 &&
+                       nent <= kGroupMaxKeys;
+  a.runs = grouped ? reinterpret_cast<const int4*>(ws) : nullptr;
   a.kp = (int)kp;
 
   Maps1 m1;
@@ -1073,6 +1344,17 @@ int launch(const DsaSfaBwdParams* p, cudaStream_t stream) {
     return DSA_ERR_CUDA;
   launch_prep(a, const_cast<int32_t*>(a.ws_rows), const_cast<int32_t*>(a.ws_count), p->num_rows,
               stream);
+  if (grouped) {
+    const int lg = group_lg(nent);
+    const int smem = group_smem_bytes(lg);
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(sfa_bwd_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem) != cudaSuccess)
+      return DSA_ERR_CUDA;
+    sfa_bwd_group_kernel<<<dim3((unsigned)((p->num_rows + 1) / 2)), dim3(kGroupThreads), smem,
+                           stream>>>(a, const_cast<int32_t*>(a.ws_rows), const_cast<int4*>(a.runs),
+                                     lg);
+  }
   {
     const int64_t n = p->num_rows * p->n1;
     sfa_bwd_delta_kernel<D, T><<<dim3((unsigned)((n + 7) / 8)), dim3(256), 0, stream>>>(
@@ -1099,7 +1381,9 @@ int launch(const DsaSfaBwdParams* p, cudaStream_t stream) {
     const int smem = Cfg3<D>::kOffBars + (int)sizeof(Bars3);
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
       return DSA_ERR_CUDA;
-    const int64_t items = p->num_rows * (p->dv_acc ? Cfg3<D>::kParts : Cfg3<D>::kDParts + 1);
+    // the kernel walks the same count (groups3)
+    const int64_t groups = grouped ? (p->num_rows + 1) / 2 : p->num_rows;
+    const int64_t items = groups * (p->dv_acc ? Cfg3<D>::kParts : Cfg3<D>::kDParts + 1);
     const int grid = (int)(items < sm_count() ? items : sm_count());
     k<<<dim3((unsigned)grid), dim3(kThreads3), smem, stream>>>(m3, a);
   }
@@ -1116,7 +1400,8 @@ extern "C" int64_t dsa_sfa_bwd_workspace_size(int64_t num_rows, int64_t topk, in
   if (num_rows < 0 || topk < 0 || sparse_block_size < 1) return -1;
   const int64_t nent = topk * sparse_block_size;
   return align256(4 * num_rows * nent) + align256(4 * num_rows) +
-         2 * align256(num_rows * kHeadsPad * padded_keys(nent) * 2) + align256(4 * num_rows * kHeadsPad);
+         2 * align256(num_rows * kHeadsPad * padded_keys(nent) * 2) + align256(4 * num_rows * kHeadsPad) +
+         runs_bytes(num_rows);
 }
 
 extern "C" int dsa_sfa_bwd(const DsaSfaBwdParams* p, void* stream_) {

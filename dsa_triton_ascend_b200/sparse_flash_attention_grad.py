@@ -26,7 +26,7 @@ def _sfa_grad(query, key, value, sparse_indices, d_out, out, softmax_max, softma
               scale_value, query_rope, key_rope, actual_seq_lengths_query,
               actual_seq_lengths_kv, sparse_block_size, layout, sparse_mode, pre_tokens,
               next_tokens, deterministic, defer_cast, accumulators=None, merged=False,
-              teacher=None):
+              teacher=None, workspace=None):
     # guards: sparse_flash_attention_grad_triton.py:428-438
     if pre_tokens != INT64_MAX or next_tokens != INT64_MAX:
         raise ValueError("pre_tokens/next_tokens only support default INT64_MAX")
@@ -119,7 +119,12 @@ def _sfa_grad(query, key, value, sparse_indices, d_out, out, softmax_max, softma
         kshape, dtype=value.dtype if value is not None else key.dtype, device=dev)
     dkr = torch.empty(key_rope.shape, dtype=key_rope.dtype, device=dev)
     ws_bytes = lib().dsa_sfa_bwd_workspace_size(num_rows, topk, int(sparse_block_size))
-    ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=dev)
+    if workspace is None:
+        ws = torch.empty(max(ws_bytes, 4), dtype=torch.uint8, device=dev)
+    else:   # caller-owned (a test reads the key lists and row-pair runs back from it)
+        if workspace.dtype != torch.uint8 or workspace.numel() < ws_bytes or workspace.device != dev:
+            raise ValueError(f"workspace must be a uint8 tensor of >= {ws_bytes} bytes on the query's device")
+        ws = workspace
 
     p = SfaBwdParams()
     p.q, p.q_rope, p.key, p.key_rope = ptr(q), ptr(qr), ptr(k), ptr(kr)

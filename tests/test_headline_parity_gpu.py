@@ -106,7 +106,9 @@ def test_config4_geometry_key_gradients_in_full():
                                     sparse_mode=3, rounding="kernel", round_out=False)
     assert_close(_np(mdkv), sfa.round_to(fdk + fdv, "bf16"), what="dk + dv")
     assert_close(_np(mdkr), ref[4], what="dk_rope (merged call)")
-    np.testing.assert_array_equal(_np(mdq), _np(grads[0]))
+    # the 5-output call reorders row pairs' key lists (K3's shared-key runs): dQ sums the same
+    # key terms in another order
+    assert_close(_np(mdq), _np(grads[0]), what="dq (merged call vs 5-output call)")
 
 
 def test_config3_decode_real_shape_all_rows():
