@@ -36,16 +36,35 @@ GATHER_BYTES_PER_PAIR = (D + DR) * 2                           # one bf16 key ro
 # backward, roofline bytes by the north-star definition (gathered bytes at HBM): the key row
 # gathered twice, for the scores (K1) and for dQ (K2)
 BWD_BYTES_PER_PAIR = 2 * GATHER_BYTES_PER_PAIR
-# backward: the fp32 dK / dKr / dV scatter-add of every pair, into accumulators that stay in
-# L2 (35.7 MB at config 4); reported beside the roofline, not in it
-BWD_SCATTER_BYTES_PER_PAIR = 4 * (2 * D + DR)
+# backward: the fp32 dK / dKr / dV scatter-add into accumulators that stay in L2 (35.7 MB at
+# config 4), per reduced key row (a key that both rows of a row pair select is reduced once);
+# reported beside the roofline, not in it
+BWD_SCATTER_BYTES_PER_KEY_ROW = 4 * (2 * D + DR)
+
+
+def reduced_key_rows(si_rows):
+    """Key rows the backward's fp32 scatter reduces in one 5-output call over these query
+    rows ([rows, topk] ids, -1 = none): the library pairs rows (2j, 2j+1) of the call and
+    reduces a key both select once, so a pair costs |keys(2j) U keys(2j+1)| and an unpaired
+    last row its own keys (the synthetic ids of a row are distinct)."""
+    import torch
+    R, K = si_rows.shape
+    P = R // 2
+    s = torch.sort(si_rows[: 2 * P].reshape(P, 2 * K), dim=1).values
+    valid = s >= 0
+    dup = (s[:, 1:] == s[:, :-1]) & valid[:, 1:]
+    n = int(valid.sum()) - int(dup.sum())
+    if R % 2:
+        n += int((si_rows[-1] >= 0).sum())
+    return n
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per valid pair, from one
 # `ncu --set full` capture of the last 256 query rows of config 4 (524,288 pairs; command and
 # figures in profiles/sfa_kernels_config4_rows256_full.md), scaled to a launch by its pairs.
-# Backward: K1 + K2 + K3, plus the delta kernel's read of dO and O (2 x N1 x D x 2 B a row).
-# Build of the capture: the kernels of commit cb19fcd.
+# Backward: K1 + K2 + the row-pair pass + K3, plus the delta kernel's read of dO and O
+# (2 x N1 x D x 2 B a row).  Builds of the captures: the forward, K1 and K2 of commit cb19fcd;
+# the row-pair pass and K3 of commit d917068 (profiles/sfa_bwd_dkv_reductions.md).
 PROFILE_PAIRS = 524288
-BWD_DRAM_BYTES_PER_PAIR = (103.11 + 218.89 + 146.14 + 19.40 + 398.23 + 30.89) * 1e6 / PROFILE_PAIRS
+BWD_DRAM_BYTES_PER_PAIR = (103.11 + 218.89 + 146.14 + 19.40 + 2.12 + 476.91 + 39.97) * 1e6 / PROFILE_PAIRS
 BWD_DRAM_BYTES_PER_ROW = 2 * N1 * D * 2
 FWD_DRAM_BYTES_PER_PAIR = (49.35 + 1.95) * 1e6 / PROFILE_PAIRS
 # DRAM traffic of one call of each secondary workload at the size bench.py runs, from one ncu
@@ -234,6 +253,7 @@ def main():
     q = w["q"][:, r0:r1].contiguous()
     qr = w["qr"][:, r0:r1].contiguous()
     si = w["si"][:, r0:r1].contiguous()
+    red_rows = reduced_key_rows(si.reshape(-1, si.shape[-1]))
     k, kr, scale = w["k"], w["kr"], w["scale"]
     dout = dout_full[:, r0:r1].contiguous()
     aq = [shard_act_q(S1, r0)]   # see dsa_triton_ascend_b200/sharding.py
@@ -437,10 +457,13 @@ def main():
             "fwd_tflops": total_pairs * FWD_FLOP_PER_PAIR / (fwd_ms * 1e-3) / 1e12 if world == 1 else None,
             "bwd_tflops": total_pairs * BWD_FLOP_PER_PAIR / (bwd_ms * 1e-3) / 1e12 if world == 1 else None,
             "fwd_roofline_frac": fwd_roof_frac,
-            "bwd_scatter": {"bytes_per_pair": BWD_SCATTER_BYTES_PER_PAIR,
-                            "bytes_per_step": my_pairs * BWD_SCATTER_BYTES_PER_PAIR,
-                            "target": "fp32 key-gradient accumulators, L2-resident",
-                            "gbs_over_bwd": my_pairs * BWD_SCATTER_BYTES_PER_PAIR / ((bwd_ms - ar_ms) * 1e-3) / 1e9},
+            "bwd_scatter": {"bytes_per_key_row": BWD_SCATTER_BYTES_PER_KEY_ROW,
+                            "key_rows_per_step": red_rows,
+                            "pairs_per_step": my_pairs,
+                            "bytes_per_step": red_rows * BWD_SCATTER_BYTES_PER_KEY_ROW,
+                            "target": "fp32 key-gradient accumulators, L2-resident; a key both "
+                                      "rows of a row pair select is reduced once",
+                            "gbs_over_bwd": red_rows * BWD_SCATTER_BYTES_PER_KEY_ROW / ((bwd_ms - ar_ms) * 1e-3) / 1e9},
             "merged_key_grad": {
                 "bwd_ms": bwd_merged_ms,
                 "step_ms": fwd_ms + bwd_merged_ms,
