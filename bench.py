@@ -37,26 +37,27 @@ GATHER_BYTES_PER_PAIR = (D + DR) * 2                           # one bf16 key ro
 # gathered twice, for the scores (K1) and for dQ (K2)
 BWD_BYTES_PER_PAIR = 2 * GATHER_BYTES_PER_PAIR
 # backward: the fp32 dK / dKr / dV scatter-add into accumulators that stay in L2 (35.7 MB at
-# config 4), per reduced key row (a key that both rows of a row pair select is reduced once);
+# config 4), per reduced key row (a key that several rows of a row group select is reduced
+# once);
 # reported beside the roofline, not in it
 BWD_SCATTER_BYTES_PER_KEY_ROW = 4 * (2 * D + DR)
 
 
-def reduced_key_rows(si_rows):
+def reduced_key_rows(si_rows, group=4):
     """Key rows the backward's fp32 scatter reduces in one 5-output call over these query
-    rows ([rows, topk] ids, -1 = none): the library pairs rows (2j, 2j+1) of the call and
-    reduces a key both select once, so a pair costs |keys(2j) U keys(2j+1)| and an unpaired
-    last row its own keys (the synthetic ids of a row are distinct)."""
+    rows ([rows, topk] ids, -1 = none): the library groups `group` adjacent rows of the call
+    (four at D = 512 with top-2048) and reduces a key the group's rows share once, so a group
+    costs the size of the union of its rows' keys (the synthetic ids of a row are distinct)."""
     import torch
     R, K = si_rows.shape
-    P = R // 2
-    s = torch.sort(si_rows[: 2 * P].reshape(P, 2 * K), dim=1).values
+    pad = (-R) % group
+    if pad:
+        si_rows = torch.cat([si_rows, si_rows.new_full((pad, K), -1)])
+    G = si_rows.shape[0] // group
+    s = torch.sort(si_rows.reshape(G, group * K), dim=1).values
     valid = s >= 0
     dup = (s[:, 1:] == s[:, :-1]) & valid[:, 1:]
-    n = int(valid.sum()) - int(dup.sum())
-    if R % 2:
-        n += int((si_rows[-1] >= 0).sum())
-    return n
+    return int(valid.sum()) - int(dup.sum())
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per valid pair, from one
 # `ncu --set full` capture of the last 256 query rows of config 4 (524,288 pairs; command and
 # figures in profiles/sfa_kernels_config4_rows256_full.md), scaled to a launch by its pairs.
@@ -461,8 +462,8 @@ def main():
                             "key_rows_per_step": red_rows,
                             "pairs_per_step": my_pairs,
                             "bytes_per_step": red_rows * BWD_SCATTER_BYTES_PER_KEY_ROW,
-                            "target": "fp32 key-gradient accumulators, L2-resident; a key both "
-                                      "rows of a row pair select is reduced once",
+                            "target": "fp32 key-gradient accumulators, L2-resident; a key the "
+                                      "rows of a four-row group share is reduced once",
                             "gbs_over_bwd": red_rows * BWD_SCATTER_BYTES_PER_KEY_ROW / ((bwd_ms - ar_ms) * 1e-3) / 1e9},
             "merged_key_grad": {
                 "bwd_ms": bwd_merged_ms,

@@ -69,6 +69,7 @@ struct Args {
   const int32_t* ws_rows;
   const int32_t* ws_count;
   const int4* runs;  // NULL, or [num_rows / 2 rounded up][3] key runs of row pairs (K3 grouped)
+  const int4* recs;  // NULL, or [num_rows / 4 rounded up][kRec4] records of four-row groups
   void* ds;        // [num_rows][kp][128 heads] scratch (key-major), dtype of the inputs
   void* pp;        // [num_rows][kp][128 heads]
   const float* delta;   // [num_rows][N1] rowsum(dO * O), from sfa_bwd_delta_kernel
@@ -936,8 +937,11 @@ __device__ __forceinline__ Part3 part3(int part, bool merged) {
 // Lane l holds column c0 + l of every key; for keys (2j, 2j+1) the lanes swap one value
 // with their neighbour so that even lanes hold columns (l, l+1) of key 2j and odd lanes
 // columns (l-1, l) of key 2j+1: each red.v2 then covers two whole 128-byte rows.
-// rows[i]: accumulator row of key 32i + l of the share (-1 = no key).
-template <int NK>
+// rows[i]: accumulator row of key 32i + l of the share (-1 = no key).  kCluster: `t_empty`
+// is a cluster-window address (the pair leader's barrier); the arrive is relaxed, because it
+// only has to follow the warp's completed TMEM reads (a cluster-scope release would wait for
+// the warp's reductions in flight to reach L2).
+template <int NK, bool kCluster = false>
 __device__ __forceinline__ void dkv_drain(uint32_t taddr, uint32_t t_empty, bool lanes_ok,
                                           float* gcol, int ld, const int (&rows)[NK / 32],
                                           int lane) {
@@ -952,7 +956,12 @@ __device__ __forceinline__ void dkv_drain(uint32_t taddr, uint32_t t_empty, bool
     if (h == NK / 16 - 1) {
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(t_empty);
+      if (lane == 0) {
+        if constexpr (kCluster)
+          mbar_arrive_cluster_relaxed(t_empty);
+        else
+          mbar_arrive(t_empty);
+      }
     }
     if (!lanes_ok) continue;
     // all exchanges first (independent shuffles in flight), then the reductions back to back
@@ -1201,6 +1210,503 @@ __global__ void __launch_bounds__(kThreads3, 1)
 }
 
 // =====================================================================================
+// K3 over groups of four rows (5-output calls, D = 256 or 512, at most 2048 keys a row)
+// =====================================================================================
+// Four adjacent query rows share more keys than two (config 4: the union of four rows'
+// lists is 0.48 of their valid pairs, of two rows' 0.73).  sfa_bwd_group4_kernel reorders
+// the four lists in place into runs, one per member mask (the rows that select the key).
+// A key's rank in its run is its rank in the list of the run's lowest member row, so every
+// member row lists the run's keys in the same order and a 128-key tile of the run is one TMA
+// box per member row.  The runs are walked with the masks that hold row 0 first (odd masks),
+// then those with row 1 (2, 6, 10, 14), row 2 (4, 12) and row 3 (8), so that each row's
+// slice is released for the next item as early as the walk allows.  A group whose lists
+// hold a key twice keeps its lists, one run per row.
+// Record of a group (kRec4 int4): [0] = (tiles, last tile of row 0, of row 1, of row 2),
+// [1] = (last tile of row 3, runs, 0, 0), then per non-empty run in walking order
+// (mask, length, first slot in row 0, in row 1) and (first slot in row 2, in row 3, 0, 0).
+// Last tile -1: the row has no keys.
+constexpr int kRec4 = 32;
+constexpr int kGroup4Threads = 1024;
+
+__device__ __forceinline__ int walk4(int p) {
+  return p < 8 ? 2 * p + 1 : p < 12 ? 2 + 4 * (p - 8) : p < 14 ? 4 + 8 * (p - 12) : 8;
+}
+
+__device__ __forceinline__ uint32_t field12(const uint64_t (&c)[3], int f) {
+  return (uint32_t)(c[f / 5] >> (12 * (f % 5))) & 0xfffu;
+}
+
+__global__ void __launch_bounds__(kGroup4Threads) sfa_bwd_group4_kernel(const Args a,
+                                                                       int32_t* ws_rows,
+                                                                       int4* recs, int lg) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ uint64_t warp_sum[3][kGroup4Threads / 32];
+  __shared__ int offs[4][16];   // first slot of the run of mask m in row g
+  __shared__ int cnt[16];       // keys of each mask
+  __shared__ int dup;
+  const int H = 1 << lg;   // >= 2 x the group's keys: the probe loops end
+  int* keys = reinterpret_cast<int*>(smem_raw);
+  uint32_t* word = reinterpret_cast<uint32_t*>(keys + H);   // mask | rank << 4
+  int* slot_of = reinterpret_cast<int*>(word + H);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r0 = 4 * blockIdx.x;
+  const size_t nent = (size_t)a.topk * a.block;
+  const bool abort = a.err != nullptr && *reinterpret_cast<volatile int*>(a.err) != 0;
+  int n[4];
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const int r = r0 + g;
+    n[g] = 0;
+    if (r < a.num_rows && !abort) {
+      const RowInfo ri = row_info(a, r);
+      n[g] = ri.active ? __ldg(a.ws_count + r) : 0;
+    }
+  }
+  const int b1 = n[0], b2 = b1 + n[1], b3 = b2 + n[2], N = b3 + n[3];
+  int4* rec = recs + (size_t)kRec4 * blockIdx.x;
+  auto unshared = [&]() {   // lists unchanged: one run per row with keys
+    if (threadIdx.x == 0) {
+      int t = 0, nr = 0, last[4];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        last[g] = -1;
+        if (n[g] == 0) continue;
+        rec[2 + 2 * nr] = make_int4(1 << g, n[g], 0, 0);
+        rec[3 + 2 * nr] = make_int4(0, 0, 0, 0);
+        ++nr;
+        t += tiles3(n[g]);
+        last[g] = t - 1;
+      }
+      rec[0] = make_int4(t, last[0], last[1], last[2]);
+      rec[1] = make_int4(last[3], nr, 0, 0);
+    }
+  };
+  if (N == 0 || 2 * N > H) {   // uniform over the block
+    unshared();
+    return;
+  }
+  for (int i = threadIdx.x; i < H; i += kGroup4Threads) {
+    keys[i] = -1;
+    word[i] = 0u;
+  }
+  if (threadIdx.x == 0) dup = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < N; i += kGroup4Threads) {
+    const int g = (i >= b1) + (i >= b2) + (i >= b3);
+    const int j = i - (g == 0 ? 0 : g == 1 ? b1 : g == 2 ? b2 : b3);
+    const int k = ws_rows[(size_t)(r0 + g) * nent + j];
+    uint32_t h = group_hash(k, lg);
+    for (int probe = 0; probe < H; ++probe) {
+      const int prev = atomicCAS(&keys[h], -1, k);
+      if (prev == -1 || prev == k) {
+        if (atomicOr(&word[h], 1u << g) & (1u << g)) dup = 1;   // listed twice in row g
+        slot_of[i] = (int)h;
+        break;
+      }
+      h = (h + 1) & (uint32_t)(H - 1);
+    }
+  }
+  __syncthreads();
+  if (dup) {   // uniform: read after the barrier
+    unshared();
+    return;
+  }
+  // Each thread takes a contiguous chunk of every list; per mask it counts the entries of the
+  // mask's lowest member row (12-bit fields: masks 1-5 in c[0], 6-10 in c[1], 11-15 in c[2];
+  // a count is at most 2048).
+  int j0[4], j1[4];
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const int pg = (n[g] + kGroup4Threads - 1) / kGroup4Threads;
+    j0[g] = min(n[g], (int)threadIdx.x * pg);
+    j1[g] = min(n[g], j0[g] + pg);
+  }
+  const int bs[4] = {0, b1, b2, b3};
+  uint64_t c[3] = {0, 0, 0};
+#pragma unroll
+  for (int g = 0; g < 4; ++g)
+    for (int j = j0[g]; j < j1[g]; ++j) {
+      const int m = (int)(word[slot_of[bs[g] + j]] & 15u);
+      if (__ffs(m) - 1 == g) {
+        const int f = m - 1;
+        c[f / 5] += 1ull << (12 * (f % 5));
+      }
+    }
+  uint64_t v[3];
+#pragma unroll
+  for (int x = 0; x < 3; ++x) {
+    v[x] = c[x];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint64_t y = __shfl_up_sync(0xffffffffu, v[x], o);
+      if (lane >= o) v[x] += y;
+    }
+    if (lane == 31) warp_sum[x][warp] = v[x];
+  }
+  __syncthreads();
+  if (warp < 3) {
+    uint64_t w = lane < kGroup4Threads / 32 ? warp_sum[warp][lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint64_t y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < kGroup4Threads / 32) warp_sum[warp][lane] = w;
+  }
+  __syncthreads();
+  uint64_t e[3], tot[3];
+#pragma unroll
+  for (int x = 0; x < 3; ++x) {
+    e[x] = v[x] - c[x] + (warp > 0 ? warp_sum[x][warp - 1] : 0);
+    tot[x] = warp_sum[x][kGroup4Threads / 32 - 1];
+  }
+  if (threadIdx.x < 15) cnt[threadIdx.x + 1] = (int)field12(tot, threadIdx.x);
+  __syncthreads();
+  if (threadIdx.x < 64) {   // offs[g][m]: keys of the earlier runs (walking order) that row g holds
+    const int g = threadIdx.x >> 4, m = threadIdx.x & 15;
+    int off = 0;
+    for (int p = 0; p < 15; ++p) {
+      const int mp = walk4(p);
+      if (mp == m) break;
+      if ((mp >> g) & 1) off += cnt[mp];
+    }
+    offs[g][m] = off;
+  }
+  __syncthreads();
+  // every list entry was read into the table above, so the lists are rewritten in place:
+  // first the lowest member row of each key (which leaves the rank for the others), ...
+#pragma unroll
+  for (int g = 0; g < 4; ++g)
+    for (int j = j0[g]; j < j1[g]; ++j) {
+      const int h = slot_of[bs[g] + j];
+      const uint32_t w = word[h];
+      const int m = (int)(w & 15u);
+      if (__ffs(m) - 1 != g) continue;
+      const int f = m - 1;
+      const int rank = (int)((e[f / 5] >> (12 * (f % 5))) & 0xfffu);
+      e[f / 5] += 1ull << (12 * (f % 5));
+      ws_rows[(size_t)(r0 + g) * nent + offs[g][m] + rank] = keys[h];
+      if (m != (1 << g)) word[h] = w | ((uint32_t)rank << 4);
+    }
+  __syncthreads();
+  // ... then the other member rows at the same rank
+#pragma unroll
+  for (int g = 0; g < 4; ++g)
+    for (int j = j0[g]; j < j1[g]; ++j) {
+      const int h = slot_of[bs[g] + j];
+      const uint32_t w = word[h];
+      const int m = (int)(w & 15u);
+      if (__ffs(m) - 1 == g) continue;
+      ws_rows[(size_t)(r0 + g) * nent + offs[g][m] + (int)(w >> 4)] = keys[h];
+    }
+  if (threadIdx.x == 0) {
+    int t = 0, nr = 0, last[4] = {-1, -1, -1, -1};
+    for (int p = 0; p < 15; ++p) {
+      const int m = walk4(p);
+      if (cnt[m] == 0) continue;
+      rec[2 + 2 * nr] = make_int4(m, cnt[m], offs[0][m], offs[1][m]);
+      rec[3 + 2 * nr] = make_int4(offs[2][m], offs[3][m], 0, 0);
+      ++nr;
+      t += tiles3(cnt[m]);
+#pragma unroll
+      for (int g = 0; g < 4; ++g)
+        if ((m >> g) & 1) last[g] = t - 1;
+    }
+    rec[0] = make_int4(t, last[0], last[1], last[2]);
+    rec[1] = make_int4(last[3], nr, 0, 0);
+  }
+}
+
+// K3 of a four-row group runs on a CTA pair (tcgen05 cta_group::2): M = 256 output columns
+// of the part (128 per CTA), N = 128 keys of the tile (each CTA loads 64 of them), K = 128
+// heads per member row.  Each CTA keeps its 128 columns of the four rows' slices (4 x 32 KB)
+// and a 6-stage ring of 64-key dS / P halves (16 KB); a tile of a run with r member rows
+// takes r ring entries into one of four TMEM accumulators (128 columns each; the drains of
+// both CTAs free it), so a key the r rows share is reduced once.
+// Each CTA drains its own 128 columns of the 128 keys (16 warps: 4 TMEM lane quadrants x 32
+// keys) with the same whole-row red.v2 form as K3.  Roles: warp 0 (one lane) loads the
+// slices and the ring entries in both CTAs, warp 1 of the leader issues the MMAs, warps 2-17
+// drain.  Parts: dK columns [0,256) and [256,512) (D = 512), the same of dV, and dKr (64
+// columns on the leader; the peer's half of that product is never read).
+constexpr int kStages4 = 6;
+
+template <int D>
+struct Cfg4 {
+  static constexpr int kW = 256;                           // output columns per part
+  static constexpr int kDParts = D / kW;
+  static constexpr int kParts = 2 * kDParts + 1;
+  static constexpr int kBox = 128 * 128;                   // 64 columns x 128 heads, MN-major
+  static constexpr int kSlot = 2 * kBox;                   // this CTA's 128 columns of a row
+  static constexpr int kHalf = 64 * 128;                   // 64 key slots x 64 heads
+  static constexpr int kTileB = 2 * kHalf;                 // 64 key slots x 128 heads
+  static constexpr int kOffA = 0;
+  static constexpr int kOffB = 4 * kSlot;
+  static constexpr int kOffBars = kOffB + kStages4 * kTileB;
+};
+
+struct Maps4 {
+  CUtensorMap ds, pp, q, qr, dout;   // scratch boxes 64 heads x 64 slots; slices 64 x 128
+};
+
+struct __align__(16) Bars4 {
+  uint64_t a_full[4], a_empty[4];
+  uint64_t b_full[kStages4], b_empty[kStages4];
+  uint64_t t_full[4], t_empty[4];
+  uint32_t tmem_slot;
+};
+
+constexpr int kThreads4 = 18 * 32;   // warp 0: TMA, 1: MMA (leader), 2-17: drain
+
+// Tile cursor over a group record's runs (every role walks the same sequence).
+struct Cur4 {
+  int r, i, nt;
+  int4 ra, rb;
+};
+
+__device__ __forceinline__ void cur4_init(Cur4& c, const int4* rec) {
+  c.r = 0;
+  c.i = 0;
+  c.ra = __ldg(rec + 2);
+  c.rb = __ldg(rec + 3);
+  c.nt = tiles3(c.ra.y);
+}
+
+__device__ __forceinline__ void cur4_next(Cur4& c, const int4* rec, int nruns) {
+  if (++c.i < c.nt) return;
+  c.i = 0;
+  if (++c.r < nruns) {
+    c.ra = __ldg(rec + 2 + 2 * c.r);
+    c.rb = __ldg(rec + 3 + 2 * c.r);
+    c.nt = tiles3(c.ra.y);
+  }
+}
+
+// first slot of the current tile in row g
+__device__ __forceinline__ int cur4_off(const Cur4& c, int g) {
+  return (g == 0 ? c.ra.z : g == 1 ? c.ra.w : g == 2 ? c.rb.x : c.rb.y) + kKeyTile3 * c.i;
+}
+
+template <int D, typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads4, 1)
+    sfa_bwd_dkv4_kernel(const __grid_constant__ Maps4 maps, const Args a) {
+  using C = Cfg4<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  Bars4& bars = *reinterpret_cast<Bars4*>(smem_raw + C::kOffBars);
+  const uint32_t sbase = smem_u32(smem_raw);
+  const uint32_t sA = sbase + C::kOffA, sB = sbase + C::kOffB;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (sbase & 1023u) {   // identical in both CTAs of the pair, so both leave together
+    if (threadIdx.x == 0) report_error(a.err, kErrMisaligned);
+    return;
+  }
+  const uint32_t cta = cluster_ctarank();
+  const bool abort = a.err != nullptr && *reinterpret_cast<volatile int*>(a.err) != 0;
+  const int ngroups = (a.num_rows + 3) / 4;
+  const int nitems = abort ? 0 : ngroups * C::kParts;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const size_t nent = (size_t)a.topk * a.block;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < 4; ++s) {
+      mbar_init(smem_u32(&bars.a_full[s]), 1);    // leader: bytes of both CTAs
+      mbar_init(smem_u32(&bars.a_empty[s]), 1);
+    }
+    for (int s = 0; s < kStages4; ++s) {
+      mbar_init(smem_u32(&bars.b_full[s]), 1);    // leader: bytes of both CTAs
+      mbar_init(smem_u32(&bars.b_empty[s]), 1);
+    }
+    for (int s = 0; s < 4; ++s) {
+      mbar_init(smem_u32(&bars.t_full[s]), 1);
+      mbar_init(smem_u32(&bars.t_empty[s]), 32);  // leader: 16 drain warps of each CTA
+    }
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc<2>(smem_u32(&bars.tmem_slot), 512);
+    tmem_relinquish<2>();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = bars.tmem_slot;
+  bool failed = false;
+
+  if (warp == 0) {
+    // ---- TMA (both CTAs): this CTA's columns of the member rows' slices, its 64 key slots
+    // of every ring entry; completion counted on the leader's barriers ----
+    if (lane == 0) {
+      int ua[4] = {0, 0, 0, 0}, nb = 0;
+      for (int it = pair; it < nitems && !failed; it += npairs) {
+        const int grp = it / C::kParts, part = it % C::kParts;
+        const int4* rec = a.recs + (size_t)kRec4 * grp;
+        const int4 h0 = __ldg(rec), h1 = __ldg(rec + 1);
+        if (h0.x == 0) continue;
+        const int last[4] = {h0.y, h0.z, h0.w, h1.x};
+        const bool rope = part == 2 * C::kDParts;
+        const bool is_dv = !rope && part >= C::kDParts;
+        const int col0 = rope ? 0 : (part % C::kDParts) * C::kW;
+        const CUtensorMap* am = rope ? &maps.qr : is_dv ? &maps.dout : &maps.q;
+        const CUtensorMap* bm = is_dv ? &maps.pp : &maps.ds;
+        const int row0 = 4 * grp;
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          if (last[g] < 0 || failed) continue;
+          if (!mbar_wait_sleep(smem_u32(&bars.a_empty[g]), (ua[g] & 1) ^ 1, a.err, &failed)) continue;
+          const uint32_t fb = smem_u32(&bars.a_full[g]);
+          if (cta == 0) mbar_arrive_expect_tx(fb, 2 * C::kSlot);
+          for (int c = 0; c < 2; ++c)
+            tma_load_2d_pair(sA + g * C::kSlot + c * C::kBox, am, mapa_shared(fb, 0),
+                             col0 + 128 * (int)cta + 64 * c, (row0 + g) * a.N1);
+          ++ua[g];
+        }
+        if (failed) break;
+        Cur4 cu;
+        cur4_init(cu, rec);
+        for (int t = 0; t < h0.x && !failed; ++t) {
+          const int mask = cu.ra.x;
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            if (!((mask >> g) & 1) || failed) continue;
+            const int s = nb % kStages4;
+            if (!mbar_wait_sleep(smem_u32(&bars.b_empty[s]), ((nb / kStages4) & 1) ^ 1, a.err, &failed))
+              continue;
+            const uint32_t fb = smem_u32(&bars.b_full[s]);
+            if (cta == 0) mbar_arrive_expect_tx(fb, 2 * C::kTileB);
+            const int srow = (row0 + g) * a.kp + cur4_off(cu, g) + 64 * (int)cta;
+            for (int c = 0; c < 2; ++c)   // heads [64c, 64c+64) of this CTA's 64 key slots
+              tma_load_2d_pair(sB + s * C::kTileB + c * C::kHalf, bm, mapa_shared(fb, 0), 64 * c, srow);
+            ++nb;
+          }
+          cur4_next(cu, rec, h1.y);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---- MMA (leader; the whole warp runs the loop, one elected lane issues) ----
+    if (cta == 0) {
+      const bool bf16 = ElemTraits<T>::kIsBf16;
+      const uint32_t id = idesc_f16(256, kKeyTile3, bf16, true, false);
+      int ua[4] = {0, 0, 0, 0}, nb = 0, nt = 0;
+      for (int it = pair; it < nitems && !failed; it += npairs) {
+        const int grp = it / C::kParts;
+        const int4* rec = a.recs + (size_t)kRec4 * grp;
+        const int4 h0 = __ldg(rec), h1 = __ldg(rec + 1);
+        if (h0.x == 0) continue;
+        const int last[4] = {h0.y, h0.z, h0.w, h1.x};
+        int waited = 0;
+        Cur4 cu;
+        cur4_init(cu, rec);
+        for (int t = 0; t < h0.x; ++t) {
+          const int tb = nt & 3;
+          const int mask = cu.ra.x;
+          const int top = 31 - __clz(mask);
+          mbar_wait_spin(smem_u32(&bars.t_empty[tb]), ((nt >> 2) & 1) ^ 1, a.err, &failed, true);
+          int e = 0;
+#pragma unroll 1
+          for (int g = 0; g < 4; ++g) {
+            if (!((mask >> g) & 1)) continue;
+            const int s = nb % kStages4;
+            if (!((waited >> g) & 1)) {
+              const int u = g == 0 ? ua[0] : g == 1 ? ua[1] : g == 2 ? ua[2] : ua[3];
+              mbar_wait_spin(smem_u32(&bars.a_full[g]), u & 1, a.err, &failed, true);
+              waited |= 1 << g;
+            }
+            mbar_wait_spin(smem_u32(&bars.b_full[s]), (nb / kStages4) & 1, a.err, &failed, true);
+            if (__any_sync(0xffffffffu, failed)) {
+              failed = true;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t da = smem_desc_sw128(sA + g * C::kSlot, C::kBox, 1024);
+            const uint64_t db = smem_desc_sw128(sB + s * C::kTileB, 16, 1024);
+            if (elect_one()) {
+#pragma unroll
+              for (int k = 0; k < kHeadsPad / 16; ++k)
+                umma_f16<2>(tmem + tb * kKeyTile3, da + (uint64_t)((k * 2048) >> 4),
+                            db + (uint64_t)(((k >> 2) * C::kHalf + (k & 3) * 32) >> 4), id,
+                            (e | k) != 0);
+              umma_commit_pair(smem_u32(&bars.b_empty[s]), 3);
+              if (g == top) umma_commit_pair(smem_u32(&bars.t_full[tb]), 3);
+              // the row's last tile of this item: its slot is free for the next item
+              if (t == (g == 0 ? last[0] : g == 1 ? last[1] : g == 2 ? last[2] : last[3]))
+                umma_commit_pair(smem_u32(&bars.a_empty[g]), 3);
+            }
+            __syncwarp();
+            ++nb;
+            ++e;
+          }
+          if (failed) break;
+          ++nt;
+          cur4_next(cu, rec, h1.y);
+        }
+        if (failed) break;
+#pragma unroll
+        for (int g = 0; g < 4; ++g)
+          if (last[g] >= 0) ++ua[g];
+      }
+      // the MMAs issued last complete before the exit (their TMEM is freed afterwards)
+      if (nt > 0) {
+        bool f2 = false;
+        mbar_wait(smem_u32(&bars.t_full[(nt - 1) & 3]), ((nt - 1) >> 2) & 1, a.err, &f2);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---- drain (both CTAs): TMEM lane = output column, column = key ----
+    const int q = warp & 3;            // TMEM lane quadrant this warp may access
+    const int cg = (warp - 2) >> 2;    // keys [32 cg, 32 cg + 32) of a tile
+    const uint32_t lead_te = mapa_shared(smem_u32(&bars.t_empty[0]), 0);
+    int nt = 0;
+    for (int it = pair; it < nitems; it += npairs) {
+      const int grp = it / C::kParts, part = it % C::kParts;
+      const int4* rec = a.recs + (size_t)kRec4 * grp;
+      const int4 h0 = __ldg(rec), h1 = __ldg(rec + 1);
+      if (h0.x == 0) continue;
+      const bool rope = part == 2 * C::kDParts;
+      const bool is_dv = !rope && part >= C::kDParts;
+      const int col0 = rope ? 0 : (part % C::kDParts) * C::kW;
+      float* acc = rope ? a.dkr_acc : is_dv ? a.dv_acc : a.dk_acc;
+      const int ld = rope ? 64 : D;
+      const bool lanes_ok = !rope || (cta == 0 && q < 2);   // rope: 64 output columns
+      float* gcol = acc + col0 + 128 * (int)cta + 32 * q + lane - (lane & 1);
+      const int row0 = 4 * grp;
+      // accumulator row of this lane's key of the cursor's tile (-1: none); a tile's keys
+      // are listed in the key list of any of its member rows (the lowest)
+      auto key_row = [&](const Cur4& c) {
+        const int g0 = __ffs(c.ra.x) - 1;
+        const int k = 32 * cg + lane;
+        const int len = min(kKeyTile3, c.ra.y - kKeyTile3 * c.i);
+        return k < len ? __ldg(a.ws_rows + (size_t)(row0 + g0) * nent + cur4_off(c, g0) + k) : -1;
+      };
+      Cur4 cu;   // one tile ahead of the tile being drained
+      cur4_init(cu, rec);
+      int kr = key_row(cu);
+      cur4_next(cu, rec, h1.y);
+      for (int t = 0; t < h0.x; ++t) {
+        const int tb = nt & 3;
+        const int kn = t + 1 < h0.x ? key_row(cu) : -1;   // in flight while this tile drains
+        if (t + 1 < h0.x) cur4_next(cu, rec, h1.y);
+        mbar_wait(smem_u32(&bars.t_full[tb]), (nt >> 2) & 1, a.err, &failed);
+        if (__any_sync(0xffffffffu, failed)) break;
+        tc_fence_after();
+        const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + tb * kKeyTile3 + 32 * cg;
+        const int rows[1] = {kr};
+        dkv_drain<32, true>(taddr, lead_te + 8 * tb, lanes_ok, gcol, ld, rows, lane);
+        kr = kn;
+        ++nt;
+      }
+      if (failed) break;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) tmem_dealloc<2>(tmem, 512);
+}
+
+// =====================================================================================
 // K4: fp32 accumulators -> key dtype
 // =====================================================================================
 template <typename T>
@@ -1249,14 +1755,19 @@ inline int sm_count() {
 // key slots per row in the P / dS scratch: whole K1 pair tiles (256 keys)
 inline int64_t padded_keys(int64_t nent) { return (nent + 255) / 256 * 256; }
 inline int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
-// run table of the row pairs (K3 grouped mode)
-inline int64_t runs_bytes(int64_t num_rows) { return align256((num_rows + 1) / 2 * 3 * 16); }
-// hash table of one row pair (log2 of its entries): at least twice the pair's keys; pairs of
-// longer key lists than kGroupMaxKeys per row stay ungrouped
+// run table of the row pairs or records of the four-row groups (K3 grouped modes)
+inline int64_t runs_bytes(int64_t num_rows) {
+  const int64_t pairs = (num_rows + 1) / 2 * 3 * 16, quads = (num_rows + 3) / 4 * kRec4 * 16;
+  return align256(pairs > quads ? pairs : quads);
+}
+// hash table of one group (log2 of its entries): at least twice the group's keys; groups of
+// longer key lists than kGroup4MaxKeys (four rows) or kGroupMaxKeys (pairs) per row are
+// formed smaller or not at all
 constexpr int64_t kGroupMaxKeys = 4096;
-inline int group_lg(int64_t nent) {
+constexpr int64_t kGroup4MaxKeys = 2048;
+inline int group_lg(int64_t keys_per_group) {
   int lg = 10;
-  while ((int64_t(1) << lg) < 4 * nent) ++lg;
+  while ((int64_t(1) << lg) < 2 * keys_per_group) ++lg;
   return lg;
 }
 
@@ -1308,16 +1819,20 @@ int launch(const DsaSfaBwdParams* p, cudaStream_t stream) {
   ws += align256(p->num_rows * kHeadsPad * kp * 2);
   a.delta = reinterpret_cast<const float*>(ws);
   ws += align256(4 * p->num_rows * kHeadsPad);
-  // row pairs share their keys' reductions in K3 (5-output calls; the merged mode's two
-  // slots already hold Q and dO, and the teacher is indexed by the untouched key order)
-  const bool grouped = p->dv_acc != nullptr && p->teacher == nullptr && p->num_rows >= 2 &&
-                       nent <= kGroupMaxKeys;
+  // adjacent rows share their keys' reductions in K3 (5-output calls; the merged mode's two
+  // slots already hold Q and dO, and the teacher is indexed by the untouched key order):
+  // groups of four on CTA pairs where the slices fit (256-column parts), else pairs
+  const bool can_group = p->dv_acc != nullptr && p->teacher == nullptr && p->num_rows >= 2;
+  const bool grouped4 = can_group && nent <= kGroup4MaxKeys && (D == 256 || D == 512);
+  const bool grouped = can_group && !grouped4 && nent <= kGroupMaxKeys;
   a.runs = grouped ? reinterpret_cast<const int4*>(ws) : nullptr;
+  a.recs = grouped4 ? reinterpret_cast<const int4*>(ws) : nullptr;
   a.kp = (int)kp;
 
   Maps1 m1;
   Maps2 m2;
   Maps3 m3;
+  Maps4 m4;
   const uint64_t krows_s = (uint64_t)p->num_rows * kp;   // scratch rows: one per key slot
   if (!make_tmap_2d_16b(&m1.q, p->q, bf16, qrows, D, (uint64_t)D * 2, 64, 64) ||
       !make_tmap_2d_16b(&m1.qr, p->q_rope, bf16, qrows, 64, 128, 64, 64) ||
@@ -1333,6 +1848,14 @@ int launch(const DsaSfaBwdParams* p, cudaStream_t stream) {
       !make_tmap_2d_16b(&m3.qr, p->q_rope, bf16, qrows, 64, 128, 64, 128) ||
       !make_tmap_2d_16b(&m3.dout, p->d_out, bf16, qrows, D, (uint64_t)D * 2, 64, 128))
     return DSA_ERR_TMA_DESCRIPTOR;
+  if (grouped4) {
+    m4.q = m3.q;
+    m4.qr = m3.qr;
+    m4.dout = m3.dout;
+    if (!make_tmap_2d_16b(&m4.ds, a.ds, bf16, krows_s, kHeadsPad, kHeadsPad * 2, 64, 64) ||
+        !make_tmap_2d_16b(&m4.pp, a.pp, bf16, krows_s, kHeadsPad, kHeadsPad * 2, 64, 64))
+      return DSA_ERR_TMA_DESCRIPTOR;
+  }
 
   // fp32 accumulators start at zero unless the caller adds several calls into them; the
   // prep pass compacts the valid keys of each row
@@ -1344,8 +1867,19 @@ int launch(const DsaSfaBwdParams* p, cudaStream_t stream) {
     return DSA_ERR_CUDA;
   launch_prep(a, const_cast<int32_t*>(a.ws_rows), const_cast<int32_t*>(a.ws_count), p->num_rows,
               stream);
+  if (grouped4) {
+    const int lg = group_lg(4 * nent);
+    const int smem = group_smem_bytes(lg);
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(sfa_bwd_group4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem) != cudaSuccess)
+      return DSA_ERR_CUDA;
+    sfa_bwd_group4_kernel<<<dim3((unsigned)((p->num_rows + 3) / 4)), dim3(kGroup4Threads), smem,
+                            stream>>>(a, const_cast<int32_t*>(a.ws_rows), const_cast<int4*>(a.recs),
+                                      lg);
+  }
   if (grouped) {
-    const int lg = group_lg(nent);
+    const int lg = group_lg(2 * nent);
     const int smem = group_smem_bytes(lg);
     if (smem > 48 * 1024 &&
         cudaFuncSetAttribute(sfa_bwd_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1376,7 +1910,19 @@ int launch(const DsaSfaBwdParams* p, cudaStream_t stream) {
       return DSA_ERR_CUDA;
     k<<<dim3(2 * (unsigned)p->num_rows), dim3(kThreads2), smem, stream>>>(m2, a);
   }
-  {
+  if (grouped4) {
+    if constexpr (D >= 256) {
+      auto k = sfa_bwd_dkv4_kernel<D, T>;
+      const int smem = Cfg4<D>::kOffBars + (int)sizeof(Bars4);
+      static_assert(Cfg4<D>::kOffBars + (int)sizeof(Bars4) <= 232448, "K3 pair smem");
+      if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+        return DSA_ERR_CUDA;
+      const int64_t items = (p->num_rows + 3) / 4 * Cfg4<D>::kParts;
+      const int64_t pairs_max = sm_count() / 2;
+      const int npairs = (int)(items < pairs_max ? items : pairs_max);
+      k<<<dim3(2 * (unsigned)npairs), dim3(kThreads4), smem, stream>>>(m4, a);
+    }
+  } else {
     auto k = sfa_bwd_dkv_kernel<D, T>;
     const int smem = Cfg3<D>::kOffBars + (int)sizeof(Bars3);
     if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)

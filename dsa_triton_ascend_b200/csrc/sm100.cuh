@@ -81,6 +81,15 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
                : "memory");
 }
 
+// Arrive on a barrier in the cluster window without ordering the thread's earlier memory
+// operations: for a consumer whose signal only says that reads it has already completed are
+// done (tcgen05.ld followed by tcgen05.wait::ld), so that the arrive does not wait for the
+// thread's outstanding global reductions as a cluster-scope release would.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(

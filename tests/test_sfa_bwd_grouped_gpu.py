@@ -1,13 +1,15 @@
-"""K3 row pairs: the shared keys of two adjacent query rows reduced once (GPU).
+"""K3 row groups: the shared keys of adjacent query rows reduced once (GPU).
 
-A 5-output backward call reorders each pair of adjacent rows' compacted key lists into three
-runs (keys of row 0 only, keys of both, keys of row 1 only; the shared run in row 0's order
-in both rows), and K3 sums the two rows' products for a shared key in TMEM before the one
-scatter into the key's fp32 accumulator.  These cases drive every pair layout against the
-oracle: identical lists in different orders, disjoint lists, partial overlap, an odd row
-count, an inactive row beside an active one, ragged -1 tails and a key listed twice (which
-keeps the pair unshared).  Some cases read the reordered lists and the run table back from
-the workspace.
+A 5-output backward call reorders the compacted key lists of adjacent rows into runs, one
+per set of member rows (the rows that select the key), every member row listing a run's keys
+in the same order, and K3 sums the member rows' products for a key in TMEM before the one
+scatter into the key's fp32 accumulator.  Groups of four rows run K3 on CTA pairs (D = 256
+or 512, at most 2048 keys a row); otherwise pairs of rows on single CTAs (D = 128, or longer
+lists).  These cases drive both against the oracle: identical lists in different orders,
+disjoint lists, partial overlap, row counts that leave a short last group, an inactive row,
+ragged -1 tails, a key listed twice (which keeps its group unshared) and lists too long for
+groups of four.  Some cases read the reordered lists and the run records back from the
+workspace.
 """
 import numpy as np
 import pytest
@@ -57,6 +59,8 @@ CASES = [
     ("duplicate", 1, 4, 700, 16, 512, 300, None),
     ("inactive", 1, 4, 700, 16, 512, 300, [3]),
     ("headline", 1, 4, 4096, 128, 512, 2048, None),
+    ("six", 1, 6, 700, 16, 256, 300, None),
+    ("long", 1, 4, 4400, 16, 512, 2100, None),
 ]
 
 
@@ -65,7 +69,7 @@ def _run(name, B, S1, S2, N1, D, cnt, act_q, workspace=None):
     from dsa_triton_ascend_b200.sparse_flash_attention_grad import _sfa_grad, INT64_MAX
     rng = np.random.default_rng(sum(map(ord, name)))
     c = I.sfa_case(B, S1, S2, N1, D, cnt, 1, 0, "bf16", seed=7)
-    pat = "overlap" if name in ("inactive", "headline") else name
+    pat = "overlap" if name in ("inactive", "headline", "six", "long") else name
     c["si"] = _pattern(pat, rng, B, S1, S2, cnt)
     act_k = [S2] * B if act_q is not None else None
     out, mx, sm = sfa.sfa_fwd(c["q"], c["k"], c["qr"], c["kr"], c["si"], c["scale"],
@@ -93,11 +97,44 @@ def _align256(x):
     return (x + 255) // 256 * 256
 
 
-@pytest.mark.parametrize("name", ["overlap", "identical", "duplicate", "inactive", "odd"])
-def test_row_pair_runs_in_workspace(name):
-    """The reordered lists hold each row's keys exactly once in a fixed order (own keys, then
-    shared keys, in list order; the shared run in row 0's order in both rows); unshared pairs
-    keep their lists and describe them as two runs."""
+WALK4 = [1, 3, 5, 7, 9, 11, 13, 15, 2, 6, 10, 14, 4, 12, 8]
+
+
+def _expected_runs(lists_in, G):
+    """Reference reordering of G rows' key lists: one run per member mask (walking order:
+    for four rows the masks holding row 0 first, then row 1, row 2, row 3; for two rows
+    1, 3, 2), a run's keys in the order of its lowest member row's list.  Returns the
+    rewritten lists and the runs [(mask, length, first slot per row)], or None when a list
+    holds a key twice (the group stays unshared)."""
+    if any(len(set(l)) != len(l) for l in lists_in):
+        return None
+    member = {}
+    for g, l in enumerate(lists_in):
+        for k in l:
+            member[k] = member.get(k, 0) | (1 << g)
+    walk = WALK4 if G == 4 else [1, 3, 2]
+    out = [[] for _ in range(G)]
+    runs = []
+    for m in walk:
+        low = (m & -m).bit_length() - 1
+        if low >= G:
+            continue
+        keys = [k for k in lists_in[low] if member[k] == m]
+        if not keys:
+            continue
+        runs.append((m, len(keys), [len(out[g]) if (m >> g) & 1 else None for g in range(G)]))
+        for g in range(G):
+            if (m >> g) & 1:
+                out[g] += keys
+    return out, runs
+
+
+@pytest.mark.parametrize("name", ["overlap", "identical", "duplicate", "inactive", "odd", "six",
+                                  "long"])
+def test_row_group_runs_in_workspace(name):
+    """The reordered lists and the run records equal a plain restatement of the reordering
+    (four-row records for D = 256 / 512 with at most 2048 keys a row, pair runs otherwise);
+    groups with a key listed twice keep their lists, one run per row."""
     from dsa_triton_ascend_b200._lib import lib
     case = {c[0]: c for c in CASES}[name]
     _, B, S1, S2, N1, D, cnt, act_q = case
@@ -109,37 +146,60 @@ def test_row_pair_runs_in_workspace(name):
         assert_close(gi, ri, what=f"{name} {key}")
     w = ws.cpu().numpy()
     lists = w[: 4 * rows * cnt].view(np.int32).reshape(rows, cnt)
-    npairs = (rows + 1) // 2
-    runs_off = ws_bytes - _align256(npairs * 48)
-    runs = w[runs_off: runs_off + npairs * 48].view(np.int32).reshape(npairs, 3, 4)
+    G = 4 if D in (256, 512) and cnt <= 2048 else 2
+    ngroups = (rows + G - 1) // G
+    region = _align256(max((rows + 1) // 2 * 48, (rows + 3) // 4 * 512))
+    tab = w[ws_bytes - region:].view(np.int32)
     si = c["si"].reshape(rows, cnt)
     active = np.ones(rows, bool)
     if act_q is not None:
         for b in range(B):
             active[b * S1 + act_q[b]: (b + 1) * S1] = False
 
-    def keys_of(r):   # key-matrix rows the row selects (BSND: batch b's keys start at b*S2)
+    def keys_of(r):   # the row's compacted list (BSND: batch b's keys start at b*S2)
         if r >= rows or not active[r]:
-            return np.zeros(0, np.int64)
+            return []
         v = si[r][si[r] >= 0].astype(np.int64)
-        return v + (r // S1) * S2
+        return (v + (r // S1) * S2).tolist()
 
-    for g in range(npairs):
-        r0, r1 = 2 * g, 2 * g + 1
-        k0, k1 = keys_of(r0), keys_of(r1)
-        (m1, c1, a1, b1), (m3, c3, a3, b3), (m2, c2, a2, b2) = runs[g]
-        assert (m1, m3, m2) == (1, 3, 2)
-        grouped = len(k0) > 0 and len(k1) > 0 and len(set(k0)) == len(k0) and len(set(k1)) == len(k1)
-        if not grouped:
-            assert (c1, c3, c2) == (len(k0), 0, len(k1)) and (a1, b1, a2, b2) == (0, 0, 0, 0)
-            continue
-        shared = set(k0.tolist()) & set(k1.tolist())
-        assert (c1, c3, c2) == (len(k0) - len(shared), len(shared), len(k1) - len(shared))
-        assert (a3, b3, b2) == (c1, 0, c3)
-        # row 0: its own keys, then the shared ones, each in row 0's order; row 1: the shared
-        # keys in row 0's order, then its own keys in its own order
-        own0 = [k for k in k0 if k not in shared]
-        sh0 = [k for k in k0 if k in shared]
-        own1 = [k for k in k1 if k not in shared]
-        assert lists[r0, : c1 + c3].tolist() == own0 + sh0
-        assert lists[r1, : c3 + c2].tolist() == sh0 + own1
+    tiles = lambda n: (n + 127) // 128
+    for grp in range(ngroups):
+        r0 = G * grp
+        ins = [keys_of(r0 + g) for g in range(G)]
+        exp = _expected_runs(ins, G)
+        if exp is None:   # unshared: lists as compacted, one run per row with keys
+            outs = ins
+            runs = [(1 << g, len(ins[g]), [0 if h == g else None for h in range(G)])
+                    for g in range(G) if ins[g]]
+        else:
+            outs, runs = exp
+        for g in range(G):
+            if r0 + g < rows:
+                assert lists[r0 + g, : len(outs[g])].tolist() == outs[g], (grp, g)
+        if G == 4:
+            rec = tab[grp * 128: (grp + 1) * 128].reshape(32, 4)
+            t, last = 0, [-1] * 4
+            for i, (m, n, offs) in enumerate(runs):
+                ra, rb = rec[2 + 2 * i], rec[3 + 2 * i]
+                assert (ra[0], ra[1]) == (m, n), (grp, i)
+                got_offs = [ra[2], ra[3], rb[0], rb[1]]
+                for g in range(4):
+                    if offs[g] is not None:
+                        assert got_offs[g] == offs[g], (grp, i, g)
+                t += tiles(n)
+                for g in range(4):
+                    if (m >> g) & 1:
+                        last[g] = t - 1
+            assert rec[0].tolist() == [t, last[0], last[1], last[2]], grp
+            assert rec[1][:2].tolist() == [last[3], len(runs)], grp
+        else:
+            rec = tab[grp * 12: (grp + 1) * 12].reshape(3, 4)
+            byk = {m: (n, offs) for m, n, offs in runs}
+            for j, m in enumerate([1, 3, 2]):
+                assert rec[j][0] == m
+                n, offs = byk.get(m, (0, [None, None]))
+                assert rec[j][1] == n, (grp, m)
+                if n:
+                    for g in range(2):
+                        if offs[g] is not None:
+                            assert rec[j][2 + g] == offs[g], (grp, m, g)
