@@ -1542,25 +1542,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads4, 1)
         const int4* rec = a.recs + (size_t)kRec4 * grp;
         const int4 h0 = __ldg(rec), h1 = __ldg(rec + 1);
         if (h0.x == 0) continue;
-        const int last[4] = {h0.y, h0.z, h0.w, h1.x};
         const bool rope = part == 2 * C::kDParts;
         const bool is_dv = !rope && part >= C::kDParts;
         const int col0 = rope ? 0 : (part % C::kDParts) * C::kW;
         const CUtensorMap* am = rope ? &maps.qr : is_dv ? &maps.dout : &maps.q;
         const CUtensorMap* bm = is_dv ? &maps.pp : &maps.ds;
         const int row0 = 4 * grp;
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          if (last[g] < 0 || failed) continue;
-          if (!mbar_wait_sleep(smem_u32(&bars.a_empty[g]), (ua[g] & 1) ^ 1, a.err, &failed)) continue;
-          const uint32_t fb = smem_u32(&bars.a_full[g]);
-          if (cta == 0) mbar_arrive_expect_tx(fb, 2 * C::kSlot);
-          for (int c = 0; c < 2; ++c)
-            tma_load_2d_pair(sA + g * C::kSlot + c * C::kBox, am, mapa_shared(fb, 0),
-                             col0 + 128 * (int)cta + 64 * c, (row0 + g) * a.N1);
-          ++ua[g];
-        }
-        if (failed) break;
+        // a row's slice is loaded just before the first ring entry that needs it, so the
+        // item's first tiles do not wait for the slots the previous item releases last
+        int loaded = 0;
         Cur4 cu;
         cur4_init(cu, rec);
         for (int t = 0; t < h0.x && !failed; ++t) {
@@ -1568,6 +1558,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads4, 1)
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
             if (!((mask >> g) & 1) || failed) continue;
+            if (!((loaded >> g) & 1)) {
+              if (!mbar_wait_sleep(smem_u32(&bars.a_empty[g]), (ua[g] & 1) ^ 1, a.err, &failed))
+                continue;
+              const uint32_t fa = smem_u32(&bars.a_full[g]);
+              if (cta == 0) mbar_arrive_expect_tx(fa, 2 * C::kSlot);
+              for (int c = 0; c < 2; ++c)
+                tma_load_2d_pair(sA + g * C::kSlot + c * C::kBox, am, mapa_shared(fa, 0),
+                                 col0 + 128 * (int)cta + 64 * c, (row0 + g) * a.N1);
+              ++ua[g];
+              loaded |= 1 << g;
+            }
             const int s = nb % kStages4;
             if (!mbar_wait_sleep(smem_u32(&bars.b_empty[s]), ((nb / kStages4) & 1) ^ 1, a.err, &failed))
               continue;
