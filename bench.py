@@ -61,11 +61,11 @@ def reduced_key_rows(si_rows, group=4):
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per valid pair, from one
 # `ncu --set full` capture of the last 256 query rows of config 4 (524,288 pairs; command and
 # figures in profiles/sfa_kernels_config4_rows256_full.md), scaled to a launch by its pairs.
-# Backward: K1 + K2 + the row-pair pass + K3, plus the delta kernel's read of dO and O
+# Backward: K1 + K2 + the four-row group pass + K3, plus the delta kernel's read of dO and O
 # (2 x N1 x D x 2 B a row).  Builds of the captures: the forward, K1 and K2 of commit cb19fcd;
-# the row-pair pass and K3 of commit d917068 (profiles/sfa_bwd_dkv_reductions.md).
+# the group pass and K3 of commit a714e58 (profiles/sfa_bwd_dkv_reductions.md).
 PROFILE_PAIRS = 524288
-BWD_DRAM_BYTES_PER_PAIR = (103.11 + 218.89 + 146.14 + 19.40 + 2.12 + 476.91 + 39.97) * 1e6 / PROFILE_PAIRS
+BWD_DRAM_BYTES_PER_PAIR = (103.11 + 218.89 + 146.14 + 19.40 + 2.14 + 392.66 + 15.62) * 1e6 / PROFILE_PAIRS
 BWD_DRAM_BYTES_PER_ROW = 2 * N1 * D * 2
 FWD_DRAM_BYTES_PER_PAIR = (49.35 + 1.95) * 1e6 / PROFILE_PAIRS
 # DRAM traffic of one call of each secondary workload at the size bench.py runs, from one ncu
