@@ -46,7 +46,8 @@ BWD_SCATTER_BYTES_PER_KEY_ROW = 4 * (2 * D + DR)
 def reduced_key_rows(si_rows, group=4):
     """Key rows the backward's fp32 scatter reduces in one 5-output call over these query
     rows ([rows, topk] ids, -1 = none): the library groups `group` adjacent rows of the call
-    (four at D = 512 with top-2048) and reduces a key the group's rows share once, so a group
+    (four at D = 512 with top-2048; two in the merged key == value mode) and reduces a key the
+    group's rows share once, so a group
     costs the size of the union of its rows' keys (the synthetic ids of a row are distinct)."""
     import torch
     R, K = si_rows.shape
@@ -255,6 +256,7 @@ def main():
     qr = w["qr"][:, r0:r1].contiguous()
     si = w["si"][:, r0:r1].contiguous()
     red_rows = reduced_key_rows(si.reshape(-1, si.shape[-1]))
+    red_rows_merged = reduced_key_rows(si.reshape(-1, si.shape[-1]), group=2)   # key == value
     k, kr, scale = w["k"], w["kr"], w["scale"]
     dout = dout_full[:, r0:r1].contiguous()
     aq = [shard_act_q(S1, r0)]   # see dsa_triton_ascend_b200/sharding.py
@@ -470,7 +472,8 @@ def main():
                 "step_ms": fwd_ms + bwd_merged_ms,
                 "value": flops_total / ((fwd_ms + bwd_merged_ms) * 1e-3) / 1e12,
                 "unit": "TFLOP/s",
-                "scatter_bytes_per_pair": 4 * (D + DR),
+                "scatter_bytes_per_key_row": 4 * (D + DR),
+                "key_rows_per_step": red_rows_merged,
                 "note": "key == value (MLA): dK + dV accumulated as one (the autograd path); "
                         "forward time from the headline run, backward timed separately"},
             "ranks": [{"rank": i, "step_ms": r[0], "fwd_ms": r[1], "bwd_ms": r[2],

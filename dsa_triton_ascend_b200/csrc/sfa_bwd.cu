@@ -1221,6 +1221,8 @@ __global__ void __launch_bounds__(kThreads3, 1)
 // then those with row 1 (2, 6, 10, 14), row 2 (4, 12) and row 3 (8), so that each row's
 // slice is released for the next item as early as the walk allows.  A group whose lists
 // hold a key twice keeps its lists, one run per row.
+// The merged mode (key == value) groups two rows (`gs` = 2): its slices are twice as many
+// (Q and dO), so two rows fill the four slots; its records have rows 2 and 3 empty.
 // Record of a group (kRec4 int4): [0] = (tiles, last tile of row 0, of row 1, of row 2),
 // [1] = (last tile of row 3, runs, 0, 0), then per non-empty run in walking order
 // (mask, length, first slot in row 0, in row 1) and (first slot in row 2, in row 3, 0, 0).
@@ -1238,7 +1240,8 @@ __device__ __forceinline__ uint32_t field12(const uint64_t (&c)[3], int f) {
 
 __global__ void __launch_bounds__(kGroup4Threads) sfa_bwd_group4_kernel(const Args a,
                                                                        int32_t* ws_rows,
-                                                                       int4* recs, int lg) {
+                                                                       int4* recs, int lg,
+                                                                       int gs) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ uint64_t warp_sum[3][kGroup4Threads / 32];
   __shared__ int offs[4][16];   // first slot of the run of mask m in row g
@@ -1249,7 +1252,7 @@ __global__ void __launch_bounds__(kGroup4Threads) sfa_bwd_group4_kernel(const Ar
   uint32_t* word = reinterpret_cast<uint32_t*>(keys + H);   // mask | rank << 4
   int* slot_of = reinterpret_cast<int*>(word + H);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r0 = 4 * blockIdx.x;
+  const int r0 = gs * blockIdx.x;
   const size_t nent = (size_t)a.topk * a.block;
   const bool abort = a.err != nullptr && *reinterpret_cast<volatile int*>(a.err) != 0;
   int n[4];
@@ -1257,7 +1260,7 @@ __global__ void __launch_bounds__(kGroup4Threads) sfa_bwd_group4_kernel(const Ar
   for (int g = 0; g < 4; ++g) {
     const int r = r0 + g;
     n[g] = 0;
-    if (r < a.num_rows && !abort) {
+    if (g < gs && r < a.num_rows && !abort) {
       const RowInfo ri = row_info(a, r);
       n[g] = ri.active ? __ldg(a.ws_count + r) : 0;
     }
@@ -1427,7 +1430,10 @@ __global__ void __launch_bounds__(kGroup4Threads) sfa_bwd_group4_kernel(const Ar
 // keys) with the same whole-row red.v2 form as K3.  Roles: warp 0 (one lane) loads the
 // slices and the ring entries in both CTAs, warp 1 of the leader issues the MMAs, warps 2-17
 // drain.  Parts: dK columns [0,256) and [256,512) (D = 512), the same of dV, and dKr (64
-// columns on the leader; the peer's half of that product is never read).
+// columns on the leader; the peer's half of that product is never read).  Merged mode
+// (dv_acc == NULL): groups of two rows, row g's Q and dO slices in slots 2g and 2g+1, parts
+// dK + dV of [0,256) and [256,512) and dKr; a merged part's tile takes two entries per member
+// row, dS with Q and then P with dO, into the same accumulator.
 constexpr int kStages4 = 6;
 
 template <int D>
@@ -1501,8 +1507,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads4, 1)
   }
   const uint32_t cta = cluster_ctarank();
   const bool abort = a.err != nullptr && *reinterpret_cast<volatile int*>(a.err) != 0;
-  const int ngroups = (a.num_rows + 3) / 4;
-  const int nitems = abort ? 0 : ngroups * C::kParts;
+  const bool merged = a.dv_acc == nullptr;
+  const int gs = merged ? 2 : 4;                       // rows per group
+  const int nparts = merged ? C::kDParts + 1 : C::kParts;
+  const int ngroups = (a.num_rows + gs - 1) / gs;
+  const int nitems = abort ? 0 : ngroups * nparts;
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const size_t nent = (size_t)a.topk * a.block;
 
@@ -1538,18 +1547,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads4, 1)
     if (lane == 0) {
       int ua[4] = {0, 0, 0, 0}, nb = 0;
       for (int it = pair; it < nitems && !failed; it += npairs) {
-        const int grp = it / C::kParts, part = it % C::kParts;
+        const int grp = it / nparts, part = it % nparts;
         const int4* rec = a.recs + (size_t)kRec4 * grp;
         const int4 h0 = __ldg(rec), h1 = __ldg(rec + 1);
         if (h0.x == 0) continue;
-        const bool rope = part == 2 * C::kDParts;
-        const bool is_dv = !rope && part >= C::kDParts;
+        const bool rope = part == (merged ? C::kDParts : 2 * C::kDParts);
+        const bool mixed = merged && !rope;
+        const bool is_dv = !merged && !rope && part >= C::kDParts;
         const int col0 = rope ? 0 : (part % C::kDParts) * C::kW;
-        const CUtensorMap* am = rope ? &maps.qr : is_dv ? &maps.dout : &maps.q;
-        const CUtensorMap* bm = is_dv ? &maps.pp : &maps.ds;
-        const int row0 = 4 * grp;
-        // a row's slice is loaded just before the first ring entry that needs it, so the
-        // item's first tiles do not wait for the slots the previous item releases last
+        const int row0 = gs * grp;
+        // a slice is loaded just before the first ring entry that needs it, so the item's
+        // first tiles do not wait for the slots the previous item releases last
         int loaded = 0;
         Cur4 cu;
         cur4_init(cu, rec);
@@ -1557,27 +1565,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads4, 1)
           const int mask = cu.ra.x;
 #pragma unroll
           for (int g = 0; g < 4; ++g) {
-            if (!((mask >> g) & 1) || failed) continue;
-            if (!((loaded >> g) & 1)) {
-              if (!mbar_wait_sleep(smem_u32(&bars.a_empty[g]), (ua[g] & 1) ^ 1, a.err, &failed))
+            if (!((mask >> g) & 1)) continue;
+#pragma unroll
+            for (int hm = 0; hm < 2; ++hm) {
+              if ((hm == 1 && !mixed) || failed) continue;
+              // slot and operands of this entry: the member row's slice (merged: Q then dO)
+              const int slot = merged ? 2 * g + hm : g;
+              const bool second = is_dv || hm == 1;   // dO / P
+              if (!((loaded >> slot) & 1)) {
+                if (!mbar_wait_sleep(smem_u32(&bars.a_empty[slot]), (ua[slot] & 1) ^ 1, a.err, &failed))
+                  continue;
+                const CUtensorMap* am = rope ? &maps.qr : second ? &maps.dout : &maps.q;
+                const uint32_t fa = smem_u32(&bars.a_full[slot]);
+                if (cta == 0) mbar_arrive_expect_tx(fa, 2 * C::kSlot);
+                for (int c = 0; c < 2; ++c)
+                  tma_load_2d_pair(sA + slot * C::kSlot + c * C::kBox, am, mapa_shared(fa, 0),
+                                   col0 + 128 * (int)cta + 64 * c, (row0 + g) * a.N1);
+                ++ua[slot];
+                loaded |= 1 << slot;
+              }
+              const int s = nb % kStages4;
+              if (!mbar_wait_sleep(smem_u32(&bars.b_empty[s]), ((nb / kStages4) & 1) ^ 1, a.err, &failed))
                 continue;
-              const uint32_t fa = smem_u32(&bars.a_full[g]);
-              if (cta == 0) mbar_arrive_expect_tx(fa, 2 * C::kSlot);
-              for (int c = 0; c < 2; ++c)
-                tma_load_2d_pair(sA + g * C::kSlot + c * C::kBox, am, mapa_shared(fa, 0),
-                                 col0 + 128 * (int)cta + 64 * c, (row0 + g) * a.N1);
-              ++ua[g];
-              loaded |= 1 << g;
+              const uint32_t fb = smem_u32(&bars.b_full[s]);
+              if (cta == 0) mbar_arrive_expect_tx(fb, 2 * C::kTileB);
+              const int srow = (row0 + g) * a.kp + cur4_off(cu, g) + 64 * (int)cta;
+              const CUtensorMap* bm = second ? &maps.pp : &maps.ds;
+              for (int c = 0; c < 2; ++c)   // heads [64c, 64c+64) of this CTA's 64 key slots
+                tma_load_2d_pair(sB + s * C::kTileB + c * C::kHalf, bm, mapa_shared(fb, 0), 64 * c, srow);
+              ++nb;
             }
-            const int s = nb % kStages4;
-            if (!mbar_wait_sleep(smem_u32(&bars.b_empty[s]), ((nb / kStages4) & 1) ^ 1, a.err, &failed))
-              continue;
-            const uint32_t fb = smem_u32(&bars.b_full[s]);
-            if (cta == 0) mbar_arrive_expect_tx(fb, 2 * C::kTileB);
-            const int srow = (row0 + g) * a.kp + cur4_off(cu, g) + 64 * (int)cta;
-            for (int c = 0; c < 2; ++c)   // heads [64c, 64c+64) of this CTA's 64 key slots
-              tma_load_2d_pair(sB + s * C::kTileB + c * C::kHalf, bm, mapa_shared(fb, 0), 64 * c, srow);
-            ++nb;
           }
           cur4_next(cu, rec, h1.y);
         }
@@ -1591,28 +1608,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads4, 1)
       const uint32_t id = idesc_f16(256, kKeyTile3, bf16, true, false);
       int ua[4] = {0, 0, 0, 0}, nb = 0, nt = 0;
       for (int it = pair; it < nitems && !failed; it += npairs) {
-        const int grp = it / C::kParts;
+        const int grp = it / nparts, part = it % nparts;
         const int4* rec = a.recs + (size_t)kRec4 * grp;
         const int4 h0 = __ldg(rec), h1 = __ldg(rec + 1);
         if (h0.x == 0) continue;
+        const bool mixed = merged && part != C::kDParts;
         const int last[4] = {h0.y, h0.z, h0.w, h1.x};
-        int waited = 0;
+        int waited = 0, used = 0;
         Cur4 cu;
         cur4_init(cu, rec);
         for (int t = 0; t < h0.x; ++t) {
           const int tb = nt & 3;
           const int mask = cu.ra.x;
-          const int top = 31 - __clz(mask);
+          const int ne = __popc(mask) * (mixed ? 2 : 1);
           mbar_wait_spin(smem_u32(&bars.t_empty[tb]), ((nt >> 2) & 1) ^ 1, a.err, &failed, true);
           int e = 0;
 #pragma unroll 1
-          for (int g = 0; g < 4; ++g) {
-            if (!((mask >> g) & 1)) continue;
+          for (int x = 0; x < 8; ++x) {   // entry x: member row x >> 1, Q / dO part x & 1
+            const int g = x >> 1, hm = x & 1;
+            if (!((mask >> g) & 1) || (hm == 1 && !mixed)) continue;
+            const int slot = merged ? 2 * g + hm : g;
             const int s = nb % kStages4;
-            if (!((waited >> g) & 1)) {
-              const int u = g == 0 ? ua[0] : g == 1 ? ua[1] : g == 2 ? ua[2] : ua[3];
-              mbar_wait_spin(smem_u32(&bars.a_full[g]), u & 1, a.err, &failed, true);
-              waited |= 1 << g;
+            if (!((waited >> slot) & 1)) {
+              const int u = slot == 0 ? ua[0] : slot == 1 ? ua[1] : slot == 2 ? ua[2] : ua[3];
+              mbar_wait_spin(smem_u32(&bars.a_full[slot]), u & 1, a.err, &failed, true);
+              waited |= 1 << slot;
+              used |= 1 << slot;
             }
             mbar_wait_spin(smem_u32(&bars.b_full[s]), (nb / kStages4) & 1, a.err, &failed, true);
             if (__any_sync(0xffffffffu, failed)) {
@@ -1620,7 +1641,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads4, 1)
               break;
             }
             tc_fence_after();
-            const uint64_t da = smem_desc_sw128(sA + g * C::kSlot, C::kBox, 1024);
+            const uint64_t da = smem_desc_sw128(sA + slot * C::kSlot, C::kBox, 1024);
             const uint64_t db = smem_desc_sw128(sB + s * C::kTileB, 16, 1024);
             if (elect_one()) {
 #pragma unroll
@@ -1629,10 +1650,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads4, 1)
                             db + (uint64_t)(((k >> 2) * C::kHalf + (k & 3) * 32) >> 4), id,
                             (e | k) != 0);
               umma_commit_pair(smem_u32(&bars.b_empty[s]), 3);
-              if (g == top) umma_commit_pair(smem_u32(&bars.t_full[tb]), 3);
-              // the row's last tile of this item: its slot is free for the next item
+              if (e == ne - 1) umma_commit_pair(smem_u32(&bars.t_full[tb]), 3);
+              // the member row's last tile of this item: its slot is free for the next item
               if (t == (g == 0 ? last[0] : g == 1 ? last[1] : g == 2 ? last[2] : last[3]))
-                umma_commit_pair(smem_u32(&bars.a_empty[g]), 3);
+                umma_commit_pair(smem_u32(&bars.a_empty[slot]), 3);
             }
             __syncwarp();
             ++nb;
@@ -1644,8 +1665,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads4, 1)
         }
         if (failed) break;
 #pragma unroll
-        for (int g = 0; g < 4; ++g)
-          if (last[g] >= 0) ++ua[g];
+        for (int sl = 0; sl < 4; ++sl)
+          if ((used >> sl) & 1) ++ua[sl];
       }
       // the MMAs issued last complete before the exit (their TMEM is freed afterwards)
       if (nt > 0) {
@@ -1661,18 +1682,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads4, 1)
     const uint32_t lead_te = mapa_shared(smem_u32(&bars.t_empty[0]), 0);
     int nt = 0;
     for (int it = pair; it < nitems; it += npairs) {
-      const int grp = it / C::kParts, part = it % C::kParts;
+      const int grp = it / nparts, part = it % nparts;
       const int4* rec = a.recs + (size_t)kRec4 * grp;
       const int4 h0 = __ldg(rec), h1 = __ldg(rec + 1);
       if (h0.x == 0) continue;
-      const bool rope = part == 2 * C::kDParts;
-      const bool is_dv = !rope && part >= C::kDParts;
+      const bool rope = part == (merged ? C::kDParts : 2 * C::kDParts);
+      const bool is_dv = !merged && !rope && part >= C::kDParts;
       const int col0 = rope ? 0 : (part % C::kDParts) * C::kW;
-      float* acc = rope ? a.dkr_acc : is_dv ? a.dv_acc : a.dk_acc;
+      float* acc = rope ? a.dkr_acc : is_dv ? a.dv_acc : a.dk_acc;   // merged: dK + dV
       const int ld = rope ? 64 : D;
       const bool lanes_ok = !rope || (cta == 0 && q < 2);   // rope: 64 output columns
       float* gcol = acc + col0 + 128 * (int)cta + 32 * q + lane - (lane & 1);
-      const int row0 = 4 * grp;
+      const int row0 = gs * grp;
       // accumulator row of this lane's key of the cursor's tile (-1: none); a tile's keys
       // are listed in the key list of any of its member rows (the lowest)
       auto key_row = [&](const Cur4& c) {
@@ -1756,10 +1777,11 @@ inline int sm_count() {
 // key slots per row in the P / dS scratch: whole K1 pair tiles (256 keys)
 inline int64_t padded_keys(int64_t nent) { return (nent + 255) / 256 * 256; }
 inline int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
-// run table of the row pairs or records of the four-row groups (K3 grouped modes)
+// run table of the row pairs, or records of the groups of the CTA-pair K3 (four rows, or
+// two in the merged mode)
 inline int64_t runs_bytes(int64_t num_rows) {
-  const int64_t pairs = (num_rows + 1) / 2 * 3 * 16, quads = (num_rows + 3) / 4 * kRec4 * 16;
-  return align256(pairs > quads ? pairs : quads);
+  const int64_t pairs = (num_rows + 1) / 2 * 3 * 16, recs = (num_rows + 1) / 2 * kRec4 * 16;
+  return align256(pairs > recs ? pairs : recs);
 }
 // hash table of one group (log2 of its entries): at least twice the group's keys; groups of
 // longer key lists than kGroup4MaxKeys (four rows) or kGroupMaxKeys (pairs) per row are
@@ -1820,12 +1842,13 @@ int launch(const DsaSfaBwdParams* p, cudaStream_t stream) {
   ws += align256(p->num_rows * kHeadsPad * kp * 2);
   a.delta = reinterpret_cast<const float*>(ws);
   ws += align256(4 * p->num_rows * kHeadsPad);
-  // adjacent rows share their keys' reductions in K3 (5-output calls; the merged mode's two
-  // slots already hold Q and dO, and the teacher is indexed by the untouched key order):
-  // groups of four on CTA pairs where the slices fit (256-column parts), else pairs
-  const bool can_group = p->dv_acc != nullptr && p->teacher == nullptr && p->num_rows >= 2;
+  // adjacent rows share their keys' reductions in K3 (not with the teacher, which is indexed
+  // by the untouched key order): on CTA pairs where the slices fit (256-column parts; groups
+  // of four rows, of two in the merged mode), else in pairs on single CTAs (5-output calls)
+  const bool can_group = p->teacher == nullptr && p->num_rows >= 2;
   const bool grouped4 = can_group && nent <= kGroup4MaxKeys && (D == 256 || D == 512);
-  const bool grouped = can_group && !grouped4 && nent <= kGroupMaxKeys;
+  const bool grouped = can_group && p->dv_acc != nullptr && !grouped4 && nent <= kGroupMaxKeys;
+  const int gs4 = p->dv_acc != nullptr ? 4 : 2;   // rows per group of the CTA-pair K3
   a.runs = grouped ? reinterpret_cast<const int4*>(ws) : nullptr;
   a.recs = grouped4 ? reinterpret_cast<const int4*>(ws) : nullptr;
   a.kp = (int)kp;
@@ -1869,15 +1892,15 @@ int launch(const DsaSfaBwdParams* p, cudaStream_t stream) {
   launch_prep(a, const_cast<int32_t*>(a.ws_rows), const_cast<int32_t*>(a.ws_count), p->num_rows,
               stream);
   if (grouped4) {
-    const int lg = group_lg(4 * nent);
+    const int lg = group_lg(gs4 * nent);
     const int smem = group_smem_bytes(lg);
     if (smem > 48 * 1024 &&
         cudaFuncSetAttribute(sfa_bwd_group4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              smem) != cudaSuccess)
       return DSA_ERR_CUDA;
-    sfa_bwd_group4_kernel<<<dim3((unsigned)((p->num_rows + 3) / 4)), dim3(kGroup4Threads), smem,
-                            stream>>>(a, const_cast<int32_t*>(a.ws_rows), const_cast<int4*>(a.recs),
-                                      lg);
+    sfa_bwd_group4_kernel<<<dim3((unsigned)((p->num_rows + gs4 - 1) / gs4)), dim3(kGroup4Threads),
+                            smem, stream>>>(a, const_cast<int32_t*>(a.ws_rows),
+                                            const_cast<int4*>(a.recs), lg, gs4);
   }
   if (grouped) {
     const int lg = group_lg(2 * nent);
@@ -1918,7 +1941,8 @@ int launch(const DsaSfaBwdParams* p, cudaStream_t stream) {
       static_assert(Cfg4<D>::kOffBars + (int)sizeof(Bars4) <= 232448, "K3 pair smem");
       if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
         return DSA_ERR_CUDA;
-      const int64_t items = (p->num_rows + 3) / 4 * Cfg4<D>::kParts;
+      const int64_t items = (p->num_rows + gs4 - 1) / gs4 *
+                            (p->dv_acc ? Cfg4<D>::kParts : Cfg4<D>::kDParts + 1);
       const int64_t pairs_max = sm_count() / 2;
       const int npairs = (int)(items < pairs_max ? items : pairs_max);
       k<<<dim3(2 * (unsigned)npairs), dim3(kThreads4), smem, stream>>>(m4, a);

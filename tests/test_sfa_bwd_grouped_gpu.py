@@ -4,8 +4,8 @@ A 5-output backward call reorders the compacted key lists of adjacent rows into 
 per set of member rows (the rows that select the key), every member row listing a run's keys
 in the same order, and K3 sums the member rows' products for a key in TMEM before the one
 scatter into the key's fp32 accumulator.  Groups of four rows run K3 on CTA pairs (D = 256
-or 512, at most 2048 keys a row); otherwise pairs of rows on single CTAs (D = 128, or longer
-lists).  These cases drive both against the oracle: identical lists in different orders,
+or 512, at most 2048 keys a row; groups of two in the merged key == value mode); otherwise
+pairs of rows on single CTAs (D = 128, or longer lists).  These cases drive both against the oracle: identical lists in different orders,
 disjoint lists, partial overlap, row counts that leave a short last group, an inactive row,
 ragged -1 tails, a key listed twice (which keeps its group unshared) and lists too long for
 groups of four.  Some cases read the reordered lists and the run records back from the
@@ -64,7 +64,7 @@ CASES = [
 ]
 
 
-def _run(name, B, S1, S2, N1, D, cnt, act_q, workspace=None):
+def _run(name, B, S1, S2, N1, D, cnt, act_q, workspace=None, merged=False):
     from dsa_triton_ascend_b200 import check_device_errors
     from dsa_triton_ascend_b200.sparse_flash_attention_grad import _sfa_grad, INT64_MAX
     rng = np.random.default_rng(sum(map(ord, name)))
@@ -78,11 +78,15 @@ def _run(name, B, S1, S2, N1, D, cnt, act_q, workspace=None):
         cuda(c["q"]), cuda(c["k"]), cuda(c["k"]), icuda(c["si"]), cuda(c["dout"]), cuda(out),
         cuda(mx, "fp32"), cuda(sm, "fp32"), c["scale"], cuda(c["qr"]), cuda(c["kr"]),
         act_q, act_k, 1, "BSND", 0, INT64_MAX, INT64_MAX, False, defer_cast=False,
-        workspace=workspace)
+        workspace=workspace, merged=merged)
     check_device_errors()
     ref = sfa.sfa_bwd(c["q"], c["k"], c["qr"], c["kr"], c["si"], c["dout"], out, mx, sm,
                       c["scale"], act_q=act_q, act_k=act_k, sparse_mode=0, dtype="bf16",
-                      rounding="kernel")
+                      rounding="kernel", round_out=not merged)
+    if merged:   # dK + dV as one fp32 sum rounded once
+        dq, dk, dv, dqr, dkr = ref
+        ref = [sfa.round_to(dq, "bf16"), sfa.round_to(dk + dv, "bf16"), sfa.round_to(dqr, "bf16"),
+               sfa.round_to(dkr, "bf16")]
     return c, [host(t) for t in res], ref
 
 
@@ -91,6 +95,19 @@ def test_bwd_row_pairs_match_oracle(case):
     c, got, ref = _run(*case)
     for gi, ri, key in zip(got, ref, NAMES):
         assert_close(gi, ri, what=f"{case[0]} {key}")
+
+
+MERGED = ["overlap", "identical", "duplicate", "inactive", "six", "headline"]
+
+
+@pytest.mark.parametrize("name", MERGED)
+def test_bwd_row_groups_merged_match_oracle(name):
+    """key == value: the merged K3 on CTA pairs (groups of two rows) against the oracle's
+    dq, dk + dv (one fp32 sum rounded once), dq_rope, dk_rope."""
+    case = {c[0]: c for c in CASES}[name]
+    c, got, ref = _run(*case, merged=True)
+    for gi, ri, key in zip(got, ref, ("dq", "dk + dv", "dqr", "dkr")):
+        assert_close(gi, ri, what=f"merged {name} {key}")
 
 
 def _align256(x):
@@ -129,26 +146,29 @@ def _expected_runs(lists_in, G):
     return out, runs
 
 
-@pytest.mark.parametrize("name", ["overlap", "identical", "duplicate", "inactive", "odd", "six",
-                                  "long"])
-def test_row_group_runs_in_workspace(name):
+@pytest.mark.parametrize("name,merged", [(n, False) for n in ["overlap", "identical", "duplicate",
+                                                                "inactive", "odd", "six", "long"]]
+                         + [("overlap", True), ("inactive", True)])
+def test_row_group_runs_in_workspace(name, merged):
     """The reordered lists and the run records equal a plain restatement of the reordering
-    (four-row records for D = 256 / 512 with at most 2048 keys a row, pair runs otherwise);
-    groups with a key listed twice keep their lists, one run per row."""
+    (records of four rows for D = 256 / 512 with at most 2048 keys a row, of two rows in the
+    merged mode, pair runs otherwise); groups with a key listed twice keep their lists, one
+    run per row."""
     from dsa_triton_ascend_b200._lib import lib
     case = {c[0]: c for c in CASES}[name]
     _, B, S1, S2, N1, D, cnt, act_q = case
     rows = B * S1
     ws_bytes = lib().dsa_sfa_bwd_workspace_size(rows, cnt, 1)
     ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda")
-    c, got, ref = _run(*case, workspace=ws)
-    for gi, ri, key in zip(got, ref, NAMES):
-        assert_close(gi, ri, what=f"{name} {key}")
+    c, got, ref = _run(*case, workspace=ws, merged=merged)
+    for gi, ri in zip(got, ref):
+        assert_close(gi, ri, what=f"{name}")
     w = ws.cpu().numpy()
     lists = w[: 4 * rows * cnt].view(np.int32).reshape(rows, cnt)
-    G = 4 if D in (256, 512) and cnt <= 2048 else 2
+    pair_k3 = D in (256, 512) and cnt <= 2048   # records (CTA-pair K3) or pair runs
+    G = (2 if merged else 4) if pair_k3 else 2
     ngroups = (rows + G - 1) // G
-    region = _align256(max((rows + 1) // 2 * 48, (rows + 3) // 4 * 512))
+    region = _align256((rows + 1) // 2 * 512)
     tab = w[ws_bytes - region:].view(np.int32)
     si = c["si"].reshape(rows, cnt)
     active = np.ones(rows, bool)
@@ -176,14 +196,14 @@ def test_row_group_runs_in_workspace(name):
         for g in range(G):
             if r0 + g < rows:
                 assert lists[r0 + g, : len(outs[g])].tolist() == outs[g], (grp, g)
-        if G == 4:
+        if pair_k3:
             rec = tab[grp * 128: (grp + 1) * 128].reshape(32, 4)
             t, last = 0, [-1] * 4
             for i, (m, n, offs) in enumerate(runs):
                 ra, rb = rec[2 + 2 * i], rec[3 + 2 * i]
                 assert (ra[0], ra[1]) == (m, n), (grp, i)
                 got_offs = [ra[2], ra[3], rb[0], rb[1]]
-                for g in range(4):
+                for g in range(len(offs)):
                     if offs[g] is not None:
                         assert got_offs[g] == offs[g], (grp, i, g)
                 t += tiles(n)
