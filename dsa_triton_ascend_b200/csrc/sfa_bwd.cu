@@ -69,7 +69,9 @@ struct Args {
   const int32_t* ws_rows;
   const int32_t* ws_count;
   const int4* runs;  // NULL, or [num_rows / 2 rounded up][3] key runs of row pairs (K3 grouped)
-  const int4* recs;  // NULL, or [num_rows / 4 rounded up][kRec4] records of four-row groups
+  const int4* recs;  // NULL, or [groups][kRec4] records of the CTA-pair K3's row groups
+  int16_t* orig;     // NULL, or [num_rows][topk]: a reordered slot's position in the compacted
+                     // list (teacher with row groups: K1 writes the teacher there)
   void* ds;        // [num_rows][kp][128 heads] scratch (key-major), dtype of the inputs
   void* pp;        // [num_rows][kp][128 heads]
   const float* delta;   // [num_rows][N1] rowsum(dO * O), from sfa_bwd_delta_kernel
@@ -346,9 +348,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads1, 1)
         st_global_v8(ds_row + h0 / 8, pk_s);
         st_global_v8(p_row + h0 / 8, pk_p);
       }
-      // the indexer loss's teacher: (1/N1) sum_h P; the two head halves of a key add theirs
-      if (a.teacher != nullptr && valid && !wfail)
-        atomicAdd(a.teacher + (size_t)row * a.topk + e, psum * (1.f / (float)a.N1));
+      // the indexer loss's teacher: (1/N1) sum_h P; the two head halves of a key add theirs;
+      // at the key's position in the compacted list (row groups reorder the list)
+      if (a.teacher != nullptr && valid && !wfail) {
+        const int eo = a.orig != nullptr ? (int)a.orig[(size_t)row * a.topk + e] : e;
+        atomicAdd(a.teacher + (size_t)row * a.topk + eo, psum * (1.f / (float)a.N1));
+      }
       tc_fence_before();
       named_bar(1, 32 * kElemWarps1);
       if (warp == 2 && lane == 0) mbar_arrive_cluster(b ? lead_f1 : lead_f0);
@@ -1268,6 +1273,10 @@ __global__ void __launch_bounds__(kGroup4Threads) sfa_bwd_group4_kernel(const Ar
   const int b1 = n[0], b2 = b1 + n[1], b3 = b2 + n[2], N = b3 + n[3];
   int4* rec = recs + (size_t)kRec4 * blockIdx.x;
   auto unshared = [&]() {   // lists unchanged: one run per row with keys
+    if (a.orig != nullptr)
+      for (int g = 0; g < 4; ++g)
+        for (int j = threadIdx.x; j < n[g]; j += kGroup4Threads)
+          a.orig[(size_t)(r0 + g) * nent + j] = (int16_t)j;
     if (threadIdx.x == 0) {
       int t = 0, nr = 0, last[4];
 #pragma unroll
@@ -1389,6 +1398,7 @@ __global__ void __launch_bounds__(kGroup4Threads) sfa_bwd_group4_kernel(const Ar
       const int rank = (int)((e[f / 5] >> (12 * (f % 5))) & 0xfffu);
       e[f / 5] += 1ull << (12 * (f % 5));
       ws_rows[(size_t)(r0 + g) * nent + offs[g][m] + rank] = keys[h];
+      if (a.orig != nullptr) a.orig[(size_t)(r0 + g) * nent + offs[g][m] + rank] = (int16_t)j;
       if (m != (1 << g)) word[h] = w | ((uint32_t)rank << 4);
     }
   __syncthreads();
@@ -1401,6 +1411,7 @@ __global__ void __launch_bounds__(kGroup4Threads) sfa_bwd_group4_kernel(const Ar
       const int m = (int)(w & 15u);
       if (__ffs(m) - 1 == g) continue;
       ws_rows[(size_t)(r0 + g) * nent + offs[g][m] + (int)(w >> 4)] = keys[h];
+      if (a.orig != nullptr) a.orig[(size_t)(r0 + g) * nent + offs[g][m] + (int)(w >> 4)] = (int16_t)j;
     }
   if (threadIdx.x == 0) {
     int t = 0, nr = 0, last[4] = {-1, -1, -1, -1};
@@ -1842,15 +1853,18 @@ int launch(const DsaSfaBwdParams* p, cudaStream_t stream) {
   ws += align256(p->num_rows * kHeadsPad * kp * 2);
   a.delta = reinterpret_cast<const float*>(ws);
   ws += align256(4 * p->num_rows * kHeadsPad);
-  // adjacent rows share their keys' reductions in K3 (not with the teacher, which is indexed
-  // by the untouched key order): on CTA pairs where the slices fit (256-column parts; groups
-  // of four rows, of two in the merged mode), else in pairs on single CTAs (5-output calls)
-  const bool can_group = p->teacher == nullptr && p->num_rows >= 2;
-  const bool grouped4 = can_group && nent <= kGroup4MaxKeys && (D == 256 || D == 512);
-  const bool grouped = can_group && p->dv_acc != nullptr && !grouped4 && nent <= kGroupMaxKeys;
+  // adjacent rows share their keys' reductions in K3: on CTA pairs where the slices fit
+  // (256-column parts; groups of four rows, of two in the merged mode; with the teacher, K1
+  // writes it through the map of original positions), else in pairs on single CTAs
+  // (5-output calls without the teacher)
+  const bool grouped4 = p->num_rows >= 2 && nent <= kGroup4MaxKeys && (D == 256 || D == 512);
+  const bool grouped = !grouped4 && p->teacher == nullptr && p->num_rows >= 2 &&
+                       p->dv_acc != nullptr && nent <= kGroupMaxKeys;
   const int gs4 = p->dv_acc != nullptr ? 4 : 2;   // rows per group of the CTA-pair K3
   a.runs = grouped ? reinterpret_cast<const int4*>(ws) : nullptr;
   a.recs = grouped4 ? reinterpret_cast<const int4*>(ws) : nullptr;
+  ws += runs_bytes(p->num_rows);
+  a.orig = grouped4 && p->teacher != nullptr ? reinterpret_cast<int16_t*>(ws) : nullptr;
   a.kp = (int)kp;
 
   Maps1 m1;
@@ -1972,7 +1986,7 @@ extern "C" int64_t dsa_sfa_bwd_workspace_size(int64_t num_rows, int64_t topk, in
   const int64_t nent = topk * sparse_block_size;
   return align256(4 * num_rows * nent) + align256(4 * num_rows) +
          2 * align256(num_rows * kHeadsPad * padded_keys(nent) * 2) + align256(4 * num_rows * kHeadsPad) +
-         runs_bytes(num_rows);
+         runs_bytes(num_rows) + align256(2 * num_rows * nent);
 }
 
 extern "C" int dsa_sfa_bwd(const DsaSfaBwdParams* p, void* stream_) {

@@ -169,7 +169,8 @@ def test_row_group_runs_in_workspace(name, merged):
     G = (2 if merged else 4) if pair_k3 else 2
     ngroups = (rows + G - 1) // G
     region = _align256((rows + 1) // 2 * 512)
-    tab = w[ws_bytes - region:].view(np.int32)
+    orig_map = _align256(2 * rows * cnt)   # the teacher's position map follows the records
+    tab = w[ws_bytes - orig_map - region: ws_bytes - orig_map].view(np.int32)
     si = c["si"].reshape(rows, cnt)
     active = np.ones(rows, bool)
     if act_q is not None:
