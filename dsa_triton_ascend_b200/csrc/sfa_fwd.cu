@@ -24,7 +24,8 @@
 // the second half.  Valid indices are compacted by sfa_prep_kernel, so causal rows
 // with fewer than topK visible keys only pay for their valid keys.
 //
-// Warp roles (512 threads): warps 0 and 6 copy X -> H (warp 0 first loads Q); warp 1
+// Warp roles (512 threads): warps 0 and 6 copy X -> H (warp 0 first loads Q; at D = 512
+// they take alternate tiles, otherwise both copy every tile); warp 1
 // issues UMMA (pair leader) and owns TMEM; warps 2-5 run the online softmax, the lazy O
 // rescale and the epilogue; warps 7-15 gather the QK^T keys with TMA gather4, one 64-dim
 // chunk each.  Rows with few keys per SM (decode) are split into key ranges whose fp32
@@ -207,11 +208,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tma_load_2d_pair(sQ + lane * kHeads * 128, m, lead_q, x, qrow0);
       }
     }
-    const int ci = (warp == 0 ? 0 : 32) + lane;         // copy thread 0..63
+    // D = 512: warp 0 copies the even tiles and warp 6 the odd ones, so a tile's copy and
+    // its release arrive overlap the next tile's (2.7 % faster at config 4; at D = 128 the
+    // shorter copies gain nothing and both warps share every tile)
+    constexpr bool kAlt = D == 512;
+    constexpr int kCT = kAlt ? 32 : kCopyThreads;        // copy threads of one tile
+    const int ci = kAlt ? lane : (warp == 0 ? 0 : 32) + lane;
     const uint32_t peer = cta ^ 1u;
     const uint32_t lead_h0 = mapa_shared(smem_u32(&bars.h_full[0]), 0);
     const uint32_t lead_h1 = mapa_shared(smem_u32(&bars.h_full[1]), 0);
-    for (int t = 0; t < ntiles; ++t) {
+    for (int t = kAlt && warp == 6 ? 1 : 0; t < ntiles; t += kAlt ? 2 : 1) {
       const int b = t & 1;
       const uint32_t ph = (uint32_t)(t >> 1) & 1u;
       // QK^T(t) done (so X(t) landed in both CTAs) and PV(t-2) done (H slot b free in
@@ -226,22 +232,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t src_own = xs + C::slot_chunk(sl, cta) * kChunkBytesX;
           const uint32_t src_peer = xs + C::slot_chunk(sl, peer) * kChunkBytesX;
           const uint32_t dst = hs + sl * kChunkBytesH;
-          uint4 v[8];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            v[j] = *reinterpret_cast<const uint4*>(smem_raw + src_own + 16 * (ci + 64 * j));
-            v[4 + j] = *reinterpret_cast<const uint4*>(smem_raw + src_peer + 16 * (ci + 64 * j));
-          }
+          for (int hh = 0; hh < kChunkBytesH / 16 / kCT / 4; ++hh) {   // 4 own + 4 peer in flight
+            uint4 v[8];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            *reinterpret_cast<uint4*>(smem_raw + dst + 16 * (ci + 64 * j)) = v[j];
-            st_cluster_v4(mapa_shared(sbase + dst + 16 * (ci + 64 * j), peer), v[4 + j]);
+            for (int j = 0; j < 4; ++j) {
+              const int o = 16 * (ci + kCT * (4 * hh + j));
+              v[j] = *reinterpret_cast<const uint4*>(smem_raw + src_own + o);
+              v[4 + j] = *reinterpret_cast<const uint4*>(smem_raw + src_peer + o);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int o = 16 * (ci + kCT * (4 * hh + j));
+              *reinterpret_cast<uint4*>(smem_raw + dst + o) = v[j];
+              st_cluster_v4(mapa_shared(sbase + dst + o, peer), v[4 + j]);
+            }
           }
         }
       }
       fence_proxy_async_smem();
       asm volatile("fence.proxy.async.shared::cluster;" ::: "memory");
-      named_bar_sync(2, kCopyThreads);
+      if constexpr (kAlt)
+        __syncwarp();
+      else
+        named_bar_sync(2, kCopyThreads);
       if (ci == 0) {
         mbar_arrive(smem_u32(&bars.x_empty[b]));             // X(t) read: refill it
         mbar_arrive_cluster(b ? lead_h1 : lead_h0);           // H slot b of tile t written
