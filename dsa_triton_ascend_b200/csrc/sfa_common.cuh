@@ -9,6 +9,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "sm100.cuh"
+
 namespace dsa {
 namespace sfa {
 
@@ -85,6 +87,7 @@ __device__ __forceinline__ void named_bar_sync(int id, int n) {
 // with one coalesced load and no per-tile scanning.
 template <class A>
 __global__ void __launch_bounds__(128) sfa_prep_kernel(const A a, int32_t* ws_rows, int32_t* ws_count) {
+  griddep_launch_dependents();   // a forward launched as our dependent may start its set-up
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 4 + warp;
   if (row >= a.num_rows) return;
@@ -122,6 +125,7 @@ __global__ void __launch_bounds__(kPrepBlockThreads, 1) sfa_prep_block_kernel(co
   constexpr int kWarps = kPrepBlockThreads / 32;
   __shared__ int warp_sums[kWarps];
   __shared__ int s_batch;
+  griddep_launch_dependents();   // a forward launched as our dependent may start its set-up
   const int row = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) s_batch = 0;

@@ -159,19 +159,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int row = pair / a.splits;
   const int split = pair - row * a.splits;
   const RowInfo ri = row_info(a, row);
-  // Valid keys of this row, compacted by sfa_prep_kernel (identical in both CTAs).
-  // A CTA that finds an earlier error recorded skips its row, so one protocol failure
-  // does not turn into a slow cascade of timeouts over the whole grid.
-  const bool abort = a.err != nullptr && *reinterpret_cast<volatile int*>(a.err) != 0;
-  const int nvalid_row = (ri.active && !abort) ? __ldg(a.ws_count + row) : 0;
-  const int ntiles_row = (nvalid_row + kTile - 1) / kTile;
-  // this pair's tiles [t0, t1) of the row (all of them unless the row is split)
-  const int t0 = (int)((int64_t)split * ntiles_row / a.splits);
-  const int t1 = (int)((int64_t)(split + 1) * ntiles_row / a.splits);
-  const int ntiles = t1 - t0;
-  const int nvalid = ntiles > 0 ? min(nvalid_row - kTile * t0, kTile * ntiles) : 0;
-  const int32_t* rows = a.ws_rows + (size_t)row * a.topk * a.block + (size_t)kTile * t0;
 
+  // Set-up first: this kernel is launched as a programmatic dependent of the compaction
+  // pass, so barriers and TMEM are ready while that pass finishes.
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(&bars.q_full), 1);
     for (int b = 0; b < 2; ++b) {
@@ -194,6 +184,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bars.tmem_slot;
   bool failed = false;
+
+  // the compaction pass's results (and any error it recorded) are visible from here on
+  griddep_wait();
+  griddep_launch_dependents();   // the split-combine kernel may start staging
+  // Valid keys of this row, compacted by sfa_prep_kernel (identical in both CTAs).
+  // A CTA that finds an earlier error recorded skips its row, so one protocol failure
+  // does not turn into a slow cascade of timeouts over the whole grid.
+  const bool abort = a.err != nullptr && *reinterpret_cast<volatile int*>(a.err) != 0;
+  const int nvalid_row = (ri.active && !abort) ? __ldg(a.ws_count + row) : 0;
+  const int ntiles_row = (nvalid_row + kTile - 1) / kTile;
+  // this pair's tiles [t0, t1) of the row (all of them unless the row is split)
+  const int t0 = (int)((int64_t)split * ntiles_row / a.splits);
+  const int t1 = (int)((int64_t)(split + 1) * ntiles_row / a.splits);
+  const int ntiles = t1 - t0;
+  const int nvalid = ntiles > 0 ? min(nvalid_row - kTile * t0, kTile * ntiles) : 0;
+  const int32_t* rows = a.ws_rows + (size_t)row * a.topk * a.block + (size_t)kTile * t0;
 
   if (warp == 0 || warp == 6) {
     // ====== warp 0: Q of this CTA's 64 heads (once); warps 0 and 6: X -> H copies ======
@@ -508,6 +514,7 @@ __global__ void __launch_bounds__(256) sfa_fwd_combine_kernel(const float* __res
                                                               T* __restrict__ out, float* smax,
                                                               float* ssum, int num_rows, int n1,
                                                               int splits, float scale) {
+  griddep_wait();   // launched as a programmatic dependent of the forward: its partials
   const int gw = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
   if (gw >= num_rows * n1) return;
   const int row = gw / n1, h = gw - row * n1;
@@ -636,12 +643,34 @@ int launch(const DsaSfaFwdParams* p, cudaStream_t stream) {
   constexpr int kSmem = smem_bytes<D>();
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
     return DSA_ERR_CUDA;
-  kern<<<dim3(2 * (unsigned)(p->num_rows * splits)), dim3(kThreads), kSmem, stream>>>(maps, a);
+  // the forward and the split combine are programmatic dependents of the kernel before them
+  // (each waits for its predecessor's results before reading them), so their launch and
+  // set-up overlap the predecessor's tail; with few rows (decode) that latency is a
+  // sizeable part of the call
+  cudaLaunchAttribute pdl[1];
+  pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  pdl[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * (unsigned)(p->num_rows * splits));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = stream;
+  cfg.attrs = pdl;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, maps, a) != cudaSuccess) return DSA_ERR_CUDA;
   if (splits > 1) {
     const int64_t warps = p->num_rows * p->n1;
-    sfa_fwd_combine_kernel<D, T><<<dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, stream>>>(
-        a.part_o, a.part_s, static_cast<T*>(p->out), p->softmax_max, p->softmax_sum,
-        (int)p->num_rows, (int)p->n1, splits, p->scale);
+    cudaLaunchConfig_t cc = {};
+    cc.gridDim = dim3((unsigned)((warps + 7) / 8));
+    cc.blockDim = dim3(256);
+    cc.stream = stream;
+    cc.attrs = pdl;
+    cc.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cc, sfa_fwd_combine_kernel<D, T>, static_cast<const float*>(a.part_o),
+                           static_cast<const float4*>(a.part_s), static_cast<T*>(p->out),
+                           p->softmax_max, p->softmax_sum, (int)p->num_rows, (int)p->n1, splits,
+                           p->scale) != cudaSuccess)
+      return DSA_ERR_CUDA;
   }
   return cudaGetLastError() == cudaSuccess ? DSA_OK : DSA_ERR_CUDA;
 }

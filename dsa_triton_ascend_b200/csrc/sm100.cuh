@@ -81,6 +81,17 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
                : "memory");
 }
 
+// Programmatic dependent launch.  A kernel launched with the programmatic stream
+// serialization attribute may start while the previous kernel of the stream still runs:
+// griddep_wait returns once that kernel has completed and its memory operations are
+// visible, so everything before it may only read what earlier work produced.
+// griddep_launch_dependents lets the next such kernel start early.  Both do nothing in a
+// kernel launched without the attribute.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Arrive on a barrier in the cluster window without ordering the thread's earlier memory
 // operations: for a consumer whose signal only says that reads it has already completed are
 // done (tcgen05.ld followed by tcgen05.wait::ld), so that the arrive does not wait for the
