@@ -9,7 +9,7 @@
 // P and dS are rounded to the input dtype before the three products, exactly where the
 // reference kernel rounds them (`.to(k_full.dtype)`, :271-298).
 //
-// Four kernels (the per-query working set -- Q, dO, dQ, 128 heads x 576 dims -- does not
+// Four stages (the per-query working set -- Q, dO, dQ, 128 heads x 576 dims -- does not
 // fit one SM, and the dK/dV products need the heads as their reduction dimension):
 //   K1 probs : CTA pair per query row: S^T = K Q^T and dP^T = V dO^T on tcgen05 (2-SM,
 //              M = 256 keys, 128 per CTA, N = 128 heads; one gathered key chunk feeds
@@ -21,6 +21,11 @@
 //              (M = 128 output columns, N = 128 keys, K = 128 heads), double-buffered in
 //              TMEM and drained into fp32 accumulators with whole-row vector reductions
 //              (red.global.add.v2.f32), the scatter-add of the reference (:289-300).
+//              Adjacent rows share keys, so a pass after the compaction reorders their key
+//              lists into runs of shared keys and K3 reduces a shared key once: groups of
+//              four rows (two when key == value) on CTA pairs (sfa_bwd_group4_kernel,
+//              sfa_bwd_dkv4_kernel) where their slices fit, else row pairs on single CTAs
+//              (sfa_bwd_group_kernel, K3's grouped mode).
 //   K4 cast  : fp32 accumulators -> key dtype (separate entry point so a multi-GPU
 //              caller can all-reduce the fp32 accumulators first).
 
